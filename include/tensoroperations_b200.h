@@ -1,0 +1,164 @@
+/*
+ * tensoroperations_b200.h -- C ABI of the B200 (sm_100a) evaluator for the
+ * fused spectral-element stiffness path of TensorOperations.
+ *
+ * Everything here is plain C: pointers, sizes and integer status codes.  No
+ * call traps or aborts; every failure comes back as a non-zero `to_status`
+ * and `to_last_error()` holds a one-line reason for the calling thread.
+ * Device pointers are CUDA device addresses of the current device; `stream`
+ * arguments are `cudaStream_t` values passed as `void*` (NULL = legacy
+ * default stream).  Nothing in a launch entry point allocates device memory.
+ *
+ * The reference interface each entry point replaces is cited as
+ * path:line inside Rohit-Kakodkar/TensorOperations.
+ */
+#ifndef TENSOROPERATIONS_B200_H_
+#define TENSOROPERATIONS_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TO_ABI_VERSION 1
+
+typedef enum to_status {
+  TO_OK = 0,
+  TO_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad size, bad enum          */
+  TO_ERR_UNSUPPORTED = 2,      /* dtype / NGLL combination not built        */
+  TO_ERR_CUDA = 3,             /* a CUDA runtime call failed                */
+  TO_ERR_SCRATCH = 4,          /* shared-memory request above device limit  */
+  TO_ERR_ALIGNMENT = 5,        /* a pointer is not aligned as required      */
+  TO_ERR_TIMEOUT = 6,          /* a bounded device-side wait gave up        */
+  TO_ERR_COMM = 7,             /* a collective / peer exchange failed       */
+  TO_ERR_NO_DEVICE = 8,        /* no CUDA device visible                    */
+  TO_ERR_GRID = 9              /* a LabelWhole label longer than its tile   */
+} to_status;
+
+typedef enum to_dtype { TO_F32 = 0, TO_F64 = 1 } to_dtype;
+
+/* ---------------------------------------------------------------------- */
+/* Library                                                                 */
+/* ---------------------------------------------------------------------- */
+
+/* ABI version of the loaded library (compare with TO_ABI_VERSION). */
+int to_abi_version(void);
+
+/* Static text for a status code. */
+const char* to_status_string(int status);
+
+/* Detail of the last failure on the calling thread ("" if none). */
+const char* to_last_error(void);
+
+/* Number of SMs of the current device, or a negative to_status. */
+int to_device_sm_count(void);
+
+/* ---------------------------------------------------------------------- */
+/* Mesh and operators (host utilities)                                     */
+/* ---------------------------------------------------------------------- */
+
+/*
+ * Structured shared-node numbering of an nex x ney x nez hexahedral mesh with
+ * NGLL points per direction.  Element e = (ez*ney + ey)*nex + ex; node
+ *   ibool[e][k][j][i] = ((ez*(N-1)+k)*ny + ey*(N-1)+j)*nx + ex*(N-1)+i,
+ * nx = nex*(N-1)+1 (same for y, z).  `ibool` is a HOST buffer of
+ * nex*ney*nez*N^3 int32.  The reference has no global numbering: its SEM
+ * programs are element-local (benchmarks/sem_stiffness/bench_sem_stiffness.cpp:8-11,
+ * benchmarks/sem_stiffness_3d/bench_sem3d_levelgraph.cpp:104-105); this
+ * defines the one the assembled mode uses.
+ */
+int to_mesh_structured_ibool(int32_t nex, int32_t ney, int32_t nez,
+                             int32_t ngll, int32_t* ibool);
+
+/*
+ * GLL nodes, weights, derivative matrix H(i,p) = l_p'(x_i) and the weighted
+ * transpose Hw(q,i) = H(q,i) * w(q) (hprimewgll), all HOST double arrays
+ * (nodes/weights [N], hprime/hprimewgll [N][N]).  Any pointer may be NULL.
+ * 2 <= ngll <= 16.
+ */
+int to_gll_operators(int32_t ngll, double* nodes, double* weights,
+                     double* hprime, double* hprimewgll);
+
+/*
+ * Seeded synthetic fill of a HOST buffer: dst[n] of `dtype`.  Element m gets
+ * a value derived from splitmix64(seed, m) only, so any slice can be
+ * generated independently and identically anywhere.
+ *   dist 0: Uniform[a, b)      dist 1: Normal(mean a, stddev b)
+ */
+int to_synth_fill(void* dst, int32_t dtype, int64_t n, uint64_t seed,
+                  int32_t dist, double a, double b);
+
+/* ---------------------------------------------------------------------- */
+/* SEM 3D isotropic-elastic stiffness operator                             */
+/* ---------------------------------------------------------------------- */
+/*
+ * One application f = K u of the pipeline the reference builds as a
+ * LevelGraph in benchmarks/sem_stiffness_3d/bench_sem3d_levelgraph.cpp:247-351
+ * (stage H,Hw | stage u | 9 gradient contractions | 1 nine-output combine
+ * Integrand9 | 9 divergence contractions | 3 WeightedSum combines) and
+ * launches through LevelOutputs::execute (include/TensorOperations/LevelGraph.hpp:664-667):
+ *
+ *   grad    dxi_c = sum_p H(i,p) u_c(k,j,p)   (and eta over j, gamma over k)
+ *   stress  ds = chain_rule(dxi,deta,dgam,J); sigma = mu(ds+ds^T)+lambda tr(ds) I,
+ *           lambda = l2m - 2 mu
+ *   flux    F^r_c = jac * sum_d sigma[c][d] J[r][d]
+ *   div     t^xi_c = sum_q Hw(q,i) F^xi_c(k,j,q)  (eta over j, gamma over k)
+ *   force   f_c = w_j w_k t^xi_c + w_i w_k t^eta_c + w_i w_j t^gam_c
+ *
+ * Per-point arrays are [E][k][j][i] (i fastest), one array per quantity, as the
+ * reference's Kokkos::View<T*[N][N][N], LayoutRight> fields.
+ * Element-local mode (ibool == NULL): u_c and f_c are [E][N][N][N] and f is
+ * overwritten.  Assembled mode: u_c and f_c are [nglob] and f_c[ibool[...]]
+ * receives the scatter-add of every element's contribution; with
+ * accumulate == 0 f is zeroed first (stream-ordered memset), else added to.
+ */
+typedef struct to_sem3d_desc {
+  int32_t dtype;            /* TO_F32 or TO_F64                              */
+  int32_t ngll;             /* N: 5 (f32, f64) or 8 (f32, f64)               */
+  int64_t nelem;            /* E                                              */
+  int64_t nglob;            /* assembled: number of global nodes; else 0     */
+  int32_t assembled;        /* 1 = through ibool, 0 = element-local          */
+  int32_t reserved0;
+  const double* hprime;     /* HOST [N][N]  H(i,p)   (reference d.H)          */
+  const double* hprimewgll; /* HOST [N][N]  Hw(q,i)  (reference d.Hw)         */
+  const double* wgll;       /* HOST [N]     w        (reference d.w)           */
+} to_sem3d_desc;
+
+typedef struct to_sem3d_fields {
+  const void* u[3];         /* displacement components                       */
+  void* f[3];               /* force components (output)                     */
+  const int32_t* ibool;     /* [E][N][N][N] global node ids (assembled mode) */
+  /* inverse Jacobian J[r][d] = d(xi_r)/d(x_d), then jac, l2m, mu            */
+  const void* xix;  const void* xiy;  const void* xiz;
+  const void* etax; const void* etay; const void* etaz;
+  const void* gamx; const void* gamy; const void* gamz;
+  const void* jac;  const void* l2m;  const void* mu;
+} to_sem3d_fields;
+
+typedef struct to_sem3d_plan to_sem3d_plan;
+
+/* Validate a description and capture the operators.  Host only. */
+int to_sem3d_plan_create(const to_sem3d_desc* desc, to_sem3d_plan** plan);
+int to_sem3d_plan_destroy(to_sem3d_plan* plan);
+
+/* Launch one application on `stream` (asynchronous).  Device pointers in
+ * `fields` must be 4-byte (f32) or 8-byte (f64) aligned; all per-point arrays
+ * hold E*N^3 values. */
+int to_sem3d_apply(const to_sem3d_plan* plan, const to_sem3d_fields* fields,
+                   int32_t accumulate, void* stream);
+
+/* Algorithmic HBM bytes of one application of `plan` (the roofline numerator:
+ * every per-point array read once, ibool read once, u read and f written once
+ * per global node in assembled mode, per point in element-local mode). */
+double to_sem3d_algorithmic_bytes(const to_sem3d_plan* plan);
+
+/* Useful floating-point operations of one application (36N+159 per point). */
+double to_sem3d_flops(const to_sem3d_plan* plan);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* TENSOROPERATIONS_B200_H_ */

@@ -1,0 +1,201 @@
+"""ctypes binding of include/tensoroperations_b200.h.
+
+This is the Python-side counterpart a maintainer binds against the C ABI; the
+C++ frontend under include/ and tensoroperations_b200/include/ is the other.
+Every wrapper raises `ToError` with the library's own one-line reason when a
+call returns a non-zero status.  The library is loaded from the package
+directory (in-tree build); a missing library is an ImportError, never a silent
+fallback.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import re
+from pathlib import Path
+
+import numpy as np
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libtensoroperations_b200.so"
+HEADER = PKG.parent / "include" / "tensoroperations_b200.h"
+
+TO_OK = 0
+TO_ERR_INVALID_ARGUMENT = 1
+TO_ERR_UNSUPPORTED = 2
+TO_ERR_CUDA = 3
+TO_ERR_SCRATCH = 4
+TO_ERR_ALIGNMENT = 5
+TO_ERR_TIMEOUT = 6
+TO_ERR_COMM = 7
+TO_ERR_NO_DEVICE = 8
+TO_ERR_GRID = 9
+
+TO_F32 = 0
+TO_F64 = 1
+
+
+class ToError(RuntimeError):
+    def __init__(self, status: int, where: str, detail: str):
+        super().__init__(f"{where}: {status_name(status)}: {detail}")
+        self.status = status
+
+
+def _load():
+    if not LIB_PATH.exists():
+        raise ImportError(
+            f"{LIB_PATH} is missing: build it with `python -c 'import __graft_entry__ as g; g.build()'`")
+    return C.CDLL(str(LIB_PATH))
+
+
+lib = _load()
+
+
+class Sem3dDesc(C.Structure):
+    _fields_ = [("dtype", C.c_int32), ("ngll", C.c_int32), ("nelem", C.c_int64),
+                ("nglob", C.c_int64), ("assembled", C.c_int32), ("reserved0", C.c_int32),
+                ("hprime", C.POINTER(C.c_double)), ("hprimewgll", C.POINTER(C.c_double)),
+                ("wgll", C.POINTER(C.c_double))]
+
+
+POINT_ARRAYS = ("xix", "xiy", "xiz", "etax", "etay", "etaz", "gamx", "gamy", "gamz",
+                "jac", "l2m", "mu")
+
+
+class Sem3dFields(C.Structure):
+    _fields_ = [("u", C.c_void_p * 3), ("f", C.c_void_p * 3), ("ibool", C.c_void_p)] + \
+        [(n, C.c_void_p) for n in POINT_ARRAYS]
+
+
+def _sig(name, restype, argtypes):
+    fn = getattr(lib, name)
+    fn.restype = restype
+    fn.argtypes = argtypes
+    return fn
+
+
+_sig("to_abi_version", C.c_int, [])
+_sig("to_status_string", C.c_char_p, [C.c_int])
+_sig("to_last_error", C.c_char_p, [])
+_sig("to_device_sm_count", C.c_int, [])
+_sig("to_mesh_structured_ibool", C.c_int, [C.c_int32] * 4 + [C.c_void_p])
+_sig("to_gll_operators", C.c_int, [C.c_int32] + [C.c_void_p] * 4)
+_sig("to_synth_fill", C.c_int, [C.c_void_p, C.c_int32, C.c_int64, C.c_uint64, C.c_int32,
+                                C.c_double, C.c_double])
+_sig("to_sem3d_plan_create", C.c_int, [C.POINTER(Sem3dDesc), C.POINTER(C.c_void_p)])
+_sig("to_sem3d_plan_destroy", C.c_int, [C.c_void_p])
+_sig("to_sem3d_apply", C.c_int, [C.c_void_p, C.POINTER(Sem3dFields), C.c_int32, C.c_void_p])
+_sig("to_sem3d_algorithmic_bytes", C.c_double, [C.c_void_p])
+_sig("to_sem3d_flops", C.c_double, [C.c_void_p])
+
+
+def status_name(status: int) -> str:
+    return lib.to_status_string(status).decode()
+
+
+def check(status: int, where: str):
+    if status != TO_OK:
+        raise ToError(status, where, lib.to_last_error().decode())
+
+
+def header_functions(header: Path = HEADER):
+    """Names of every function the public header declares."""
+    text = re.sub(r"/\*.*?\*/", "", header.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(to_[a-z0-9_]+)\s*\(", text)))
+
+
+def _ptr(a) -> int:
+    if a is None:
+        return 0
+    if isinstance(a, int):
+        return a
+    if isinstance(a, np.ndarray):
+        return a.ctypes.data
+    return a.data_ptr()  # torch.Tensor
+
+
+# ---- host utilities ---------------------------------------------------------
+
+def gll_operators(ngll: int):
+    """(nodes, weights, hprime H(i,p), hprimewgll Hw(q,i)) as float64 numpy arrays."""
+    x = np.zeros(ngll)
+    w = np.zeros(ngll)
+    H = np.zeros((ngll, ngll))
+    Hw = np.zeros((ngll, ngll))
+    check(lib.to_gll_operators(ngll, _ptr(x), _ptr(w), _ptr(H), _ptr(Hw)), "to_gll_operators")
+    return x, w, H, Hw
+
+
+def structured_ibool(nex: int, ney: int, nez: int, ngll: int) -> np.ndarray:
+    out = np.empty((nex * ney * nez, ngll, ngll, ngll), dtype=np.int32)
+    check(lib.to_mesh_structured_ibool(nex, ney, nez, ngll, _ptr(out)), "to_mesh_structured_ibool")
+    return out
+
+
+def synth_fill(n: int, dtype, seed: int, dist: str, a: float, b: float) -> np.ndarray:
+    """Seeded fill: dist 'uniform' -> U[a,b), 'normal' -> N(a, b^2)."""
+    dt = np.dtype(dtype)
+    code = TO_F32 if dt == np.float32 else TO_F64
+    out = np.empty(n, dtype=dt)
+    check(lib.to_synth_fill(_ptr(out), code, n, seed, {"uniform": 0, "normal": 1}[dist], a, b),
+          "to_synth_fill")
+    return out
+
+
+def sm_count() -> int:
+    n = lib.to_device_sm_count()
+    if n < 0:
+        check(-n, "to_device_sm_count")
+    return n
+
+
+# ---- SEM 3D elastic operator ------------------------------------------------
+
+class Sem3dPlan:
+    """A validated operator description (host) -> launches on any stream."""
+
+    def __init__(self, dtype, ngll: int, nelem: int, H, Hw, w, nglob: int = 0,
+                 assembled: bool = False):
+        self.dtype = np.dtype(dtype)
+        self._H = np.ascontiguousarray(H, dtype=np.float64)
+        self._Hw = np.ascontiguousarray(Hw, dtype=np.float64)
+        self._w = np.ascontiguousarray(w, dtype=np.float64)
+        d = Sem3dDesc()
+        d.dtype = TO_F32 if self.dtype == np.float32 else TO_F64
+        d.ngll = ngll
+        d.nelem = nelem
+        d.nglob = nglob
+        d.assembled = 1 if assembled else 0
+        d.hprime = self._H.ctypes.data_as(C.POINTER(C.c_double))
+        d.hprimewgll = self._Hw.ctypes.data_as(C.POINTER(C.c_double))
+        d.wgll = self._w.ctypes.data_as(C.POINTER(C.c_double))
+        self.desc = d
+        self._h = C.c_void_p()
+        check(lib.to_sem3d_plan_create(C.byref(d), C.byref(self._h)), "to_sem3d_plan_create")
+        self.ngll, self.nelem, self.nglob, self.assembled = ngll, nelem, nglob, assembled
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value:
+            lib.to_sem3d_plan_destroy(h)
+            self._h = None
+
+    @staticmethod
+    def fields(u, f, arrays, ibool=None) -> Sem3dFields:
+        fl = Sem3dFields()
+        for c in range(3):
+            fl.u[c] = _ptr(u[c])
+            fl.f[c] = _ptr(f[c])
+        fl.ibool = _ptr(ibool)
+        for n in POINT_ARRAYS:
+            setattr(fl, n, _ptr(arrays[n]))
+        return fl
+
+    def apply(self, fields: Sem3dFields, accumulate: bool = False, stream: int = 0):
+        check(lib.to_sem3d_apply(self._h, C.byref(fields), 1 if accumulate else 0, stream),
+              "to_sem3d_apply")
+
+    def algorithmic_bytes(self) -> float:
+        return lib.to_sem3d_algorithmic_bytes(self._h)
+
+    def flops(self) -> float:
+        return lib.to_sem3d_flops(self._h)

@@ -1,0 +1,206 @@
+// sem3d_elastic.cu -- C-ABI plan / launch for the fused SEM 3D elastic operator.
+#include <cstring>
+#include <mutex>
+#include <new>
+
+#include "common.hpp"
+#include "sem3d_elastic.cuh"
+
+struct to_sem3d_plan {
+  to_sem3d_desc desc;
+  double H[16 * 16];
+  double Hw[16 * 16];
+  double w[16];
+};
+
+namespace to_b200 {
+namespace {
+
+// Elements per CTA batch for each instantiation: EB * N^2 threads per CTA.
+template <typename T, int N>
+struct Sem3dConfig;
+template <>
+struct Sem3dConfig<float, 5> {
+  static constexpr int EB = 32;  // 800 threads, 25 warps
+};
+template <>
+struct Sem3dConfig<double, 5> {
+  static constexpr int EB = 16;  // 400 threads
+};
+
+template <typename T, int N>
+size_t sem3d_smem_bytes() {
+  constexpr int EB = Sem3dConfig<T, N>::EB;
+  return sizeof(T) * (9ull * N * EB * N * N + 2ull * N * N) + 4ull * N * EB * N * N;
+}
+
+template <typename T, int N, bool ASM>
+int launch_sem3d(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t stream) {
+  constexpr int EB = Sem3dConfig<T, N>::EB;
+  constexpr int NT = EB * N * N;
+  const size_t smem = sem3d_smem_bytes<T, N>();
+  auto kernel = sem3d_elastic_kernel<T, N, EB, ASM>;
+
+  int dev = 0;
+  const int sms = device_sm_count(&dev);
+  if (sms <= 0) return -sms;
+
+  // Opt in to the large shared-memory carve-out once per device.
+  static std::mutex mu;
+  static unsigned long long configured = 0;  // bit per device id (< 64)
+  static int blocks_per_sm[64] = {0};
+  if (dev >= 64) return set_error(TO_ERR_UNSUPPORTED, "device id %d >= 64", dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!(configured & (1ull << dev))) {
+      TO_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem)));
+      int nb = 0;
+      TO_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kernel, NT, smem));
+      if (nb <= 0)
+        return set_error(TO_ERR_SCRATCH,
+                         "sem3d kernel (%d threads, %zu B shared) cannot be resident", NT,
+                         smem);
+      blocks_per_sm[dev] = nb;
+      configured |= (1ull << dev);
+    }
+  }
+
+  Sem3dArgs<T, N> a;
+  std::memset(&a, 0, sizeof(a));
+  for (int c = 0; c < 3; ++c) {
+    a.u[c] = static_cast<const T*>(fl->u[c]);
+    a.f[c] = static_cast<T*>(fl->f[c]);
+  }
+  a.ibool = fl->ibool;
+  const void* m[kNumPointArrays] = {fl->xix,  fl->xiy,  fl->xiz,  fl->etax,
+                                    fl->etay, fl->etaz, fl->gamx, fl->gamy,
+                                    fl->gamz, fl->jac,  fl->l2m,  fl->mu};
+  bool pf = aligned(fl->ibool, 16) || !ASM;
+  for (int q = 0; q < kNumPointArrays; ++q) {
+    a.m[q] = static_cast<const T*>(m[q]);
+    pf = pf && aligned(m[q], 16);
+  }
+  if (!ASM)
+    for (int c = 0; c < 3; ++c) pf = pf && aligned(fl->u[c], 16);
+  a.prefetch = pf ? 1 : 0;
+  a.nelem = plan->desc.nelem;
+  for (int i = 0; i < N; ++i) {
+    a.ops.w[i] = static_cast<T>(plan->w[i]);
+    for (int p = 0; p < N; ++p) {
+      a.ops.H[i][p] = static_cast<T>(plan->H[i * N + p]);
+      a.ops.Hw[i][p] = static_cast<T>(plan->Hw[i * N + p]);
+    }
+  }
+
+  const long long nbatch = (plan->desc.nelem + EB - 1) / EB;
+  const long long cap = static_cast<long long>(sms) * blocks_per_sm[dev];
+  const int grid = static_cast<int>(nbatch < cap ? nbatch : cap);
+  if (grid <= 0) return ok();
+  kernel<<<grid, NT, smem, stream>>>(a);
+  TO_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
+template <typename T, int N>
+int apply_typed(const to_sem3d_plan* plan, const to_sem3d_fields* fl, int accumulate,
+                cudaStream_t stream) {
+  const size_t al = sizeof(T);
+  const void* ptrs[] = {fl->u[0], fl->u[1], fl->u[2], fl->f[0], fl->f[1], fl->f[2],
+                        fl->xix,  fl->xiy,  fl->xiz,  fl->etax, fl->etay, fl->etaz,
+                        fl->gamx, fl->gamy, fl->gamz, fl->jac,  fl->l2m,  fl->mu};
+  for (const void* p : ptrs) {
+    if (!p) return set_error(TO_ERR_INVALID_ARGUMENT, "to_sem3d_apply: null field pointer");
+    if (!aligned(p, al))
+      return set_error(TO_ERR_ALIGNMENT, "to_sem3d_apply: field pointer %p not %zu-byte aligned",
+                       p, al);
+  }
+  if (plan->desc.assembled) {
+    if (!fl->ibool)
+      return set_error(TO_ERR_INVALID_ARGUMENT, "to_sem3d_apply: assembled mode needs ibool");
+    if (!aligned(fl->ibool, 4))
+      return set_error(TO_ERR_ALIGNMENT, "to_sem3d_apply: ibool not 4-byte aligned");
+    if (!accumulate)
+      for (int c = 0; c < 3; ++c)
+        TO_CUDA_TRY(cudaMemsetAsync(fl->f[c], 0, sizeof(T) * plan->desc.nglob, stream));
+    return launch_sem3d<T, N, true>(plan, fl, stream);
+  }
+  return launch_sem3d<T, N, false>(plan, fl, stream);
+}
+
+}  // namespace
+}  // namespace to_b200
+
+using namespace to_b200;
+
+extern "C" {
+
+int to_sem3d_plan_create(const to_sem3d_desc* desc, to_sem3d_plan** plan) {
+  if (!desc || !plan) return set_error(TO_ERR_INVALID_ARGUMENT, "to_sem3d_plan_create: null");
+  *plan = nullptr;
+  if (desc->dtype != TO_F32 && desc->dtype != TO_F64)
+    return set_error(TO_ERR_INVALID_ARGUMENT, "to_sem3d_plan_create: dtype %d", desc->dtype);
+  if (desc->ngll < 2 || desc->ngll > 16)
+    return set_error(TO_ERR_INVALID_ARGUMENT, "to_sem3d_plan_create: ngll %d", desc->ngll);
+  const bool built = (desc->ngll == 5);
+  if (!built)
+    return set_error(TO_ERR_UNSUPPORTED, "to_sem3d_plan_create: ngll %d (%s) not built",
+                     desc->ngll, desc->dtype == TO_F32 ? "f32" : "f64");
+  if (desc->nelem < 0)
+    return set_error(TO_ERR_INVALID_ARGUMENT, "to_sem3d_plan_create: nelem %lld < 0",
+                     static_cast<long long>(desc->nelem));
+  if (desc->assembled && (desc->nglob <= 0 || desc->nglob > INT32_MAX))
+    return set_error(TO_ERR_INVALID_ARGUMENT,
+                     "to_sem3d_plan_create: assembled mode needs 0 < nglob <= INT32_MAX");
+  if (!desc->hprime || !desc->hprimewgll || !desc->wgll)
+    return set_error(TO_ERR_INVALID_ARGUMENT, "to_sem3d_plan_create: null operator array");
+  to_sem3d_plan* p = new (std::nothrow) to_sem3d_plan;
+  if (!p) return set_error(TO_ERR_INVALID_ARGUMENT, "to_sem3d_plan_create: out of host memory");
+  std::memset(p, 0, sizeof(*p));
+  p->desc = *desc;
+  p->desc.hprime = p->H;
+  p->desc.hprimewgll = p->Hw;
+  p->desc.wgll = p->w;
+  const int N = desc->ngll;
+  std::memcpy(p->H, desc->hprime, sizeof(double) * N * N);
+  std::memcpy(p->Hw, desc->hprimewgll, sizeof(double) * N * N);
+  std::memcpy(p->w, desc->wgll, sizeof(double) * N);
+  *plan = p;
+  return ok();
+}
+
+int to_sem3d_plan_destroy(to_sem3d_plan* plan) {
+  delete plan;
+  return ok();
+}
+
+int to_sem3d_apply(const to_sem3d_plan* plan, const to_sem3d_fields* fields,
+                   int32_t accumulate, void* stream) {
+  if (!plan || !fields) return set_error(TO_ERR_INVALID_ARGUMENT, "to_sem3d_apply: null");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const to_sem3d_desc& d = plan->desc;
+  if (d.nelem == 0) return ok();
+  if (d.ngll == 5 && d.dtype == TO_F32) return apply_typed<float, 5>(plan, fields, accumulate, s);
+  if (d.ngll == 5 && d.dtype == TO_F64) return apply_typed<double, 5>(plan, fields, accumulate, s);
+  return set_error(TO_ERR_UNSUPPORTED, "to_sem3d_apply: ngll %d dtype %d not built", d.ngll,
+                   d.dtype);
+}
+
+double to_sem3d_algorithmic_bytes(const to_sem3d_plan* plan) {
+  if (!plan) return 0.0;
+  const to_sem3d_desc& d = plan->desc;
+  const double s = d.dtype == TO_F64 ? 8.0 : 4.0;
+  const double P = static_cast<double>(d.ngll) * d.ngll * d.ngll;
+  const double E = static_cast<double>(d.nelem);
+  if (d.assembled) return E * P * (12.0 * s + 4.0) + static_cast<double>(d.nglob) * 3.0 * s * 2.0;
+  return E * P * (12.0 * s + 3.0 * s * 2.0);
+}
+
+double to_sem3d_flops(const to_sem3d_plan* plan) {
+  if (!plan) return 0.0;
+  const to_sem3d_desc& d = plan->desc;
+  const double P = static_cast<double>(d.ngll) * d.ngll * d.ngll;
+  return static_cast<double>(d.nelem) * P * (36.0 * d.ngll + 159.0);
+}
+
+}  // extern "C"

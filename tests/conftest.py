@@ -1,0 +1,40 @@
+"""pytest configuration: the `gpu` marker, repo on sys.path, in-tree builds.
+
+CPU runs (`-m "not gpu"`) need the product library and the oracle built; both
+builds are incremental and take seconds, so they run here if stale.  GPU tests
+skip cleanly when no device is visible.
+"""
+import os
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200)")
+    from tensoroperations_b200 import _build
+    _build.build_library()
+    from oracle import build as oracle_build
+    oracle_build.build()
+
+
+def _cuda_available():
+    try:
+        import torch
+        return torch.cuda.is_available()
+    except Exception:
+        return False
+
+
+def pytest_collection_modifyitems(config, items):
+    if _cuda_available():
+        return
+    skip = pytest.mark.skip(reason="no CUDA device")
+    for item in items:
+        if "gpu" in item.keywords:
+            item.add_marker(skip)
