@@ -45,6 +45,9 @@ METRIC = ("SEM stiffness Melem/s and HBM GB/s (% of ~8 TB/s) at 1/2/4/8 B200 vs 
 MESH_PER_GPU = (64, 64, 64)
 NGLL = 5
 FALLBACK_HBM_GBS = 6650.0
+KERNEL_NAMES = {"0": "sem3d_elastic_tma_kernel<float,5,8,2,true>",
+                "1": "sem3d_elastic_tma_kernel<float,5,16,1,true>",
+                "2": "sem3d_elastic_kernel<float,5,32,true>"}
 
 
 def measured_peak_hbm():
@@ -232,10 +235,14 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--variant", type=int, default=None,
+                    help="f32 kernel variant (TO_SEM3D_VARIANT): 0 TMA 8x2, 1 TMA 16x1, 2 streaming")
     ap.add_argument("--mesh", type=int, nargs=3, default=[64, 64, 64],
                     metavar=("NEX", "NEY", "NEZ"), help="hexes per GPU (profiling runs)")
     args = ap.parse_args()
     MESH_PER_GPU = tuple(args.mesh)
+    if args.variant is not None:
+        os.environ["TO_SEM3D_VARIANT"] = str(args.variant)
     if args.impl == "reference":
         return run_reference(args)
 
@@ -352,7 +359,7 @@ def main():
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": None, "peak_source": peak_src,
                          "algorithmic_bytes_per_launch": alg, "kernel_ms": kern_ms,
-                         "kernel": "sem3d_elastic_kernel<float,5,32,true>"},
+                         "kernel": KERNEL_NAMES.get(os.environ.get("TO_SEM3D_VARIANT", "0"))},
             "cpu_baseline": cpu,
             "e2e": None if not e2e_steps else
                    {"value": prob.nelem * world / (e2e_ms * 1e-3) / 1e6, "unit": "Melem/s",

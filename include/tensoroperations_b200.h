@@ -55,6 +55,11 @@ const char* to_last_error(void);
 /* Number of SMs of the current device, or a negative to_status. */
 int to_device_sm_count(void);
 
+/* Device status word of the current device: TO_OK, or the status a kernel
+ * recorded instead of trapping (TO_ERR_TIMEOUT when a bounded wait gave up).
+ * Synchronous (reads device memory).  reset != 0 clears it. */
+int to_device_status(int32_t reset);
+
 /* ---------------------------------------------------------------------- */
 /* Mesh and operators (host utilities)                                     */
 /* ---------------------------------------------------------------------- */

@@ -77,6 +77,7 @@ _sig("to_abi_version", C.c_int, [])
 _sig("to_status_string", C.c_char_p, [C.c_int])
 _sig("to_last_error", C.c_char_p, [])
 _sig("to_device_sm_count", C.c_int, [])
+_sig("to_device_status", C.c_int, [C.c_int32])
 _sig("to_mesh_structured_ibool", C.c_int, [C.c_int32] * 4 + [C.c_void_p])
 _sig("to_gll_operators", C.c_int, [C.c_int32] + [C.c_void_p] * 4)
 _sig("to_synth_fill", C.c_int, [C.c_void_p, C.c_int32, C.c_int64, C.c_uint64, C.c_int32,

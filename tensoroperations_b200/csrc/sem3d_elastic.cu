@@ -2,9 +2,18 @@
 #include <cstring>
 #include <mutex>
 #include <new>
+#include <type_traits>
+
+#include <cstdlib>
 
 #include "common.hpp"
 #include "sem3d_elastic.cuh"
+
+namespace to_b200 {
+__device__ int g_to_device_status = 0;
+}
+
+#include "sem3d_elastic_tma.cuh"
 
 struct to_sem3d_plan {
   to_sem3d_desc desc;
@@ -34,38 +43,40 @@ size_t sem3d_smem_bytes() {
   return sizeof(T) * (9ull * N * EB * N * N + 2ull * N * N) + 4ull * N * EB * N * N;
 }
 
-template <typename T, int N, bool ASM>
-int launch_sem3d(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t stream) {
-  constexpr int EB = Sem3dConfig<T, N>::EB;
-  constexpr int NT = EB * N * N;
-  const size_t smem = sem3d_smem_bytes<T, N>();
-  auto kernel = sem3d_elastic_kernel<T, N, EB, ASM>;
+// Per-kernel launch state, configured once per device: the shared-memory
+// opt-in and the number of resident CTAs per SM.
+struct KernelSlot {
+  std::mutex mu;
+  unsigned long long configured = 0;  // bit per device id (< 64)
+  int blocks_per_sm[64] = {0};
+};
 
-  int dev = 0;
-  const int sms = device_sm_count(&dev);
-  if (sms <= 0) return -sms;
-
-  // Opt in to the large shared-memory carve-out once per device.
-  static std::mutex mu;
-  static unsigned long long configured = 0;  // bit per device id (< 64)
-  static int blocks_per_sm[64] = {0};
+template <typename Kernel>
+int configure(KernelSlot& slot, Kernel kernel, int dev, int threads, size_t smem, int* nb_out) {
   if (dev >= 64) return set_error(TO_ERR_UNSUPPORTED, "device id %d >= 64", dev);
-  {
-    std::lock_guard<std::mutex> lock(mu);
-    if (!(configured & (1ull << dev))) {
-      TO_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem)));
-      int nb = 0;
-      TO_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kernel, NT, smem));
-      if (nb <= 0)
-        return set_error(TO_ERR_SCRATCH,
-                         "sem3d kernel (%d threads, %zu B shared) cannot be resident", NT,
-                         smem);
-      blocks_per_sm[dev] = nb;
-      configured |= (1ull << dev);
-    }
+  std::lock_guard<std::mutex> lock(slot.mu);
+  if (!(slot.configured & (1ull << dev))) {
+    int optin = 0;
+    TO_CUDA_TRY(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    if (smem > static_cast<size_t>(optin))
+      return set_error(TO_ERR_SCRATCH, "kernel needs %zu B of shared memory, device allows %d",
+                       smem, optin);
+    TO_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(smem)));
+    int nb = 0;
+    TO_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kernel, threads, smem));
+    if (nb <= 0)
+      return set_error(TO_ERR_SCRATCH, "kernel (%d threads, %zu B shared) cannot be resident",
+                       threads, smem);
+    slot.blocks_per_sm[dev] = nb;
+    slot.configured |= (1ull << dev);
   }
+  *nb_out = slot.blocks_per_sm[dev];
+  return TO_OK;
+}
 
+template <typename T, int N>
+Sem3dArgs<T, N> make_args(const to_sem3d_plan* plan, const to_sem3d_fields* fl) {
   Sem3dArgs<T, N> a;
   std::memset(&a, 0, sizeof(a));
   for (int c = 0; c < 3; ++c) {
@@ -76,14 +87,7 @@ int launch_sem3d(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStrea
   const void* m[kNumPointArrays] = {fl->xix,  fl->xiy,  fl->xiz,  fl->etax,
                                     fl->etay, fl->etaz, fl->gamx, fl->gamy,
                                     fl->gamz, fl->jac,  fl->l2m,  fl->mu};
-  bool pf = aligned(fl->ibool, 16) || !ASM;
-  for (int q = 0; q < kNumPointArrays; ++q) {
-    a.m[q] = static_cast<const T*>(m[q]);
-    pf = pf && aligned(m[q], 16);
-  }
-  if (!ASM)
-    for (int c = 0; c < 3; ++c) pf = pf && aligned(fl->u[c], 16);
-  a.prefetch = pf ? 1 : 0;
+  for (int q = 0; q < kNumPointArrays; ++q) a.m[q] = static_cast<const T*>(m[q]);
   a.nelem = plan->desc.nelem;
   for (int i = 0; i < N; ++i) {
     a.ops.w[i] = static_cast<T>(plan->w[i]);
@@ -92,14 +96,89 @@ int launch_sem3d(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStrea
       a.ops.Hw[i][p] = static_cast<T>(plan->Hw[i * N + p]);
     }
   }
+  return a;
+}
 
+// Every array the TMA kernel stages is 16-byte aligned.
+bool staged_arrays_aligned(const to_sem3d_fields* fl, bool assembled) {
+  const void* m[] = {fl->xix, fl->xiy, fl->xiz, fl->etax, fl->etay, fl->etaz,
+                     fl->gamx, fl->gamy, fl->gamz, fl->jac, fl->l2m, fl->mu};
+  for (const void* p : m)
+    if (!aligned(p, 16)) return false;
+  if (assembled) return aligned(fl->ibool, 16);
+  for (int c = 0; c < 3; ++c)
+    if (!aligned(fl->u[c], 16)) return false;
+  return true;
+}
+
+// The register-streaming kernel (any 4-byte alignment).
+template <typename T, int N, bool ASM>
+int launch_ldg(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t stream,
+               int dev, int sms) {
+  constexpr int EB = Sem3dConfig<T, N>::EB;
+  constexpr int NT = EB * N * N;
+  const size_t smem = sem3d_smem_bytes<T, N>();
+  auto kernel = sem3d_elastic_kernel<T, N, EB, ASM>;
+  static KernelSlot slot;
+  int nb = 0;
+  if (int st = configure(slot, kernel, dev, NT, smem, &nb)) return st;
+  Sem3dArgs<T, N> a = make_args<T, N>(plan, fl);
+  bool pf = ASM ? aligned(fl->ibool, 16) : true;
+  for (int q = 0; q < kNumPointArrays; ++q) pf = pf && aligned(a.m[q], 16);
+  if (!ASM)
+    for (int c = 0; c < 3; ++c) pf = pf && aligned(fl->u[c], 16);
+  a.prefetch = pf ? 1 : 0;
   const long long nbatch = (plan->desc.nelem + EB - 1) / EB;
-  const long long cap = static_cast<long long>(sms) * blocks_per_sm[dev];
+  const long long cap = static_cast<long long>(sms) * nb;
   const int grid = static_cast<int>(nbatch < cap ? nbatch : cap);
-  if (grid <= 0) return ok();
   kernel<<<grid, NT, smem, stream>>>(a);
   TO_CUDA_TRY(cudaGetLastError());
   return ok();
+}
+
+// The TMA-staged kernel (all staged arrays 16-byte aligned).
+template <typename T, int N, int EB, int MINB, bool ASM>
+int launch_tma(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t stream,
+               int dev, int sms) {
+  constexpr int NT = EB * N * N;
+  const size_t smem = Sem3dTmaLayout<T, N, EB, ASM>::kTotal;
+  auto kernel = sem3d_elastic_tma_kernel<T, N, EB, MINB, ASM>;
+  static KernelSlot slot;
+  int nb = 0;
+  if (int st = configure(slot, kernel, dev, NT, smem, &nb)) return st;
+  Sem3dArgs<T, N> a = make_args<T, N>(plan, fl);
+  a.prefetch = 1;
+  const long long nbatch = (plan->desc.nelem + EB - 1) / EB;
+  const long long cap = static_cast<long long>(sms) * nb;
+  const int grid = static_cast<int>(nbatch < cap ? nbatch : cap);
+  kernel<<<grid, NT, smem, stream>>>(a);
+  TO_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
+// Kernel variant for f32 NGLL 5: 0 = TMA EB 8 x 2 CTAs/SM (default),
+// 1 = TMA EB 16 x 1 CTA/SM, 2 = register-streaming kernel.
+int sem3d_f32_variant() {
+  static const int v = [] {
+    const char* e = std::getenv("TO_SEM3D_VARIANT");
+    return e ? std::atoi(e) : 0;
+  }();
+  return v;
+}
+
+template <typename T, int N, bool ASM>
+int launch_sem3d(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t stream) {
+  int dev = 0;
+  const int sms = device_sm_count(&dev);
+  if (sms <= 0) return -sms;
+  if constexpr (std::is_same_v<T, float> && N == 5) {
+    const int v = sem3d_f32_variant();
+    if (v != 2 && staged_arrays_aligned(fl, ASM)) {
+      if (v == 1) return launch_tma<T, N, 16, 1, ASM>(plan, fl, stream, dev, sms);
+      return launch_tma<T, N, 8, 2, ASM>(plan, fl, stream, dev, sms);
+    }
+  }
+  return launch_ldg<T, N, ASM>(plan, fl, stream, dev, sms);
 }
 
 template <typename T, int N>
@@ -184,6 +263,17 @@ int to_sem3d_apply(const to_sem3d_plan* plan, const to_sem3d_fields* fields,
   if (d.ngll == 5 && d.dtype == TO_F64) return apply_typed<double, 5>(plan, fields, accumulate, s);
   return set_error(TO_ERR_UNSUPPORTED, "to_sem3d_apply: ngll %d dtype %d not built", d.ngll,
                    d.dtype);
+}
+
+int to_device_status(int32_t reset) {
+  int v = 0;
+  TO_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_to_device_status, sizeof(int)));
+  if (reset && v) {
+    const int z = 0;
+    TO_CUDA_TRY(cudaMemcpyToSymbol(g_to_device_status, &z, sizeof(int)));
+  }
+  if (v) return set_error(v, "a kernel reported %s", to_status_string(v));
+  return ok();
 }
 
 double to_sem3d_algorithmic_bytes(const to_sem3d_plan* plan) {

@@ -90,7 +90,7 @@ __global__ void __launch_bounds__(EB* N* N, 1)
   constexpr int NN = N * N;
   constexpr int P = N * N * N;
   constexpr int NT = EB * NN;  // threads per CTA = points per k-slice of a batch
-  extern __shared__ __align__(16) unsigned char smem_raw[];
+  extern __shared__ __align__(128) unsigned char smem_raw[];
   T* su = reinterpret_cast<T*>(smem_raw);  // [3][N][NT]   u_c(k, thread)
   T* sF = su + 3 * N * NT;                 // [6][N][NT]   F^xi_c, F^eta_c
 
