@@ -45,9 +45,11 @@ METRIC = ("SEM stiffness Melem/s and HBM GB/s (% of ~8 TB/s) at 1/2/4/8 B200 vs 
 MESH_PER_GPU = (64, 64, 64)
 NGLL = 5
 FALLBACK_HBM_GBS = 6650.0
-KERNEL_NAMES = {"0": "sem3d_elastic_tma_kernel<float,5,8,2,true>",
-                "1": "sem3d_elastic_tma_kernel<float,5,16,1,true>",
-                "2": "sem3d_elastic_kernel<float,5,32,true>"}
+KERNEL_NAMES = {"0": "sem3d_elastic_v3_kernel<5,8,2,true>",
+                "1": "sem3d_elastic_tma_kernel<float,5,8,2,true>",
+                "2": "sem3d_elastic_kernel<float,5,32,true>",
+                "3": "sem3d_elastic_v3_kernel<5,4,4,true>",
+                "4": "sem3d_elastic_v3_kernel<5,16,1,true>"}
 
 
 def measured_peak_hbm():
@@ -236,7 +238,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--variant", type=int, default=None,
-                    help="f32 kernel variant (TO_SEM3D_VARIANT): 0 TMA 8x2, 1 TMA 16x1, 2 streaming")
+                    help="f32 kernel variant (TO_SEM3D_VARIANT): 0 point-pair 8x2, 1 TMA 8x2, "
+                         "2 streaming, 3 point-pair 4x4, 4 point-pair 16x1")
     ap.add_argument("--mesh", type=int, nargs=3, default=[64, 64, 64],
                     metavar=("NEX", "NEY", "NEZ"), help="hexes per GPU (profiling runs)")
     args = ap.parse_args()

@@ -14,6 +14,7 @@ __device__ int g_to_device_status = 0;
 }
 
 #include "sem3d_elastic_tma.cuh"
+#include "sem3d_elastic_v3.cuh"
 
 struct to_sem3d_plan {
   to_sem3d_desc desc;
@@ -156,8 +157,32 @@ int launch_tma(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_
   return ok();
 }
 
-// Kernel variant for f32 NGLL 5: 0 = TMA EB 8 x 2 CTAs/SM (default),
-// 1 = TMA EB 16 x 1 CTA/SM, 2 = register-streaming kernel.
+// The point-pair / gather-pipelined kernel (f32, staged arrays 16-byte aligned).
+template <int N, int EB, int MINB, bool ASM>
+int launch_v3(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t stream,
+              int dev, int sms) {
+  constexpr int NT = EB * N * N;
+  const size_t smem = Sem3dV3Layout<N, EB, ASM>::kTotal;
+  auto kernel = sem3d_elastic_v3_kernel<N, EB, MINB, ASM>;
+  static KernelSlot slot;
+  int nb = 0;
+  if (int st = configure(slot, kernel, dev, NT, smem, &nb)) return st;
+  Sem3dArgs<float, N> a = make_args<float, N>(plan, fl);
+  a.prefetch = 1;
+  const long long nbatch = (plan->desc.nelem + EB - 1) / EB;
+  const long long cap = static_cast<long long>(sms) * nb;
+  const int grid = static_cast<int>(nbatch < cap ? nbatch : cap);
+  kernel<<<grid, NT, smem, stream>>>(a);
+  TO_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
+// Kernel variant for f32 NGLL 5 (TO_SEM3D_VARIANT):
+//   0 point-pair pipelined kernel, 8 elements x 2 CTAs/SM (default)
+//   1 TMA-staged kernel, 8 elements x 2 CTAs/SM
+//   2 register-streaming kernel
+//   3 point-pair pipelined kernel, 4 elements x 4 CTAs/SM
+//   4 point-pair pipelined kernel, 16 elements x 1 CTA/SM
 int sem3d_f32_variant() {
   static const int v = [] {
     const char* e = std::getenv("TO_SEM3D_VARIANT");
@@ -174,8 +199,10 @@ int launch_sem3d(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStrea
   if constexpr (std::is_same_v<T, float> && N == 5) {
     const int v = sem3d_f32_variant();
     if (v != 2 && staged_arrays_aligned(fl, ASM)) {
-      if (v == 1) return launch_tma<T, N, 16, 1, ASM>(plan, fl, stream, dev, sms);
-      return launch_tma<T, N, 8, 2, ASM>(plan, fl, stream, dev, sms);
+      if (v == 1) return launch_tma<T, N, 8, 2, ASM>(plan, fl, stream, dev, sms);
+      if (v == 3) return launch_v3<N, 4, 4, ASM>(plan, fl, stream, dev, sms);
+      if (v == 4) return launch_v3<N, 16, 1, ASM>(plan, fl, stream, dev, sms);
+      return launch_v3<N, 8, 2, ASM>(plan, fl, stream, dev, sms);
     }
   }
   return launch_ldg<T, N, ASM>(plan, fl, stream, dev, sms);

@@ -110,3 +110,32 @@ __device__ __forceinline__ double mul2(double a, double b) { return a * b; }
 __device__ __forceinline__ double add2(double a, double b) { return a + b; }
 
 }  // namespace to_b200
+
+namespace to_b200 {
+
+// L2 cache policy that evicts first: for data streamed exactly once.
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes,
+                                              uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void l2_prefetch_bulk_hint(const void* p, uint32_t bytes,
+                                                      uint64_t policy) {
+  bytes &= ~15u;
+  if (bytes == 0) return;
+  asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(p),
+               "r"(bytes), "l"(policy)
+               : "memory");
+}
+
+}  // namespace to_b200
