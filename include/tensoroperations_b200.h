@@ -162,6 +162,60 @@ double to_sem3d_algorithmic_bytes(const to_sem3d_plan* plan);
 /* Useful floating-point operations of one application (36N+159 per point). */
 double to_sem3d_flops(const to_sem3d_plan* plan);
 
+/* ---------------------------------------------------------------------- */
+/* Level-graph lowering                                                    */
+/* ---------------------------------------------------------------------- */
+/*
+ * The header-only C++ frontend (make_level_graph / add / outputs / execute)
+ * plans a level graph at compile time -- slots, level-timeline liveness,
+ * pooled scratch, tiles -- and lowers the plan to this descriptor before every
+ * launch (the reference launches from LevelGraph::launch / lg_execute,
+ * include/TensorOperations/LevelGraph.hpp:576-628,718-733).  The library
+ * re-checks the plan independently and returns the launch shape:
+ *   - every pair of slots sharing a pool has disjoint live ranges and every
+ *     pool is large enough for its slots (else TO_ERR_INVALID_ARGUMENT);
+ *   - a label declared whole on a staged input is not longer than its tile
+ *     (TO_ERR_GRID; the reference aborts, LevelGraph.hpp:519-522);
+ *   - league = product over blocked labels of ceil(extent / tile);
+ *   - team: the requested size (1..1024) or, when <= 0, the smallest multiple
+ *     of 32 covering the widest level, clamped to [64, 512];
+ *   - with query_device != 0, the scratch must fit the current device's
+ *     opt-in shared memory per block (TO_ERR_SCRATCH).
+ * Host only apart from the optional device-attribute query.
+ */
+typedef struct to_level_plan_desc {
+  int32_t value_bytes;          /* sizeof(value type)                          */
+  int32_t num_levels;
+  int32_t num_slots;
+  int32_t num_pools;
+  const int32_t* level_kind;    /* [num_levels] 0 stage, 1 contraction, 2 combine */
+  const int32_t* level_members; /* [num_levels]                                */
+  const int64_t* level_space;   /* [num_levels] items of the level's one loop  */
+  const int32_t* slot_def;      /* [num_slots] level that writes the slot      */
+  const int32_t* slot_last;     /* [num_slots] last level reading it (roots: num_levels) */
+  const int32_t* slot_pool;     /* [num_slots]                                 */
+  const int64_t* slot_bytes;    /* [num_slots]                                 */
+  const int64_t* pool_offset;   /* [num_pools + 1] byte offsets, then the total */
+  int32_t grid_rank;            /* number of blocked labels carried by stages  */
+  int32_t num_whole;            /* whole-label checks                          */
+  const int64_t* grid_extent;   /* [grid_rank] global extent per blocked label */
+  const int32_t* grid_tile;     /* [grid_rank]                                 */
+  const int64_t* whole_extent;  /* [num_whole] staged extent along a whole label */
+  const int32_t* whole_tile;    /* [num_whole]                                 */
+  int32_t team_size;            /* <= 0: automatic                             */
+  int32_t reserved0;
+} to_level_plan_desc;
+
+typedef struct to_level_launch {
+  int64_t league;         /* CTAs (one per grid tile)                          */
+  int64_t scratch_bytes;  /* dynamic shared memory per CTA                     */
+  int32_t team;           /* threads per CTA                                   */
+  int32_t reserved0;
+} to_level_launch;
+
+int to_level_plan_lower(const to_level_plan_desc* desc, int32_t query_device,
+                        to_level_launch* out);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -1,0 +1,77 @@
+"""Build recipe for artefacts compiled from the REFERENCE's own sources.
+
+Test infrastructure only.  Run here, where the reference tree is mounted; the
+outputs (in oracle/_ref/, git-ignored, shipped with the repository snapshot)
+are what the tests use on the GPU box, which has no reference tree.
+
+  libref_sem3d.so         benchmarks/sem_stiffness_3d/bench_sem3d_levelgraph.cpp
+                          compiled host-only (g++, -ffp-contract=off) through
+                          oracle/ref_pin.cpp: the reference's fill() and
+                          reference() behind a C ABI, to pin the CPU oracle.
+  bench_sem3d_levelgraph  the same reference program, unmodified, compiled for
+                          sm_100a against this repository's frontend headers
+                          and Kokkos subset: the drop-in check (its own
+                          PASS/FAIL against its own host reference).
+
+The reference's own build (CMake fetching Kokkos/GoogleTest/KokkosKernels) is
+not used; Kokkos is replaced by tensoroperations_b200/include/Kokkos_Core.hpp.
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parent
+OUT = HERE / "_ref"
+REF = Path(os.environ.get("TO_REFERENCE_ROOT", "/root/reference"))
+SEM3D = REF / "benchmarks" / "sem_stiffness_3d" / "bench_sem3d_levelgraph.cpp"
+INC = [f"-I{ROOT / 'include'}", f"-I{ROOT / 'tensoroperations_b200' / 'include'}"]
+LIBDIR = ROOT / "tensoroperations_b200"
+NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+
+PIN = OUT / "libref_sem3d.so"
+DROPIN = OUT / "bench_sem3d_levelgraph"
+
+
+def available() -> bool:
+    return SEM3D.exists()
+
+
+def _run(cmd):
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError("reference build failed: " + " ".join(map(str, cmd)) + "\n" + r.stderr[-4000:])
+
+
+def _stale(target: Path, deps) -> bool:
+    return not target.exists() or any(d.stat().st_mtime > target.stat().st_mtime for d in deps)
+
+
+def _frontend_headers():
+    inc = ROOT / "tensoroperations_b200" / "include"
+    return sorted(inc.rglob("*.hpp")) + sorted(inc.rglob("*.cuh")) + [ROOT / "include" / "tensoroperations_b200.h"]
+
+
+def build(force: bool = False):
+    if not available():
+        return None
+    OUT.mkdir(exist_ok=True)
+    deps = [SEM3D, HERE / "ref_pin.cpp"] + _frontend_headers()
+    if force or _stale(PIN, deps):
+        _run(["g++", "-std=c++20", "-O2", "-ffp-contract=off", "-fno-fast-math", "-fPIC", "-shared",
+              *INC, f'-DBENCH_SEM3D_SOURCE="{SEM3D}"', str(HERE / "ref_pin.cpp"),
+              f"-L{LIBDIR}", "-ltensoroperations_b200", f"-Wl,-rpath,{LIBDIR}",
+              "-Wl,-rpath,$ORIGIN/../../tensoroperations_b200", "-o", str(PIN)])
+    if force or _stale(DROPIN, deps + [LIBDIR / "libtensoroperations_b200.so"]):
+        _run([NVCC, "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++20",
+              "--extended-lambda", "--expt-relaxed-constexpr", "-diag-suppress", "186,20012",
+              *INC, "-x", "cu", str(SEM3D), f"-L{LIBDIR}", "-ltensoroperations_b200",
+              "-Xlinker", "-rpath,$ORIGIN/../../tensoroperations_b200", "-o", str(DROPIN)])
+    return PIN, DROPIN
+
+
+if __name__ == "__main__":
+    print(build(force="--force" in sys.argv))

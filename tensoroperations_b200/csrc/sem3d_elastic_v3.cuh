@@ -9,18 +9,20 @@
 //    batch -- that wait was 38% of all stall cycles in the TMA-only design.
 //  * Shared-memory operands of the contractions are stored as point-pair
 //    blocks: for the k-pair (k0, k1) a thread's block holds, per component c,
-//    the float2 (x(k0), x(k1)) -- 3 float2 + pad = 32 B.  One LDS.128 then
-//    feeds packed f32x2 FMAs for two points at once with no register
-//    shuffles, and the operator coefficients are held as duplicated float2
-//    pairs built once per phase.  The odd last k of NGLL 5 uses a float4
-//    (c0, c1, c2, pad) block with scalar FMAs.
+//    the float2 (x(k0), x(k1)): components 0 and 1 in one float4 array and
+//    component 2 in a float2 array (no padding -- shared-memory wavefronts
+//    are the limiting resource).  One LDS.128 + one LDS.64 then feed packed
+//    f32x2 FMAs for two points at once with no register shuffles; the
+//    operator coefficients are held as duplicated float2 pairs built once
+//    per phase.  The odd last k of NGLL 5 uses float2 + float arrays with
+//    scalar FMAs.
 //  * The 12 per-point arrays of a batch move global -> shared with one bulk
 //    copy each (cp.async.bulk, L2::evict_first: the data is read exactly once)
 //    after an L2 bulk prefetch two batches ahead.  ibool is not staged: it is
 //    read by the gather pipeline.
 //
 // Shared memory per CTA (EB elements, NT = 25 EB threads): stage 12 EB 500 B,
-// u / F^xi / F^eta blocks 3 x (2 x 32 + 16) B x NT, H and Hw.
+// u / F^xi / F^eta blocks 3 x (2 x 24 + 12) B x NT, H and Hw.
 #pragma once
 
 #include <cstdint>
@@ -40,8 +42,11 @@ struct Sem3dV3Layout {
   static constexpr int kStaged = kNumPointArrays + (ASM ? 0 : 3);
   static constexpr size_t kHeader = 128;
   static constexpr size_t kStageBytes = size_t(kStaged) * EP * 4;
-  // one "block set": NP pair blocks (32 B) + one single block (16 B) per thread
-  static constexpr size_t kBlockSetBytes = size_t(NT) * (NP * 32 + (ODD ? 16 : 0));
+  // one "block set" per quantity: for each k-pair a float4 (c0, c1 pairs) and a
+  // float2 (c2 pair) per thread; for the odd k a float2 (c0, c1) and a float (c2)
+  static constexpr size_t kPairA = size_t(NT) * NP * 16, kPairB = size_t(NT) * NP * 8;
+  static constexpr size_t kSingA = ODD ? size_t(NT) * 8 : 0, kSingB = ODD ? size_t(NT) * 4 : 0;
+  static constexpr size_t kBlockSetBytes = (kPairA + kPairB + kSingA + kSingB + 15) & ~size_t(15);
   static constexpr size_t kOpsBytes = size_t(2) * NN * 4;
   static constexpr size_t kTotal = kHeader + kStageBytes + 3 * kBlockSetBytes + kOpsBytes;
 };
@@ -60,13 +65,20 @@ __global__ void __launch_bounds__(EB* N* N, MINB)
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);
   float* stage = reinterpret_cast<float*>(smem_raw + LY::kHeader);
   unsigned char* blocks = smem_raw + LY::kHeader + LY::kStageBytes;
-  // block sets: 0 = u, 1 = F^xi, 2 = F^eta.  Pair blocks: float4 index (kp*NT + t)*2 + h.
-  float4* pairU = reinterpret_cast<float4*>(blocks);
-  float4* singU = reinterpret_cast<float4*>(blocks + size_t(NT) * NP * 32);
-  float4* pairX = reinterpret_cast<float4*>(blocks + LY::kBlockSetBytes);
-  float4* singX = reinterpret_cast<float4*>(blocks + LY::kBlockSetBytes + size_t(NT) * NP * 32);
-  float4* pairE = reinterpret_cast<float4*>(blocks + 2 * LY::kBlockSetBytes);
-  float4* singE = reinterpret_cast<float4*>(blocks + 2 * LY::kBlockSetBytes + size_t(NT) * NP * 32);
+  // block sets: 0 = u, 1 = F^xi, 2 = F^eta
+  struct BlockSet {
+    float4* pa;  // [NP][NT]  (c0(k0), c0(k1), c1(k0), c1(k1))
+    float2* pb;  // [NP][NT]  (c2(k0), c2(k1))
+    float2* sa;  // [NT]      (c0, c1) of the odd k
+    float* sb;   // [NT]      c2 of the odd k
+  };
+  auto block_set = [&](int q) {
+    unsigned char* p = blocks + size_t(q) * LY::kBlockSetBytes;
+    return BlockSet{reinterpret_cast<float4*>(p), reinterpret_cast<float2*>(p + LY::kPairA),
+                    reinterpret_cast<float2*>(p + LY::kPairA + LY::kPairB),
+                    reinterpret_cast<float*>(p + LY::kPairA + LY::kPairB + LY::kSingA)};
+  };
+  const BlockSet BU = block_set(0), BX = block_set(1), BE = block_set(2);
   float* sops = reinterpret_cast<float*>(blocks + 3 * LY::kBlockSetBytes);
 
   const int tid = threadIdx.x;
@@ -200,10 +212,13 @@ __global__ void __launch_bounds__(EB* N* N, MINB)
 #pragma unroll
       for (int kp = 0; kp < NP; ++kp) {
         const int k0 = 2 * kp, k1 = k0 + 1;
-        pairU[(kp * NT + tid) * 2 + 0] = make_float4(uc[0][k0], uc[0][k1], uc[1][k0], uc[1][k1]);
-        pairU[(kp * NT + tid) * 2 + 1] = make_float4(uc[2][k0], uc[2][k1], 0.f, 0.f);
+        BU.pa[kp * NT + tid] = make_float4(uc[0][k0], uc[0][k1], uc[1][k0], uc[1][k1]);
+        BU.pb[kp * NT + tid] = f2(uc[2][k0], uc[2][k1]);
       }
-      if (ODD) singU[tid] = make_float4(uc[0][N - 1], uc[1][N - 1], uc[2][N - 1], 0.f);
+      if (ODD) {
+        BU.sa[tid] = f2(uc[0][N - 1], uc[1][N - 1]);
+        BU.sb[tid] = uc[2][N - 1];
+      }
 #pragma unroll
       for (int c = 0; c < 3; ++c) {
 #pragma unroll
@@ -243,16 +258,16 @@ __global__ void __launch_bounds__(EB* N* N, MINB)
         float2 ge[3] = {f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f)};
 #pragma unroll
         for (int p = 0; p < N; ++p) {
-          const float4 xl = pairU[(kp * NT + row + p) * 2 + 0];
-          const float4 xh = pairU[(kp * NT + row + p) * 2 + 1];
-          const float4 yl = pairU[(kp * NT + col + p * N) * 2 + 0];
-          const float4 yh = pairU[(kp * NT + col + p * N) * 2 + 1];
+          const float4 xl = BU.pa[kp * NT + row + p];
+          const float2 xh = BU.pb[kp * NT + row + p];
+          const float4 yl = BU.pa[kp * NT + col + p * N];
+          const float2 yh = BU.pb[kp * NT + col + p * N];
           gx[0] = ffma2(HiHi[p], f2(xl.x, xl.y), gx[0]);
           gx[1] = ffma2(HiHi[p], f2(xl.z, xl.w), gx[1]);
-          gx[2] = ffma2(HiHi[p], f2(xh.x, xh.y), gx[2]);
+          gx[2] = ffma2(HiHi[p], xh, gx[2]);
           ge[0] = ffma2(HjHj[p], f2(yl.x, yl.y), ge[0]);
           ge[1] = ffma2(HjHj[p], f2(yl.z, yl.w), ge[1]);
-          ge[2] = ffma2(HjHj[p], f2(yh.x, yh.y), ge[2]);
+          ge[2] = ffma2(HjHj[p], yh, ge[2]);
         }
         V2<float> dxi[3], det[3], dgm[3], J[3][3];
 #pragma unroll
@@ -275,10 +290,10 @@ __global__ void __launch_bounds__(EB* N* N, MINB)
         integrand9_lanes<V2<float>, float>(dxi, det, dgm, J, mk2(ql[k0 * NN], ql[k1 * NN]),
                                            mk2(qm[k0 * NN], qm[k1 * NN]),
                                            mk2(qj[k0 * NN], qj[k1 * NN]), F);
-        pairX[(kp * NT + tid) * 2 + 0] = make_float4(F[0][0].v.x, F[0][0].v.y, F[0][1].v.x, F[0][1].v.y);
-        pairX[(kp * NT + tid) * 2 + 1] = make_float4(F[0][2].v.x, F[0][2].v.y, 0.f, 0.f);
-        pairE[(kp * NT + tid) * 2 + 0] = make_float4(F[1][0].v.x, F[1][0].v.y, F[1][1].v.x, F[1][1].v.y);
-        pairE[(kp * NT + tid) * 2 + 1] = make_float4(F[1][2].v.x, F[1][2].v.y, 0.f, 0.f);
+        BX.pa[kp * NT + tid] = make_float4(F[0][0].v.x, F[0][0].v.y, F[0][1].v.x, F[0][1].v.y);
+        BX.pb[kp * NT + tid] = F[0][2].v;
+        BE.pa[kp * NT + tid] = make_float4(F[1][0].v.x, F[1][0].v.y, F[1][1].v.x, F[1][1].v.y);
+        BE.pb[kp * NT + tid] = F[1][2].v;
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
           Fg[c][k0] = F[2][c].v.x;
@@ -290,14 +305,16 @@ __global__ void __launch_bounds__(EB* N* N, MINB)
         float gx[3] = {0.f, 0.f, 0.f}, ge[3] = {0.f, 0.f, 0.f};
 #pragma unroll
         for (int p = 0; p < N; ++p) {
-          const float4 x = singU[row + p];
-          const float4 y = singU[col + p * N];
+          const float2 x = BU.sa[row + p];
+          const float x2 = BU.sb[row + p];
+          const float2 y = BU.sa[col + p * N];
+          const float y2 = BU.sb[col + p * N];
           gx[0] += HiHi[p].x * x.x;
           gx[1] += HiHi[p].x * x.y;
-          gx[2] += HiHi[p].x * x.z;
+          gx[2] += HiHi[p].x * x2;
           ge[0] += HjHj[p].x * y.x;
           ge[1] += HjHj[p].x * y.y;
-          ge[2] += HjHj[p].x * y.z;
+          ge[2] += HjHj[p].x * y2;
         }
         float J[3][3];
 #pragma unroll
@@ -308,8 +325,10 @@ __global__ void __launch_bounds__(EB* N* N, MINB)
         integrand9_lanes<float, float>(gx, ge, dgs, J, stage[size_t(kL2M) * EP + spt + k * NN],
                                        stage[size_t(kMU) * EP + spt + k * NN],
                                        stage[size_t(kJAC) * EP + spt + k * NN], F);
-        singX[tid] = make_float4(F[0][0], F[0][1], F[0][2], 0.f);
-        singE[tid] = make_float4(F[1][0], F[1][1], F[1][2], 0.f);
+        BX.sa[tid] = f2(F[0][0], F[0][1]);
+        BX.sb[tid] = F[0][2];
+        BE.sa[tid] = f2(F[1][0], F[1][1]);
+        BE.sb[tid] = F[1][2];
 #pragma unroll
         for (int c = 0; c < 3; ++c) Fg[c][k] = F[2][c];
       }
@@ -336,16 +355,16 @@ __global__ void __launch_bounds__(EB* N* N, MINB)
         float2 te[3] = {f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f)};
 #pragma unroll
         for (int q = 0; q < N; ++q) {
-          const float4 xl = pairX[(kp * NT + row + q) * 2 + 0];
-          const float4 xh = pairX[(kp * NT + row + q) * 2 + 1];
-          const float4 yl = pairE[(kp * NT + col + q * N) * 2 + 0];
-          const float4 yh = pairE[(kp * NT + col + q * N) * 2 + 1];
+          const float4 xl = BX.pa[kp * NT + row + q];
+          const float2 xh = BX.pb[kp * NT + row + q];
+          const float4 yl = BE.pa[kp * NT + col + q * N];
+          const float2 yh = BE.pb[kp * NT + col + q * N];
           tx[0] = ffma2(WiWi[q], f2(xl.x, xl.y), tx[0]);
           tx[1] = ffma2(WiWi[q], f2(xl.z, xl.w), tx[1]);
-          tx[2] = ffma2(WiWi[q], f2(xh.x, xh.y), tx[2]);
+          tx[2] = ffma2(WiWi[q], xh, tx[2]);
           te[0] = ffma2(WjWj[q], f2(yl.x, yl.y), te[0]);
           te[1] = ffma2(WjWj[q], f2(yl.z, yl.w), te[1]);
-          te[2] = ffma2(WjWj[q], f2(yh.x, yh.y), te[2]);
+          te[2] = ffma2(WjWj[q], yh, te[2]);
         }
         const float2 wjk = f2(wj * a.ops.w[k0], wj * a.ops.w[k1]);
         const float2 wik = f2(wi * a.ops.w[k0], wi * a.ops.w[k1]);
@@ -375,14 +394,16 @@ __global__ void __launch_bounds__(EB* N* N, MINB)
         float tx[3] = {0.f, 0.f, 0.f}, te[3] = {0.f, 0.f, 0.f};
 #pragma unroll
         for (int q = 0; q < N; ++q) {
-          const float4 x = singX[row + q];
-          const float4 y = singE[col + q * N];
+          const float2 x = BX.sa[row + q];
+          const float x2 = BX.sb[row + q];
+          const float2 y = BE.sa[col + q * N];
+          const float y2 = BE.sb[col + q * N];
           tx[0] += WiWi[q].x * x.x;
           tx[1] += WiWi[q].x * x.y;
-          tx[2] += WiWi[q].x * x.z;
+          tx[2] += WiWi[q].x * x2;
           te[0] += WjWj[q].x * y.x;
           te[1] += WjWj[q].x * y.y;
-          te[2] += WjWj[q].x * y.z;
+          te[2] += WjWj[q].x * y2;
         }
         const float wjk = wj * a.ops.w[k], wik = wi * a.ops.w[k];
 #pragma unroll

@@ -199,7 +199,7 @@ struct ScratchMemorySpace {
   std::size_t size_ = 0;
   mutable std::size_t used_ = 0;
 
-  KOKKOS_INLINE_FUNCTION ScratchMemorySpace() = default;
+  ScratchMemorySpace() = default;
   KOKKOS_INLINE_FUNCTION ScratchMemorySpace(void* base, std::size_t size)
       : base_(static_cast<char*>(base)), size_(size), used_(0) {}
   KOKKOS_INLINE_FUNCTION void* get_shmem(std::size_t bytes) const {
@@ -241,12 +241,6 @@ struct DataAnalysis {
   static constexpr int rank = rank_dynamic + rank_static;
   using value_type = typename PtrDepth<no_arr>::base;
 
-  template <std::size_t... Is>
-  static constexpr Array<std::size_t, rank_static + 1> statics(std::index_sequence<Is...>) {
-    return {{std::extent_v<DataType, Is>..., 0}};
-  }
-  static constexpr Array<std::size_t, rank_static + 1> static_extents =
-      statics(std::make_index_sequence<rank_static>{});
 };
 
 template <class T>
@@ -263,10 +257,13 @@ template <class T>
 struct has_exec_space<T, std::void_t<typename T::execution_space>> : std::true_type {};
 
 // Memory space named by a View property, or void.
-template <class P>
+template <class P, class = void>
 struct MemSpaceOf {
-  using type = std::conditional_t<is_layout<P>::value || is_memory_traits<P>::value, void,
-                                  typename P::memory_space>;
+  using type = void;
+};
+template <class P>
+struct MemSpaceOf<P, std::void_t<typename P::memory_space>> {
+  using type = typename P::memory_space;
 };
 
 template <class... Props>
@@ -361,7 +358,9 @@ class View {
   static constexpr bool is_scratch = Impl::is_scratch<memory_space>::value;
   static constexpr bool managed = !PA::unmanaged && !is_scratch;
   using non_const_data_type = std::remove_const_t<DataType>;
-  using host_mirror_type = View<non_const_data_type, LayoutRight, HostSpace>;
+  using host_mirror_type =
+      std::conditional_t<std::is_same_v<memory_space, HostSpace>, View<DataType, Props...>,
+                         View<non_const_data_type, LayoutRight, HostSpace>>;
   using HostMirror = host_mirror_type;
 
  private:
@@ -455,18 +454,29 @@ class View {
     data_ = static_cast<pointer_type>(space.get_shmem(span() * sizeof(value_type)));
   }
 
+  template <std::size_t... I>
+  KOKKOS_INLINE_FUNCTION static constexpr std::size_t static_extent_impl(int s,
+                                                                         std::index_sequence<I...>) {
+    std::size_t r = 0;
+    ((s == static_cast<int>(I) ? (r = std::extent_v<DataType, I>, 0) : 0), ...);
+    return r;
+  }
+  // extent of the s-th static (bracketed) dimension
+  KOKKOS_INLINE_FUNCTION static constexpr std::size_t static_extent(int s) {
+    return static_extent_impl(s, std::make_index_sequence<DA::rank_static>{});
+  }
+
   template <class... N>
   KOKKOS_INLINE_FUNCTION static std::size_t shmem_size(N... n) {
     const std::size_t e[] = {static_cast<std::size_t>(n)..., 0};
     std::size_t total = 1;
     for (int d = 0; d < rank; ++d)
-      total *= d < rank_dynamic ? (d < int(sizeof...(N)) ? e[d] : 0)
-                                : DA::static_extents[d - rank_dynamic];
+      total *= d < rank_dynamic ? (d < int(sizeof...(N)) ? e[d] : 0) : static_extent(d - rank_dynamic);
     return ScratchMemorySpace<DefaultExecutionSpace>::round(total * sizeof(value_type));
   }
 
   KOKKOS_INLINE_FUNCTION constexpr std::size_t extent(int d) const {
-    return d < rank_dynamic ? dyn_[d] : DA::static_extents[d - rank_dynamic];
+    return d < rank_dynamic ? dyn_[d] : static_extent(d - rank_dynamic);
   }
   KOKKOS_INLINE_FUNCTION constexpr int extent_int(int d) const {
     return static_cast<int>(extent(d));
@@ -484,7 +494,7 @@ class View {
   KOKKOS_INLINE_FUNCTION std::size_t span() const { return size(); }
   KOKKOS_INLINE_FUNCTION pointer_type data() const { return data_; }
   KOKKOS_INLINE_FUNCTION bool is_allocated() const { return data_ != nullptr; }
-  Impl::ControlBlock* impl_cb() const { return cb_; }
+  KOKKOS_INLINE_FUNCTION Impl::ControlBlock* impl_cb() const { return cb_; }
   std::string label() const { return cb_ ? cb_->label : std::string(); }
   int use_count() const { return cb_ ? cb_->refs.load() : 0; }
 
@@ -557,7 +567,7 @@ template <class D, class... P>
 auto create_mirror_view(const View<D, P...>& v) {
   using V = View<D, P...>;
   using M = typename V::host_mirror_type;
-  if constexpr (std::is_same_v<typename V::memory_space, HostSpace> && std::is_same_v<M, V>) {
+  if constexpr (std::is_same_v<M, V>) {
     return v;
   } else {
     M m;
@@ -778,16 +788,17 @@ void parallel_for(const char* label, const TeamPolicy<Props...>& p, const F& f) 
                            static_cast<int>(bytes));
     Impl::team_kernel<F><<<p.league_size(), team, bytes>>>(f, bytes);
     Impl::check_launch(label);
-    return;
-  }
+  } else
 #endif
-  (void)label;
-  void* buf = bytes ? std::malloc(bytes) : nullptr;
-  for (int lr = 0; lr < p.league_size(); ++lr) {
-    TeamMember<Serial> m(lr, p.league_size(), 0, 1, buf, bytes);
-    f(m);
+  {
+    (void)label;
+    void* buf = bytes ? std::malloc(bytes) : nullptr;
+    for (int lr = 0; lr < p.league_size(); ++lr) {
+      TeamMember<Serial> m(lr, p.league_size(), 0, 1, buf, bytes);
+      f(m);
+    }
+    std::free(buf);
   }
-  std::free(buf);
 }
 template <class F, class... Props>
 void parallel_for(const TeamPolicy<Props...>& p, const F& f) {
@@ -805,11 +816,12 @@ void parallel_for(const char* label, const RangePolicy<Props...>& p, const F& f)
     Impl::range_kernel<F><<<static_cast<unsigned>(blocks < 65535 * 8 ? blocks : 65535 * 8), 256>>>(
         f, p.begin_, p.end_);
     Impl::check_launch(label);
-    return;
-  }
+  } else
 #endif
-  (void)label;
-  for (std::int64_t i = p.begin_; i < p.end_; ++i) f(i);
+  {
+    (void)label;
+    for (std::int64_t i = p.begin_; i < p.end_; ++i) f(i);
+  }
 }
 template <class F, class... Props>
 void parallel_for(const RangePolicy<Props...>& p, const F& f) {

@@ -131,6 +131,26 @@ constexpr auto label_positions() {
 template <class Seq>
 using labels_array_t = decltype(to_array<Seq>());
 
+// int sequences (axis permutations)
+template <class Seq>
+struct iseq_info;
+template <int... P>
+struct iseq_info<std::integer_sequence<int, P...>> {
+  static constexpr std::array<int, sizeof...(P)> arr{P...};
+};
+template <class Seq>
+constexpr auto to_array_int() {
+  return iseq_info<Seq>::arr;
+}
+template <auto Arr, class Idx = std::make_index_sequence<Arr.size()>>
+struct array_iseq;
+template <auto Arr, std::size_t... I>
+struct array_iseq<Arr, std::index_sequence<I...>> {
+  using type = std::integer_sequence<int, static_cast<int>(Arr[I])...>;
+};
+template <auto Arr>
+using array_iseq_t = typename array_iseq<Arr>::type;
+
 }  // namespace b200
 
 // ---------------------------------------------------------------------------

@@ -46,8 +46,9 @@ template <class Seq, class... T>
 struct TupleBase;
 template <std::size_t... I, class... T>
 struct TupleBase<std::index_sequence<I...>, T...> : TupleLeaf<I, T>... {
-  KOKKOS_INLINE_FUNCTION TupleBase() = default;
-  KOKKOS_INLINE_FUNCTION explicit TupleBase(const T&... v) : TupleLeaf<I, T>{v}... {}
+  TupleBase() = default;
+  template <class... U, class = std::enable_if_t<(sizeof...(U) > 0) && sizeof...(U) == sizeof...(T)>>
+  KOKKOS_INLINE_FUNCTION explicit TupleBase(const U&... v) : TupleLeaf<I, T>{v}... {}
 };
 }  // namespace b200
 
@@ -55,7 +56,7 @@ template <class... T>
 struct DeviceTuple : b200::TupleBase<std::index_sequence_for<T...>, T...> {
   using base = b200::TupleBase<std::index_sequence_for<T...>, T...>;
   static constexpr std::size_t size = sizeof...(T);
-  KOKKOS_INLINE_FUNCTION DeviceTuple() = default;
+  DeviceTuple() = default;
   template <class... U, class = std::enable_if_t<sizeof...(U) == sizeof...(T) && (sizeof...(T) > 0)>>
   KOKKOS_INLINE_FUNCTION explicit DeviceTuple(const U&... v) : base(v...) {}
 

@@ -21,6 +21,8 @@ def pytest_configure(config):
     _build.build_library()
     from oracle import build as oracle_build
     oracle_build.build()
+    from oracle import build_ref
+    build_ref.build()  # no-op without the reference tree (e.g. on the GPU box)
 
 
 def _cuda_available():
