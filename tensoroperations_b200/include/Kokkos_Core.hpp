@@ -268,15 +268,14 @@ struct MemSpaceOf<P, std::void_t<typename P::memory_space>> {
 
 template <class... Props>
 struct PropsAnalysis {
-  using mem_list = std::tuple<typename MemSpaceOf<Props>::type...>;
   template <class Acc, class... Rest>
   struct first_non_void {
     using type = Acc;
   };
   template <class Acc, class H, class... Rest>
   struct first_non_void<Acc, H, Rest...> {
-    using type = std::conditional_t<std::is_void_v<Acc>, H,
-                                    typename first_non_void<Acc, Rest...>::type>;
+    using type = typename first_non_void<std::conditional_t<std::is_void_v<Acc>, H, Acc>,
+                                         Rest...>::type;
   };
   using named = typename first_non_void<void, typename MemSpaceOf<Props>::type...>::type;
   using memory_space =

@@ -275,9 +275,10 @@ __device__ __forceinline__ void store_root(const View& view, const int* tile_idx
   constexpr auto perm = MT::decl_to_storage;
   using STile = typename MT::tile;
   constexpr auto sstride = tile_strides<STile>();
+  // declared-order tile extents (no local captured: every value is a constant)
   constexpr auto dext = [] {
     std::array<int, R> e{};
-    for (int d = 0; d < R; ++d) e[d] = STile::extents[perm[d]];
+    for (int d = 0; d < R; ++d) e[d] = STile::extents[MT::decl_to_storage[d]];
     return e;
   }();
   using DTile = array_tile_t<dext>;

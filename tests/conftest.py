@@ -1,7 +1,8 @@
 """pytest configuration: the `gpu` marker, repo on sys.path, in-tree builds.
 
-CPU runs (`-m "not gpu"`) need the product library and the oracle built; both
-builds are incremental and take seconds, so they run here if stale.  GPU tests
+CPU runs (`-m "not gpu"`) need the product library and the oracle built; the
+GPU test programs under tests/_bin are compiled for sm_100a here too.  Every
+build is incremental, so it runs only when a source is newer than its output.  GPU tests
 skip cleanly when no device is visible.
 """
 import os
@@ -23,6 +24,15 @@ def pytest_configure(config):
     oracle_build.build()
     from oracle import build_ref
     build_ref.build()  # no-op without the reference tree (e.g. on the GPU box)
+    _cpp_test_build().build()  # sm_100a test programs under tests/_bin (incremental)
+
+
+def _cpp_test_build():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("tests_cpp_build", ROOT / "tests" / "cpp" / "build.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
 
 
 def _cuda_available():

@@ -1,0 +1,75 @@
+"""The LevelGraph frontend on the host (no GPU).
+
+* frontend_static.cpp: the planner's slot algebra, tile derivation, declared
+  order and the SEM3D plan (6 levels, 35 slots, 19 pools) as static_asserts,
+  plus host-side scratch sizing -- compiled by g++ and run.
+* level_guard_negative.cpp: every planner guard fires on the graph it forbids,
+  with its own diagnostic (the wording the reference's negative tests pin,
+  tests/negative/level_guard_negative.cpp and labeltiles_guard_negative.cpp);
+  the control case compiles.
+* level_kernel_host_check.cpp: the device evaluator (LevelKernel.cuh) compiled
+  as host code, one thread per CTA, run on a SEM-shaped graph under
+  AddressSanitizer/UBSan and compared with a direct loop -- every pooled-slot
+  offset, stride and root store stays inside its buffer.
+"""
+import shutil
+import subprocess
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+CPP = ROOT / "tests" / "cpp"
+INC = ["-I", str(ROOT / "include"), "-I", str(ROOT / "tensoroperations_b200" / "include")]
+LIBDIR = ROOT / "tensoroperations_b200"
+GXX = shutil.which("g++")
+
+pytestmark = pytest.mark.skipif(GXX is None, reason="g++ not found")
+
+GUARDS = {
+    1: "a level must be NON-EMPTY and HOMOGENEOUS",
+    2: "must share ONE iteration space",
+    3: "must share ONE iteration space",
+    4: "may not read a slot ITS OWN LEVEL",
+    5: "must share ONE iteration space",
+    6: "may appear at most once in the map",
+    7: "must appear in the graph's tile",
+}
+ALL_MESSAGES = set(GUARDS.values())
+
+
+def _compile(args, timeout=300):
+    return subprocess.run([GXX, "-std=c++20", *INC, *args], capture_output=True, text=True,
+                          timeout=timeout)
+
+
+def test_static_plan_checks(tmp_path):
+    exe = tmp_path / "frontend_static"
+    r = _compile([str(CPP / "frontend_static.cpp"), f"-L{LIBDIR}", "-ltensoroperations_b200",
+                  f"-Wl,-rpath,{LIBDIR}", "-o", str(exe)])
+    assert r.returncode == 0, r.stderr[-3000:]
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 0, run.stdout + run.stderr
+    assert "pools 19" in run.stdout
+
+
+@pytest.mark.parametrize("case", [0, *GUARDS])
+def test_level_guard(case):
+    r = _compile(["-fsyntax-only", f"-DNEG_CASE={case}", str(CPP / "level_guard_negative.cpp")])
+    if case == 0:
+        assert r.returncode == 0, r.stderr[-3000:]
+        return
+    assert r.returncode != 0
+    fired = {m for m in ALL_MESSAGES if m in r.stderr}
+    assert fired == {GUARDS[case]}, (case, fired, r.stderr[-2000:])
+
+
+@pytest.mark.parametrize("elements", [5, 6])
+def test_evaluator_host_emulation_under_sanitizers(tmp_path, elements):
+    exe = tmp_path / "lk_host"
+    r = _compile(["-O1", "-g", "-fsanitize=address,undefined", "-fno-sanitize-recover=all",
+                  str(CPP / "level_kernel_host_check.cpp"), "-o", str(exe)], timeout=600)
+    assert r.returncode == 0, r.stderr[-3000:]
+    run = subprocess.run([str(exe), str(elements)], capture_output=True, text=True, timeout=120)
+    assert run.returncode == 0, run.stdout + run.stderr
+    assert "max abs error" in run.stdout
