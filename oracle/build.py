@@ -31,7 +31,7 @@ def build(force: bool = False):
     for target, flags in ((ORACLE, FLAGS_ORACLE), (CPU, FLAGS_CPU)):
         if force or _stale(target):
             r = subprocess.run(["g++"] + flags + [str(SRC), "-o", str(target)],
-                               capture_output=True, text=True)
+                               capture_output=True, text=True, timeout=600)
             if r.returncode != 0:
                 raise RuntimeError(f"oracle build failed ({target.name}):\n{r.stderr}")
     return ORACLE, CPU

@@ -40,8 +40,8 @@ def available() -> bool:
     return SEM3D.exists()
 
 
-def _run(cmd):
-    r = subprocess.run(cmd, capture_output=True, text=True)
+def _run(cmd, timeout=900):
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout)
     if r.returncode != 0:
         raise RuntimeError("reference build failed: " + " ".join(map(str, cmd)) + "\n" + r.stderr[-4000:])
 
