@@ -37,38 +37,67 @@ struct NoHook {};
 // ---------------------------------------------------------------------------
 // DeviceTuple: a heterogeneous tuple usable in device code.
 // ---------------------------------------------------------------------------
+// Layout note.  Tuples of nodes travel to the device as kernel parameters, so
+// the device pass must place every member at the bytes the host compiler
+// wrote.  With an empty `[[no_unique_address]]` member inside a node, nvcc's
+// device pass placed the members that follow such a node at other offsets
+// than the host compiler (same sizeof; the kernel read a View's extent where
+// the host had written its data pointer).  Every type here is therefore built
+// from plain members only: the tuple by composition (a head and a tail
+// member), nodes without `[[no_unique_address]]`.
 namespace b200 {
-template <std::size_t I, class T>
-struct TupleLeaf {
-  T value;
+template <class... T>
+struct TupleStore {};
+template <class H, class... R>
+struct TupleStore<H, R...> {
+  H head;
+  TupleStore<R...> tail;
 };
-template <class Seq, class... T>
-struct TupleBase;
-template <std::size_t... I, class... T>
-struct TupleBase<std::index_sequence<I...>, T...> : TupleLeaf<I, T>... {
-  TupleBase() = default;
-  template <class... U, class = std::enable_if_t<(sizeof...(U) > 0) && sizeof...(U) == sizeof...(T)>>
-  KOKKOS_INLINE_FUNCTION explicit TupleBase(const U&... v) : TupleLeaf<I, T>{v}... {}
+template <class H>
+struct TupleStore<H> {
+  H head;
 };
+
+template <std::size_t I, class S>
+KOKKOS_INLINE_FUNCTION constexpr const auto& store_get(const S& s) {
+  if constexpr (I == 0)
+    return s.head;
+  else
+    return store_get<I - 1>(s.tail);
+}
+template <std::size_t I, class S>
+KOKKOS_INLINE_FUNCTION constexpr auto& store_get(S& s) {
+  if constexpr (I == 0)
+    return s.head;
+  else
+    return store_get<I - 1>(s.tail);
+}
+template <class H, class... R>
+KOKKOS_INLINE_FUNCTION constexpr TupleStore<H, R...> store_make(const H& h, const R&... r) {
+  if constexpr (sizeof...(R) == 0)
+    return TupleStore<H>{h};
+  else
+    return TupleStore<H, R...>{h, store_make(r...)};
+}
 }  // namespace b200
 
 template <class... T>
-struct DeviceTuple : b200::TupleBase<std::index_sequence_for<T...>, T...> {
-  using base = b200::TupleBase<std::index_sequence_for<T...>, T...>;
+struct DeviceTuple {
   static constexpr std::size_t size = sizeof...(T);
+  b200::TupleStore<T...> store;
+
   DeviceTuple() = default;
   template <class... U, class = std::enable_if_t<sizeof...(U) == sizeof...(T) && (sizeof...(T) > 0)>>
-  KOKKOS_INLINE_FUNCTION explicit DeviceTuple(const U&... v) : base(v...) {}
+  KOKKOS_INLINE_FUNCTION explicit DeviceTuple(const U&... v)
+      : store(b200::store_make<T...>(static_cast<const T&>(v)...)) {}
 
   template <std::size_t I>
   KOKKOS_INLINE_FUNCTION const auto& get() const {
-    using E = std::tuple_element_t<I, std::tuple<T...>>;
-    return static_cast<const b200::TupleLeaf<I, E>&>(*this).value;
+    return b200::store_get<I>(store);
   }
   template <std::size_t I>
   KOKKOS_INLINE_FUNCTION auto& get() {
-    using E = std::tuple_element_t<I, std::tuple<T...>>;
-    return static_cast<b200::TupleLeaf<I, E>&>(*this).value;
+    return b200::store_get<I>(store);
   }
 };
 
@@ -163,7 +192,7 @@ struct NodeHandle<InputTag, T, ModesSeq, HookOp> {
   using modes_seq = ModesSeq;
   static constexpr int Rank = static_cast<int>(ModesSeq::size());
   TensorHandle<T, ModesSeq> handle;
-  [[no_unique_address]] HookOp hook_op;
+  HookOp hook_op;  // a plain member: see the layout note above DeviceTuple
 
   KOKKOS_INLINE_FUNCTION Kokkos::Array<int, Rank> shape() const {
     Kokkos::Array<int, Rank> s{};
@@ -413,7 +442,7 @@ struct NodeHandle<CombineTag, CombineFn, OutSeq, Scalar, ExecSpace,
   static constexpr int Rank = static_cast<int>(OutSeq::size());
   static constexpr int NumOps = static_cast<int>(sizeof...(Ops));
   static constexpr int NumOut = NumOut_;
-  [[no_unique_address]] CombineFn fn;
+  CombineFn fn;  // a plain member: see the layout note above DeviceTuple
   ops_tuple_t operands;
   Kokkos::Array<int, Rank> shape_;
 

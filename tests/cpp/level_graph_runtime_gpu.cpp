@@ -247,8 +247,92 @@ void scenarios_declared_order() {
   }
 }
 
+// Kernel-parameter layout: the device must read every member of a nested
+// DeviceTuple (the form levels, operands and root views travel in) at the
+// same bytes the host wrote.  Each value read on the device is compared with
+// the host's.
+struct Tag3 {
+  int a;
+  double b;
+};
+template <class T>
+__global__ void tuple_layout_kernel(const T t, long long* out) {
+  out[0] = (long long)t.template get<0>().template get<0>().data();
+  out[1] = (long long)t.template get<1>().template get<0>().data();
+  out[2] = (long long)t.template get<1>().template get<0>().extent(3);
+  out[3] = t.template get<2>().template get<0>();
+  out[4] = (long long)t.template get<2>().template get<1>().b;
+  out[5] = (long long)t.template get<2>().template get<2>().data();
+  out[6] = (long long)t.template get<2>().template get<2>().extent(1);
+  out[7] = (long long)sizeof(T);
+}
+
+void kernel_parameter_layout() {
+  V2 a("a", 3, 4), c("c", 5, 6);
+  V4 b("b", 2, 3, 4, 7);
+  using T = DeviceTuple<DeviceTuple<V2>, DeviceTuple<V4>, DeviceTuple<int, Tag3, V2>>;
+  const T t(DeviceTuple<V2>(a), DeviceTuple<V4>(b), DeviceTuple<int, Tag3, V2>(11, Tag3{1, 42.0}, c));
+  long long* d = nullptr;
+  cudaMalloc(&d, 8 * sizeof(long long));
+  cudaMemset(d, 0, 8 * sizeof(long long));
+  tuple_layout_kernel<T><<<1, 1>>>(t, d);
+  long long got[8] = {};
+  cudaMemcpy(got, d, sizeof(got), cudaMemcpyDeviceToHost);
+  cudaFree(d);
+  const long long want[8] = {(long long)a.data(), (long long)b.data(), 7, 11, 42,
+                             (long long)c.data(), 6, (long long)sizeof(T)};
+  int bad = 0;
+  for (int i = 0; i < 8; ++i) bad += got[i] != want[i];
+  report("kernel parameter layout (nested DeviceTuple)", bad, 0.5);
+}
+
+// The same check on a real level tuple (stage, contraction and combine
+// members): the device reads the staged View and the members' shapes.
+template <class Lv>
+__global__ void level_layout_kernel(const Lv levels, long long* out) {
+  const auto& u = levels.template get<1>().template get<0>().operand_.handle.tensor;
+  out[0] = (long long)levels.template get<0>().template get<0>().operand_.handle.tensor.data();
+  out[1] = (long long)u.data();
+  out[2] = (long long)u.extent(0);
+  out[3] = levels.template get<2>().template get<0>().shape()[1];
+  out[4] = levels.template get<3>().template get<0>().shape()[1];
+  out[5] = (long long)sizeof(Lv);
+}
+
+void level_tuple_layout() {
+  constexpr int N = 5, E = 9;
+  using Map = LabelTiles<LabelWhole<'q', N>, LabelWhole<'a', N>, LabelTile<'e', 2>,
+                         LabelWhole<'b', N>, LabelWhole<'c', N>>;
+  V2 H("H", N, N);
+  V4 U("U", E, N, N, N);
+  auto g0 = make_level_graph<float, ES>(Map{});
+  auto [g1, h] = g0.add(make_stage_node(make_input_node(make_handle<'q', 'a'>(H))));
+  auto [g2, u] = g1.add(make_stage_node(make_input_node(make_handle<'e', 'a', 'b', 'c'>(U))));
+  auto [g3, ca] = g2.add(make_contraction_node<'q', 'e', 'b', 'c'>(h, u));
+  auto [g4, pa] = g3.add(make_combine_node<'q', 'e', 'b', 'c'>(ca, Scale{}));
+  using Lv = typename decltype(g4)::levels_type;
+  long long* d = nullptr;
+  cudaMalloc(&d, 6 * sizeof(long long));
+  cudaMemset(d, 0, 6 * sizeof(long long));
+  level_layout_kernel<Lv><<<1, 1>>>(g4.levels, d);
+  long long got[6] = {};
+  cudaMemcpy(got, d, sizeof(got), cudaMemcpyDeviceToHost);
+  cudaFree(d);
+  const long long want[6] = {(long long)H.data(), (long long)U.data(), E, E, E, (long long)sizeof(Lv)};
+  int bad = 0;
+  for (int i = 0; i < 6; ++i) bad += got[i] != want[i];
+  report("kernel parameter layout (level tuple)", bad, 0.5);
+}
+
 int main(int argc, char* argv[]) {
   Kokkos::initialize(argc, argv);
+  kernel_parameter_layout();
+  level_tuple_layout();
+  if (g_fail) {  // operands would be read from the wrong bytes: run nothing else
+    Kokkos::finalize();
+    std::printf("level graph runtime: FAIL (kernel parameter layout)\n");
+    return 1;
+  }
   scenarios_same_extents<2>();
   scenarios_same_extents<3>();  // 8 elements in tiles of 3: a partial last tile
   scenarios_declared_order<2>();
