@@ -45,6 +45,10 @@ METRIC = ("SEM stiffness Melem/s and HBM GB/s (% of ~8 TB/s) at 1/2/4/8 B200 vs 
 MESH_PER_GPU = (64, 64, 64)
 NGLL = 5
 FALLBACK_HBM_GBS = 6650.0
+# DRAM bytes (read + write) per launch of the kernel, from one ncu capture of the
+# 32^3 case scaled by elements to the 64^3 launch
+# (profiles/sem3d_elastic_v3_32cube_full.md); None where not captured.
+NCU_TRAFFIC_PER_LAUNCH = {"0": 276.76e6 * 8}
 KERNEL_NAMES = {"0": "sem3d_elastic_v3_kernel<5,8,2,true>",
                 "1": "sem3d_elastic_tma_kernel<float,5,8,2,true>",
                 "2": "sem3d_elastic_kernel<float,5,32,true>",
@@ -360,7 +364,11 @@ def main():
             "data": "synthetic (seeded splitmix64 fields on a structured mesh, GLL operators)",
             "config": config_dict(prob, world),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None, "peak_source": peak_src,
+                         "frac": achieved / peak,
+                         "traffic": (NCU_TRAFFIC_PER_LAUNCH.get(os.environ.get("TO_SEM3D_VARIANT", "0"))
+                                     if tuple(MESH_PER_GPU) == (64, 64, 64) else None),
+                         "traffic_source": "ncu dram__bytes_read+write of the 32^3 case x8",
+                         "peak_source": peak_src,
                          "algorithmic_bytes_per_launch": alg, "kernel_ms": kern_ms,
                          "kernel": KERNEL_NAMES.get(os.environ.get("TO_SEM3D_VARIANT", "0"))},
             "cpu_baseline": cpu,
