@@ -10,8 +10,10 @@ application f = K u: zero f, then the fused kernel.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
 For N > 1 (torchrun, one rank per GPU) the mesh is 64x64x(64N) hexes split in
-z-slabs, one per rank (weak scaling); each rank applies its slab and the
-interface node planes are summed with the neighbours over NCCL.
+z-slabs, one per rank (weak scaling); each rank scatters the element layers
+next to its neighbours first, then exchanges and sums the shared node planes
+over NCCL on a second stream while its interior layers compute
+(tensoroperations_b200/slab.py).
 
 Prints ONE JSON line on rank 0.  `value` is whole-job elements/s (Melem/s),
 timed with CUDA events on the launching stream over exactly K steps between
@@ -156,12 +158,13 @@ def cpu_baseline(prob, seconds: float = 12.0, max_reps: int = 50):
 
 
 def make_problem(rank: int, world: int):
-    from tensoroperations_b200.sem3d import structured_problem
+    """This rank's z-slab of the nex x ney x (world*nez) mesh: element layers
+    [rank*nez, (rank+1)*nez), generated as the exact slice of the whole
+    synthetic problem."""
+    from tensoroperations_b200.slab import SlabPartition, slab_problem
     nex, ney, nez = MESH_PER_GPU
-    # the slab of rank r is the z-range [r*nez, (r+1)*nez) of a nex x ney x (world*nez) mesh;
-    # seeds are offset per rank so slabs hold different synthetic data.
-    return structured_problem(nex, ney, nez, ngll=NGLL, dtype=np.float32, assembled=True,
-                              seed=0x5EED2026 + 1000 * rank)
+    part = SlabPartition(nex, ney, nez * world, NGLL, world, rank)
+    return part, slab_problem(part, np.float32)
 
 
 def run_reference(args):
@@ -267,25 +270,17 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
-    prob = make_problem(rank, world)
+    from tensoroperations_b200.slab import SlabOperator
+    part, prob = make_problem(rank, world)
     u, f, arrays, ibool = to_device(prob, dev)
     plan = prob.plan()
     stream = torch.cuda.Stream(device=dev)
-    s = stream.cuda_stream
     fields = plan.fields(u, f, arrays, ibool)
+    op = SlabOperator(part, plan, fields, f, dev)
 
-    def step():
-        for c in range(3):
-            f[c].zero_()
-        ev_k0.record(stream)
-        plan.apply(fields, accumulate=True, stream=s)
-        ev_k1.record(stream)
-
-    ev_k0 = torch.cuda.Event(enable_timing=True)
-    ev_k1 = torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         for _ in range(max(args.warmup, 3)):
-            step()
+            op.apply(stream)
     torch.cuda.synchronize()
 
     # ---- timed region: K steps, CUDA events on the launching stream ----
@@ -300,11 +295,7 @@ def main():
         with torch.cuda.stream(stream):
             e_start.record(stream)
             for it in range(args.steps):
-                for c in range(3):
-                    f[c].zero_()
-                kstarts[it].record(stream)
-                plan.apply(fields, accumulate=True, stream=s)
-                kends[it].record(stream)
+                op.apply(stream, (kstarts[it], kends[it]))
             e_end.record(stream)
         torch.cuda.synchronize()
     if world > 1:
@@ -325,10 +316,12 @@ def main():
     u_dev = [torch.empty_like(x) for x in u]
     fields_e2e = plan.fields(u_dev, f, arrays, ibool)
 
+    op_e2e = SlabOperator(part, plan, fields_e2e, f, dev)
+
     def e2e_step():
         for c in range(3):
             u_dev[c].copy_(u_host[c], non_blocking=True)
-        plan.apply(fields_e2e, accumulate=False, stream=s)
+        op_e2e.apply(stream)
         for c in range(3):
             f_host[c].copy_(f[c], non_blocking=True)
 
@@ -376,7 +369,7 @@ def main():
                    {"value": prob.nelem * world / (e2e_ms * 1e-3) / 1e6, "unit": "Melem/s",
                     "h2d_bytes_per_step": bytes_uf, "d2h_bytes_per_step": bytes_uf,
                     "steps": e2e_steps},
-            "gpu_launches": args.steps,
+            "gpu_launches": args.steps * op.kernel_launches(),
             "clocks": clocks.summary(),
             "gflops": plan.flops() / (kern_ms * 1e-3) / 1e9,
         }

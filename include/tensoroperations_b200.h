@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define TO_ABI_VERSION 1
+#define TO_ABI_VERSION 2
 
 typedef enum to_status {
   TO_OK = 0,
@@ -95,6 +95,12 @@ int to_gll_operators(int32_t ngll, double* nodes, double* weights,
 int to_synth_fill(void* dst, int32_t dtype, int64_t n, uint64_t seed,
                   int32_t dist, double a, double b);
 
+/* The slice [first, first + n) of the same sequence: dst[i] is element
+ * first + i of to_synth_fill's output (how a z-slab rank generates exactly its
+ * part of a global problem). */
+int to_synth_fill_at(void* dst, int32_t dtype, int64_t first, int64_t n, uint64_t seed,
+                     int32_t dist, double a, double b);
+
 /* ---------------------------------------------------------------------- */
 /* SEM 3D isotropic-elastic stiffness operator                             */
 /* ---------------------------------------------------------------------- */
@@ -154,6 +160,16 @@ int to_sem3d_plan_destroy(to_sem3d_plan* plan);
 int to_sem3d_apply(const to_sem3d_plan* plan, const to_sem3d_fields* fields,
                    int32_t accumulate, void* stream);
 
+/* The contribution of elements [first, first + count) of the plan only,
+ * ADDED to f (never zeroed): `fields` describes the whole batch exactly as for
+ * to_sem3d_apply.  Lets a caller order element ranges -- a z-slab rank
+ * computes the element layers next to its neighbours first, starts the
+ * interface exchange, then computes the interior.  The reference launches
+ * its whole league at once (include/TensorOperations/LevelGraph.hpp:576-628);
+ * this is the same operator on a sub-range. */
+int to_sem3d_apply_elements(const to_sem3d_plan* plan, const to_sem3d_fields* fields,
+                            int64_t first, int64_t count, void* stream);
+
 /* Algorithmic HBM bytes of one application of `plan` (the roofline numerator:
  * every per-point array read once, ibool read once, u read and f written once
  * per global node in assembled mode, per point in element-local mode). */
@@ -161,6 +177,27 @@ double to_sem3d_algorithmic_bytes(const to_sem3d_plan* plan);
 
 /* Useful floating-point operations of one application (36N+159 per point). */
 double to_sem3d_flops(const to_sem3d_plan* plan);
+
+/* ---------------------------------------------------------------------- */
+/* Z-slab interface planes (multi-GPU assembled mode)                      */
+/* ---------------------------------------------------------------------- */
+/*
+ * A rank of a z-slab partition owns a contiguous range of element layers
+ * and every node plane they touch; its first and last planes are shared with
+ * the neighbouring ranks and hold partial sums after the rank's own scatter.
+ * With the structured numbering a node plane is one contiguous range
+ * [offset, offset + n) of each component (n = nx*ny).
+ *   pack:        buf[c*n + i]      = f[c][offset + i]      (c = 0..2)
+ *   accumulate:  f[c][offset + i] += buf[c*n + i]
+ * `f` is a HOST array of 3 device pointers; `buf` is device memory of 3*n
+ * values.  Both launch one kernel on `stream`.  The reference is single-GPU;
+ * these are the two local steps around the neighbour exchange (NCCL
+ * send/recv of `buf`).
+ */
+int to_sem3d_halo_pack(int32_t dtype, void* const f[3], int64_t offset, int64_t n,
+                       void* buf, void* stream);
+int to_sem3d_halo_accumulate(int32_t dtype, void* const f[3], int64_t offset, int64_t n,
+                             const void* buf, void* stream);
 
 /* ---------------------------------------------------------------------- */
 /* Level-graph lowering                                                    */

@@ -82,6 +82,14 @@ _sig("to_mesh_structured_ibool", C.c_int, [C.c_int32] * 4 + [C.c_void_p])
 _sig("to_gll_operators", C.c_int, [C.c_int32] + [C.c_void_p] * 4)
 _sig("to_synth_fill", C.c_int, [C.c_void_p, C.c_int32, C.c_int64, C.c_uint64, C.c_int32,
                                 C.c_double, C.c_double])
+_sig("to_synth_fill_at", C.c_int, [C.c_void_p, C.c_int32, C.c_int64, C.c_int64, C.c_uint64,
+                                   C.c_int32, C.c_double, C.c_double])
+_sig("to_sem3d_apply_elements", C.c_int, [C.c_void_p, C.POINTER(Sem3dFields), C.c_int64,
+                                          C.c_int64, C.c_void_p])
+_sig("to_sem3d_halo_pack", C.c_int, [C.c_int32, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p,
+                                     C.c_void_p])
+_sig("to_sem3d_halo_accumulate", C.c_int, [C.c_int32, C.c_void_p, C.c_int64, C.c_int64,
+                                           C.c_void_p, C.c_void_p])
 _sig("to_sem3d_plan_create", C.c_int, [C.POINTER(Sem3dDesc), C.POINTER(C.c_void_p)])
 _sig("to_sem3d_plan_destroy", C.c_int, [C.c_void_p])
 _sig("to_sem3d_apply", C.c_int, [C.c_void_p, C.POINTER(Sem3dFields), C.c_int32, C.c_void_p])
@@ -132,14 +140,35 @@ def structured_ibool(nex: int, ney: int, nez: int, ngll: int) -> np.ndarray:
     return out
 
 
-def synth_fill(n: int, dtype, seed: int, dist: str, a: float, b: float) -> np.ndarray:
-    """Seeded fill: dist 'uniform' -> U[a,b), 'normal' -> N(a, b^2)."""
+def synth_fill(n: int, dtype, seed: int, dist: str, a: float, b: float,
+               first: int = 0) -> np.ndarray:
+    """Seeded fill: dist 'uniform' -> U[a,b), 'normal' -> N(a, b^2); elements
+    [first, first + n) of the sequence."""
     dt = np.dtype(dtype)
     code = TO_F32 if dt == np.float32 else TO_F64
     out = np.empty(n, dtype=dt)
-    check(lib.to_synth_fill(_ptr(out), code, n, seed, {"uniform": 0, "normal": 1}[dist], a, b),
-          "to_synth_fill")
+    check(lib.to_synth_fill_at(_ptr(out), code, first, n, seed,
+                               {"uniform": 0, "normal": 1}[dist], a, b), "to_synth_fill_at")
     return out
+
+
+def _fptrs(f):
+    arr = (C.c_void_p * 3)(*[_ptr(x) for x in f])
+    return arr
+
+
+def halo_pack(dtype, f, offset: int, n: int, buf, stream: int = 0):
+    """buf[c*n + i] = f[c][offset + i] on the device (one kernel)."""
+    code = TO_F32 if np.dtype(dtype) == np.float32 else TO_F64
+    check(lib.to_sem3d_halo_pack(code, _fptrs(f), offset, n, _ptr(buf), stream),
+          "to_sem3d_halo_pack")
+
+
+def halo_accumulate(dtype, f, offset: int, n: int, buf, stream: int = 0):
+    """f[c][offset + i] += buf[c*n + i] on the device (one kernel)."""
+    code = TO_F32 if np.dtype(dtype) == np.float32 else TO_F64
+    check(lib.to_sem3d_halo_accumulate(code, _fptrs(f), offset, n, _ptr(buf), stream),
+          "to_sem3d_halo_accumulate")
 
 
 def sm_count() -> int:
@@ -194,6 +223,11 @@ class Sem3dPlan:
     def apply(self, fields: Sem3dFields, accumulate: bool = False, stream: int = 0):
         check(lib.to_sem3d_apply(self._h, C.byref(fields), 1 if accumulate else 0, stream),
               "to_sem3d_apply")
+
+    def apply_elements(self, fields: Sem3dFields, first: int, count: int, stream: int = 0):
+        """Add the contribution of elements [first, first + count) to f."""
+        check(lib.to_sem3d_apply_elements(self._h, C.byref(fields), first, count, stream),
+              "to_sem3d_apply_elements")
 
     def algorithmic_bytes(self) -> float:
         return lib.to_sem3d_algorithmic_bytes(self._h)

@@ -169,31 +169,38 @@ int to_gll_operators(int32_t ngll, double* nodes, double* weights, double* hprim
   return ok();
 }
 
-int to_synth_fill(void* dst, int32_t dtype, int64_t n, uint64_t seed, int32_t dist,
-                  double a, double b) {
-  if (!dst || n < 0 || (dtype != TO_F32 && dtype != TO_F64) || (dist != 0 && dist != 1))
-    return set_error(TO_ERR_INVALID_ARGUMENT, "to_synth_fill: bad argument");
+int to_synth_fill_at(void* dst, int32_t dtype, int64_t first, int64_t n, uint64_t seed,
+                     int32_t dist, double a, double b) {
+  if (!dst || n < 0 || first < 0 || (dtype != TO_F32 && dtype != TO_F64) ||
+      (dist != 0 && dist != 1))
+    return set_error(TO_ERR_INVALID_ARGUMENT, "to_synth_fill_at: bad argument");
   const double inv53 = 1.0 / 9007199254740992.0;  // 2^-53
   float* df = static_cast<float*>(dst);
   double* dd = static_cast<double*>(dst);
 #pragma omp parallel for schedule(static)
-  for (int64_t m = 0; m < n; ++m) {
+  for (int64_t i = 0; i < n; ++i) {
+    const uint64_t m = static_cast<uint64_t>(first + i);
     double v;
     if (dist == 0) {
-      const double u = static_cast<double>(splitmix64_at(seed, static_cast<uint64_t>(m)) >> 11) * inv53;
+      const double u = static_cast<double>(splitmix64_at(seed, m) >> 11) * inv53;
       v = a + (b - a) * u;
     } else {
-      const uint64_t m2 = 2 * static_cast<uint64_t>(m);
+      const uint64_t m2 = 2 * m;
       const double u1 = (static_cast<double>(splitmix64_at(seed, m2) >> 11) + 1.0) * inv53;
       const double u2 = static_cast<double>(splitmix64_at(seed, m2 + 1) >> 11) * inv53;
       v = a + b * std::sqrt(-2.0 * std::log(u1)) * std::cos(2.0 * M_PI * u2);
     }
     if (dtype == TO_F32)
-      df[m] = static_cast<float>(v);
+      df[i] = static_cast<float>(v);
     else
-      dd[m] = v;
+      dd[i] = v;
   }
   return ok();
+}
+
+int to_synth_fill(void* dst, int32_t dtype, int64_t n, uint64_t seed, int32_t dist,
+                  double a, double b) {
+  return to_synth_fill_at(dst, dtype, 0, n, seed, dist, a, b);
 }
 
 }  // extern "C"

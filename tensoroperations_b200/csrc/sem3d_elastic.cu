@@ -292,6 +292,47 @@ int to_sem3d_apply(const to_sem3d_plan* plan, const to_sem3d_fields* fields,
                    d.dtype);
 }
 
+int to_sem3d_apply_elements(const to_sem3d_plan* plan, const to_sem3d_fields* fields,
+                            int64_t first, int64_t count, void* stream) {
+  if (!plan || !fields) return set_error(TO_ERR_INVALID_ARGUMENT, "to_sem3d_apply_elements: null");
+  const to_sem3d_desc& d = plan->desc;
+  if (first < 0 || count < 0 || first > d.nelem || count > d.nelem - first)
+    return set_error(TO_ERR_INVALID_ARGUMENT,
+                     "to_sem3d_apply_elements: range [%lld, %lld) outside [0, %lld)",
+                     static_cast<long long>(first), static_cast<long long>(first + count),
+                     static_cast<long long>(d.nelem));
+  if (count == 0) return ok();
+  // The same operator on the sub-batch: every per-element array (and, in
+  // element-local mode, u and f) starts `first` elements in; assembled u and f
+  // stay global.  The sub-plan never zeroes f.
+  to_sem3d_plan sub = *plan;
+  sub.desc.nelem = count;
+  to_sem3d_fields fl = *fields;
+  const size_t P = static_cast<size_t>(d.ngll) * d.ngll * d.ngll;
+  const size_t vb = d.dtype == TO_F64 ? 8 : 4;
+  const size_t off = static_cast<size_t>(first) * P;
+  auto shift = [&](const void* p, size_t bytes) -> const void* {
+    return p ? static_cast<const char*>(p) + off * bytes : p;
+  };
+  fl.xix = shift(fl.xix, vb);   fl.xiy = shift(fl.xiy, vb);   fl.xiz = shift(fl.xiz, vb);
+  fl.etax = shift(fl.etax, vb); fl.etay = shift(fl.etay, vb); fl.etaz = shift(fl.etaz, vb);
+  fl.gamx = shift(fl.gamx, vb); fl.gamy = shift(fl.gamy, vb); fl.gamz = shift(fl.gamz, vb);
+  fl.jac = shift(fl.jac, vb);   fl.l2m = shift(fl.l2m, vb);   fl.mu = shift(fl.mu, vb);
+  if (d.assembled) {
+    fl.ibool = static_cast<const int32_t*>(shift(fl.ibool, 4));
+  } else {
+    for (int c = 0; c < 3; ++c) {
+      fl.u[c] = shift(fl.u[c], vb);
+      fl.f[c] = const_cast<void*>(shift(fl.f[c], vb));
+    }
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (d.ngll == 5 && d.dtype == TO_F32) return apply_typed<float, 5>(&sub, &fl, 1, s);
+  if (d.ngll == 5 && d.dtype == TO_F64) return apply_typed<double, 5>(&sub, &fl, 1, s);
+  return set_error(TO_ERR_UNSUPPORTED, "to_sem3d_apply_elements: ngll %d dtype %d not built",
+                   d.ngll, d.dtype);
+}
+
 int to_device_status(int32_t reset) {
   int v = 0;
   TO_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_to_device_status, sizeof(int)));

@@ -54,17 +54,18 @@ class Sem3dProblem:
                              nglob=self.nglob, assembled=self.assembled)
 
 
-def point_arrays(npts: int, dtype, seed: int = DEFAULT_SEED) -> dict:
+def point_arrays(npts: int, dtype, seed: int = DEFAULT_SEED, first: int = 0) -> dict:
+    """The per-point arrays of points [first, first + npts) of a problem."""
     dt = np.dtype(dtype)
     out = {}
     for r, name in enumerate(abi.POINT_ARRAYS[:9]):
-        a = abi.synth_fill(npts, np.float64, seed + 3 + r, "uniform", 0.5, 1.5)
+        a = abi.synth_fill(npts, np.float64, seed + 3 + r, "uniform", 0.5, 1.5, first=first)
         if name in ("xix", "etay", "gamz"):
             a += 1.0
         out[name] = a.astype(dt)
-    out["jac"] = abi.synth_fill(npts, dt, seed + 12, "uniform", 0.5, 2.0)
-    lam = abi.synth_fill(npts, dt, seed + 13, "uniform", 1.0, 3.0)
-    mu = abi.synth_fill(npts, dt, seed + 14, "uniform", 0.5, 2.0)
+    out["jac"] = abi.synth_fill(npts, dt, seed + 12, "uniform", 0.5, 2.0, first=first)
+    lam = abi.synth_fill(npts, dt, seed + 13, "uniform", 1.0, 3.0, first=first)
+    mu = abi.synth_fill(npts, dt, seed + 14, "uniform", 0.5, 2.0, first=first)
     out["l2m"] = (lam + dt.type(2) * mu).astype(dt)
     out["mu"] = mu
     return out

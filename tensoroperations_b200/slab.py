@@ -1,0 +1,215 @@
+"""Z-slab partition of the structured SEM 3D operator over ranks (one per GPU).
+
+Element e = (ez*ney + ey)*nex + ex, so a range of element layers [z0, z1) is a
+contiguous range of elements, and with the structured numbering the node
+planes it touches, [z0*(N-1), z1*(N-1)], are a contiguous range of global
+nodes.  Rank r owns layers [z0, z1) and all of their node planes; the first
+and last planes are duplicated on the neighbours (r-1 and r+1).
+
+One application on a rank (`SlabOperator.apply`):
+  1. zero f; scatter the element layers next to a neighbour (compute stream);
+  2. on a second stream: pack the shared planes, exchange them with the
+     neighbours (NCCL send/recv through torch.distributed), add the
+     neighbour's partial sums in;
+  3. meanwhile scatter the interior layers on the compute stream -- they touch
+     no shared plane, so 2 and 3 overlap;
+  4. the compute stream waits for 2.
+Afterwards every copy of a shared node holds the full sum: f on each rank
+equals the slice of the single-mesh result for its nodes.
+
+Each rank generates exactly its slice of the global synthetic problem
+(`slab_problem`), so a multi-rank result can be checked against one
+whole-mesh computation.  The reference is single-GPU; this partition is this
+build's own.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import abi
+from .sem3d import DEFAULT_SEED, Sem3dProblem, point_arrays
+
+
+@dataclass(frozen=True)
+class SlabPartition:
+    nex: int
+    ney: int
+    nez: int  # layers of the GLOBAL mesh
+    ngll: int
+    world: int
+    rank: int
+
+    def __post_init__(self):
+        if not (0 <= self.rank < self.world):
+            raise ValueError(f"rank {self.rank} outside world {self.world}")
+        if self.nez < self.world:
+            raise ValueError(f"{self.nez} element layers cannot give {self.world} ranks one each")
+
+    # ---- element layers ------------------------------------------------------
+    @property
+    def z0(self) -> int:
+        base, extra = divmod(self.nez, self.world)
+        return self.rank * base + min(self.rank, extra)
+
+    @property
+    def z1(self) -> int:
+        base, extra = divmod(self.nez, self.world)
+        return self.z0 + base + (1 if self.rank < extra else 0)
+
+    @property
+    def nez_local(self) -> int:
+        return self.z1 - self.z0
+
+    @property
+    def layer(self) -> int:
+        return self.nex * self.ney
+
+    @property
+    def nelem(self) -> int:
+        return self.nez_local * self.layer
+
+    @property
+    def elem_first(self) -> int:
+        return self.z0 * self.layer
+
+    # ---- nodes -------------------------------------------------------------------
+    @property
+    def plane(self) -> int:
+        n1 = self.ngll - 1
+        return (self.nex * n1 + 1) * (self.ney * n1 + 1)
+
+    @property
+    def nglob(self) -> int:
+        return self.plane * (self.nez_local * (self.ngll - 1) + 1)
+
+    @property
+    def node_first(self) -> int:
+        return self.z0 * (self.ngll - 1) * self.plane
+
+    @property
+    def nglob_global(self) -> int:
+        return self.plane * (self.nez * (self.ngll - 1) + 1)
+
+    # ---- neighbours ------------------------------------------------------------
+    def interfaces(self):
+        """[(neighbour rank, offset of the shared plane in this rank's nodes)]"""
+        out = []
+        if self.rank > 0:
+            out.append((self.rank - 1, 0))
+        if self.rank < self.world - 1:
+            out.append((self.rank + 1, self.nglob - self.plane))
+        return out
+
+    def element_ranges(self):
+        """(boundary ranges, interior range) as (first, count) in local elements.
+
+        Boundary = the layers that touch a shared plane; interior = the rest
+        (one contiguous range, possibly empty)."""
+        lo = self.rank > 0
+        hi = self.rank < self.world - 1
+        bnd = []
+        if lo:
+            bnd.append((0, self.layer))
+        if hi and not (lo and self.nez_local == 1):
+            bnd.append((self.nelem - self.layer, self.layer))
+        b0 = self.layer if lo else 0
+        e0 = self.nelem - self.layer if hi else self.nelem
+        interior = (b0, max(0, e0 - b0))
+        return bnd, interior
+
+
+def slab_problem(part: SlabPartition, dtype=np.float32, seed: int = DEFAULT_SEED) -> Sem3dProblem:
+    """This rank's slice of structured_problem(nex, ney, nez, ...) (same seeds)."""
+    dt = np.dtype(dtype)
+    N = part.ngll
+    P = N ** 3
+    _, w, H, Hw = abi.gll_operators(N)
+    arrays = point_arrays(part.nelem * P, dt, seed, first=part.elem_first * P)
+    ibool = abi.structured_ibool(part.nex, part.ney, part.nez_local, N).reshape(-1)
+    u = [abi.synth_fill(part.nglob, dt, seed + c, "normal", 0.0, 1.0, first=part.node_first)
+         for c in range(3)]
+    return Sem3dProblem(N, part.nelem, dt, H, Hw, w, arrays, u, ibool, part.nglob,
+                        (part.nex, part.ney, part.nez_local))
+
+
+def exchange_planes(part: SlabPartition, sends, recvs, group=None):
+    """Send sends[i] to and receive recvs[i] from neighbour i of part.interfaces().
+
+    One batched group of point-to-point operations (NCCL: one group, so the
+    chain of neighbours cannot deadlock); tensors live where the process
+    group's backend expects them (CUDA for NCCL, CPU for gloo).  Returns after
+    the operations are enqueued and waited on (NCCL: the current stream waits;
+    gloo: the host waits)."""
+    import torch.distributed as dist
+    ops = []
+    for (peer, _), s, r in zip(part.interfaces(), sends, recvs):
+        ops.append(dist.P2POp(dist.isend, s, peer, group))
+        ops.append(dist.P2POp(dist.irecv, r, peer, group))
+    if not ops:
+        return
+    for w in dist.batch_isend_irecv(ops):
+        w.wait()
+
+
+class SlabOperator:
+    """f = K u on this rank's slab, interface planes summed with the neighbours.
+
+    `plan` is a Sem3dPlan over the rank's elements (assembled); `u`, `f`, the
+    per-point arrays and ibool are this rank's device tensors.  Exchange
+    buffers are allocated once here; apply() allocates nothing."""
+
+    def __init__(self, part: SlabPartition, plan, fields, f, device, group=None):
+        import torch
+        self.part = part
+        self.plan = plan
+        self.fields = fields
+        self.f = f
+        self.group = group
+        self.dtype = np.dtype(plan.dtype)
+        tdt = torch.float32 if self.dtype == np.float32 else torch.float64
+        n = 3 * part.plane
+        k = len(part.interfaces())
+        self.send = [torch.empty(n, dtype=tdt, device=device) for _ in range(k)]
+        self.recv = [torch.empty(n, dtype=tdt, device=device) for _ in range(k)]
+        self.comm = torch.cuda.Stream(device=device)
+        self.ev_bnd = torch.cuda.Event()
+        self.ev_done = torch.cuda.Event()
+        self.boundary, self.interior = part.element_ranges()
+
+    def kernel_launches(self) -> int:
+        """Launches of this library's kernels per apply (fills excluded)."""
+        k = len(self.part.interfaces())
+        return len(self.boundary) + (1 if self.interior[1] else 0) + 2 * k
+
+    def apply(self, stream, events=None):
+        """One application on `stream`; `events` = (start, end) CUDA events are
+        recorded on it around this rank's operator kernels (fills excluded)."""
+        import torch
+        s = stream.cuda_stream
+        for x in self.f:
+            x.zero_()
+        if events is not None:
+            events[0].record(stream)
+        for first, count in self.boundary:
+            self.plan.apply_elements(self.fields, first, count, s)
+        faces = self.part.interfaces()
+        if faces:
+            self.ev_bnd.record(stream)
+            self.comm.wait_event(self.ev_bnd)
+            cs = self.comm.cuda_stream
+            with torch.cuda.stream(self.comm):
+                for (_, off), buf in zip(faces, self.send):
+                    abi.halo_pack(self.dtype, self.f, off, self.part.plane, buf, cs)
+                exchange_planes(self.part, self.send, self.recv, self.group)
+                for (_, off), buf in zip(faces, self.recv):
+                    abi.halo_accumulate(self.dtype, self.f, off, self.part.plane, buf, cs)
+            self.ev_done.record(self.comm)
+        first, count = self.interior
+        if count:
+            self.plan.apply_elements(self.fields, first, count, s)
+        if faces:
+            stream.wait_event(self.ev_done)
+        if events is not None:
+            events[1].record(stream)
