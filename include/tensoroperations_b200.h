@@ -127,7 +127,7 @@ int to_synth_fill_at(void* dst, int32_t dtype, int64_t first, int64_t n, uint64_
  */
 typedef struct to_sem3d_desc {
   int32_t dtype;            /* TO_F32 or TO_F64                              */
-  int32_t ngll;             /* N: 5 (f32, f64) or 8 (f32, f64)               */
+  int32_t ngll;             /* N: 5 or 8 (f32 and f64 each)                  */
   int64_t nelem;            /* E                                              */
   int64_t nglob;            /* assembled: number of global nodes; else 0     */
   int32_t assembled;        /* 1 = through ibool, 0 = element-local          */
@@ -198,6 +198,31 @@ int to_sem3d_halo_pack(int32_t dtype, void* const f[3], int64_t offset, int64_t 
                        void* buf, void* stream);
 int to_sem3d_halo_accumulate(int32_t dtype, void* const f[3], int64_t offset, int64_t n,
                              const void* buf, void* stream);
+
+/* ---------------------------------------------------------------------- */
+/* Field reductions (repeated applications u <- K u / ||K u||)             */
+/* ---------------------------------------------------------------------- */
+/*
+ * Sum of squares of three device arrays over [first, first + n):
+ *   *result = sum_c sum_i x[c][first + i]^2        (accumulated in double)
+ * `x` is a HOST array of 3 device pointers, `result` one device double.  Two
+ * kernels on `stream`; the grouping of the sum is fixed by n alone (blocks of
+ * 131072 values, then a fixed-order pass over the block partials), so the
+ * result is bitwise the same on every device.  `workspace` is device memory
+ * of at least to_sumsq3_workspace_bytes(n) bytes holding the block partials;
+ * nothing in it needs to be initialised.  For a z-slab rank, [first, first+n)
+ * is the nodes it owns: a shared interface plane is counted by the lower rank
+ * only.  The reference's benchmark has no norm; this is the configuration's
+ * steady-state loop.
+ */
+size_t to_sumsq3_workspace_bytes(int64_t n);
+int to_sumsq3(int32_t dtype, const void* const x[3], int64_t first, int64_t n, double* result,
+              void* workspace, size_t workspace_bytes, void* stream);
+
+/* y[c][i] = x[c][i] / sqrt(*sumsq) for i < n (sumsq read on the device, so no
+ * host synchronisation); y may equal x. */
+int to_scale3(int32_t dtype, void* const y[3], const void* const x[3], int64_t n,
+              const double* sumsq, void* stream);
 
 /* ---------------------------------------------------------------------- */
 /* Level-graph lowering                                                    */

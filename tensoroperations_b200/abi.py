@@ -90,6 +90,10 @@ _sig("to_sem3d_halo_pack", C.c_int, [C.c_int32, C.c_void_p, C.c_int64, C.c_int64
                                      C.c_void_p])
 _sig("to_sem3d_halo_accumulate", C.c_int, [C.c_int32, C.c_void_p, C.c_int64, C.c_int64,
                                            C.c_void_p, C.c_void_p])
+_sig("to_sumsq3_workspace_bytes", C.c_size_t, [C.c_int64])
+_sig("to_sumsq3", C.c_int, [C.c_int32, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p,
+                            C.c_size_t, C.c_void_p])
+_sig("to_scale3", C.c_int, [C.c_int32, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p])
 _sig("to_sem3d_plan_create", C.c_int, [C.POINTER(Sem3dDesc), C.POINTER(C.c_void_p)])
 _sig("to_sem3d_plan_destroy", C.c_int, [C.c_void_p])
 _sig("to_sem3d_apply", C.c_int, [C.c_void_p, C.POINTER(Sem3dFields), C.c_int32, C.c_void_p])
@@ -169,6 +173,27 @@ def halo_accumulate(dtype, f, offset: int, n: int, buf, stream: int = 0):
     code = TO_F32 if np.dtype(dtype) == np.float32 else TO_F64
     check(lib.to_sem3d_halo_accumulate(code, _fptrs(f), offset, n, _ptr(buf), stream),
           "to_sem3d_halo_accumulate")
+
+
+def _dcode(dtype):
+    return TO_F32 if np.dtype(dtype) == np.float32 else TO_F64
+
+
+def sumsq3_workspace_bytes(n: int) -> int:
+    return lib.to_sumsq3_workspace_bytes(n)
+
+
+def sumsq3(dtype, x, first: int, n: int, result, workspace, stream: int = 0):
+    """result[0] (device double) = sum of x[c][first:first+n]^2; workspace is a
+    device tensor of at least sumsq3_workspace_bytes(n) bytes."""
+    nbytes = workspace.numel() * workspace.element_size()
+    check(lib.to_sumsq3(_dcode(dtype), _fptrs(x), first, n, _ptr(result), _ptr(workspace), nbytes,
+                        stream), "to_sumsq3")
+
+
+def scale3(dtype, y, x, n: int, sumsq, stream: int = 0):
+    """y[c][:n] = x[c][:n] / sqrt(sumsq[0]) on the device."""
+    check(lib.to_scale3(_dcode(dtype), _fptrs(y), _fptrs(x), n, _ptr(sumsq), stream), "to_scale3")
 
 
 def sm_count() -> int:

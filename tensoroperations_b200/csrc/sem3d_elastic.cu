@@ -37,6 +37,14 @@ template <>
 struct Sem3dConfig<double, 5> {
   static constexpr int EB = 16;  // 400 threads
 };
+template <>
+struct Sem3dConfig<float, 8> {
+  static constexpr int EB = 4;  // 256 threads
+};
+template <>
+struct Sem3dConfig<double, 8> {
+  static constexpr int EB = 2;  // 128 threads
+};
 
 template <typename T, int N>
 size_t sem3d_smem_bytes() {
@@ -234,6 +242,17 @@ int apply_typed(const to_sem3d_plan* plan, const to_sem3d_fields* fl, int accumu
   return launch_sem3d<T, N, false>(plan, fl, stream);
 }
 
+// Every built (dtype, NGLL) pair.
+int apply_dispatch(const to_sem3d_plan* plan, const to_sem3d_fields* fl, int accumulate,
+                   cudaStream_t s, const char* who) {
+  const to_sem3d_desc& d = plan->desc;
+  if (d.ngll == 5 && d.dtype == TO_F32) return apply_typed<float, 5>(plan, fl, accumulate, s);
+  if (d.ngll == 5 && d.dtype == TO_F64) return apply_typed<double, 5>(plan, fl, accumulate, s);
+  if (d.ngll == 8 && d.dtype == TO_F32) return apply_typed<float, 8>(plan, fl, accumulate, s);
+  if (d.ngll == 8 && d.dtype == TO_F64) return apply_typed<double, 8>(plan, fl, accumulate, s);
+  return set_error(TO_ERR_UNSUPPORTED, "%s: ngll %d dtype %d not built", who, d.ngll, d.dtype);
+}
+
 }  // namespace
 }  // namespace to_b200
 
@@ -248,7 +267,7 @@ int to_sem3d_plan_create(const to_sem3d_desc* desc, to_sem3d_plan** plan) {
     return set_error(TO_ERR_INVALID_ARGUMENT, "to_sem3d_plan_create: dtype %d", desc->dtype);
   if (desc->ngll < 2 || desc->ngll > 16)
     return set_error(TO_ERR_INVALID_ARGUMENT, "to_sem3d_plan_create: ngll %d", desc->ngll);
-  const bool built = (desc->ngll == 5);
+  const bool built = (desc->ngll == 5 || desc->ngll == 8);
   if (!built)
     return set_error(TO_ERR_UNSUPPORTED, "to_sem3d_plan_create: ngll %d (%s) not built",
                      desc->ngll, desc->dtype == TO_F32 ? "f32" : "f64");
@@ -286,10 +305,7 @@ int to_sem3d_apply(const to_sem3d_plan* plan, const to_sem3d_fields* fields,
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const to_sem3d_desc& d = plan->desc;
   if (d.nelem == 0) return ok();
-  if (d.ngll == 5 && d.dtype == TO_F32) return apply_typed<float, 5>(plan, fields, accumulate, s);
-  if (d.ngll == 5 && d.dtype == TO_F64) return apply_typed<double, 5>(plan, fields, accumulate, s);
-  return set_error(TO_ERR_UNSUPPORTED, "to_sem3d_apply: ngll %d dtype %d not built", d.ngll,
-                   d.dtype);
+  return apply_dispatch(plan, fields, accumulate, s, "to_sem3d_apply");
 }
 
 int to_sem3d_apply_elements(const to_sem3d_plan* plan, const to_sem3d_fields* fields,
@@ -327,10 +343,7 @@ int to_sem3d_apply_elements(const to_sem3d_plan* plan, const to_sem3d_fields* fi
     }
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (d.ngll == 5 && d.dtype == TO_F32) return apply_typed<float, 5>(&sub, &fl, 1, s);
-  if (d.ngll == 5 && d.dtype == TO_F64) return apply_typed<double, 5>(&sub, &fl, 1, s);
-  return set_error(TO_ERR_UNSUPPORTED, "to_sem3d_apply_elements: ngll %d dtype %d not built",
-                   d.ngll, d.dtype);
+  return apply_dispatch(&sub, &fl, 1, s, "to_sem3d_apply_elements");
 }
 
 int to_device_status(int32_t reset) {

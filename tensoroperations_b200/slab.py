@@ -102,6 +102,11 @@ class SlabPartition:
             out.append((self.rank + 1, self.nglob - self.plane))
         return out
 
+    @property
+    def owned_first(self) -> int:
+        """First node this rank owns: a shared plane belongs to the lower rank."""
+        return self.plane if self.rank > 0 else 0
+
     def element_ranges(self):
         """(boundary ranges, interior range) as (first, count) in local elements.
 
@@ -158,9 +163,14 @@ class SlabOperator:
 
     `plan` is a Sem3dPlan over the rank's elements (assembled); `u`, `f`, the
     per-point arrays and ibool are this rank's device tensors.  Exchange
-    buffers are allocated once here; apply() allocates nothing."""
+    buffers are allocated once here; apply() allocates nothing.
 
-    def __init__(self, part: SlabPartition, plan, fields, f, device, group=None):
+    power_step(): one step of u <- K u / ||K u|| (the steady-state loop of the
+    large configuration): apply, sum of squares over the nodes this rank owns
+    (shared planes counted once, by the lower rank), all-reduce of that one
+    double across ranks, and u rescaled on the device -- no host round trip."""
+
+    def __init__(self, part: SlabPartition, plan, fields, f, device, group=None, u=None):
         import torch
         self.part = part
         self.plan = plan
@@ -177,6 +187,11 @@ class SlabOperator:
         self.ev_bnd = torch.cuda.Event()
         self.ev_done = torch.cuda.Event()
         self.boundary, self.interior = part.element_ranges()
+        self.u = u
+        self.sumsq = torch.zeros(1, dtype=torch.float64, device=device)
+        nown = part.nglob - part.owned_first
+        self.sumsq_ws = torch.empty(max(1, abi.sumsq3_workspace_bytes(nown)), dtype=torch.uint8,
+                                    device=device)
 
     def kernel_launches(self) -> int:
         """Launches of this library's kernels per apply (fills excluded)."""
@@ -213,3 +228,17 @@ class SlabOperator:
             stream.wait_event(self.ev_done)
         if events is not None:
             events[1].record(stream)
+
+    def power_step(self, stream, events=None):
+        import torch
+        import torch.distributed as dist
+        if self.u is None:
+            raise ValueError("power_step needs the operator's u tensors (SlabOperator(..., u=u))")
+        self.apply(stream, events)
+        s = stream.cuda_stream
+        first = self.part.owned_first
+        abi.sumsq3(self.dtype, self.f, first, self.part.nglob - first, self.sumsq, self.sumsq_ws, s)
+        if self.part.world > 1:
+            with torch.cuda.stream(stream):
+                dist.all_reduce(self.sumsq, group=self.group)
+        abi.scale3(self.dtype, self.u, self.f, self.part.nglob, self.sumsq, s)

@@ -1,0 +1,101 @@
+"""The large fp64 configuration's pieces on the GPU (small meshes).
+
+* NGLL 8 operator, f64 (relative L2 <= 1e-12) and f32 (<= 1e-5), assembled
+  and element-local, against the same-precision CPU oracle;
+* the sum of squares (deterministic: same bits on every call) and the
+  device-side rescale;
+* u <- K u / ||K u|| through SlabOperator.power_step, against the same
+  iteration with the oracle on the whole mesh.
+"""
+import math
+
+import numpy as np
+import pytest
+
+from oracle import sem as osem
+from tensoroperations_b200 import abi
+from tensoroperations_b200.sem3d import structured_problem, to_device
+from tensoroperations_b200.slab import SlabOperator, SlabPartition, slab_problem
+
+pytestmark = pytest.mark.gpu
+TOL = {np.float64: 1e-12, np.float32: 1e-5}
+
+
+def _torch():
+    import torch
+    return torch
+
+
+@pytest.mark.parametrize("dtype", [np.float64, np.float32])
+@pytest.mark.parametrize("assembled", [True, False])
+def test_ngll8_operator(dtype, assembled):
+    torch = _torch()
+    prob = structured_problem(3, 2, 3, ngll=8, dtype=dtype, assembled=assembled, seed=8)
+    u, f, arrays, ibool = to_device(prob, "cuda")
+    plan = prob.plan()
+    plan.apply(plan.fields(u, f, arrays, ibool))
+    torch.cuda.synchronize()
+    got = [x.cpu().numpy() for x in f]
+    if assembled:
+        ref = osem.assembled(prob.nelem, 8, prob.nglob, prob.ibool, prob.u, prob.arrays, prob.H,
+                             prob.Hw, prob.w, dtype)
+    else:
+        ref = osem.local(prob.nelem, 8, prob.u, prob.arrays, prob.H, prob.Hw, prob.w, dtype)
+    assert osem.rel_l2(got, ref) < TOL[dtype]
+
+
+@pytest.mark.parametrize("dtype", [np.float64, np.float32])
+@pytest.mark.parametrize("n,first", [(1, 0), (1000, 7), (200_003, 11), (131072, 0)])
+def test_sumsq3(dtype, n, first):
+    torch = _torch()
+    tdt = torch.float64 if dtype == np.float64 else torch.float32
+    x = [torch.randn(first + n + 5, dtype=tdt, device="cuda") for _ in range(3)]
+    res = torch.zeros(1, dtype=torch.float64, device="cuda")
+    ws = torch.empty(abi.sumsq3_workspace_bytes(n), dtype=torch.uint8, device="cuda")
+    abi.sumsq3(dtype, x, first, n, res, ws)
+    r1 = float(res.item())
+    abi.sumsq3(dtype, x, first, n, res, ws)
+    assert float(res.item()) == r1  # deterministic
+    ref = math.fsum(float(v) ** 2 for c in range(3) for v in x[c][first:first + n].double().cpu().numpy())
+    assert abs(r1 - ref) <= 1e-13 * ref
+    with pytest.raises(abi.ToError):
+        abi.sumsq3(dtype, x, first, n, res, ws[:max(0, ws.numel() - 8)] if ws.numel() > 8 else ws[:0])
+
+
+def test_scale3():
+    torch = _torch()
+    x = [torch.randn(5000, dtype=torch.float64, device="cuda") for _ in range(3)]
+    y = [torch.empty_like(v) for v in x]
+    ss = torch.tensor([4.0], dtype=torch.float64, device="cuda")
+    abi.scale3(np.float64, y, x, 5000, ss)
+    torch.cuda.synchronize()
+    for a, b in zip(x, y):
+        assert torch.equal(b, a / 2.0)
+
+
+def _oracle_power(prob, steps):
+    u = prob.u
+    for _ in range(steps):
+        f = osem.assembled(prob.nelem, prob.ngll, prob.nglob, prob.ibool, u, prob.arrays, prob.H,
+                           prob.Hw, prob.w, prob.dtype)
+        nrm = math.sqrt(sum(float(np.dot(v.astype(np.float64), v.astype(np.float64))) for v in f))
+        u = [(v / nrm).astype(prob.dtype) for v in f]
+    return u
+
+
+@pytest.mark.parametrize("ngll", [5, 8])
+def test_power_iteration_single_gpu(ngll):
+    torch = _torch()
+    part = SlabPartition(3, 2, 3, ngll, 1, 0)
+    prob = slab_problem(part, np.float64, 55)
+    u, f, arrays, ibool = to_device(prob, "cuda")
+    plan = prob.plan()
+    op = SlabOperator(part, plan, plan.fields(u, f, arrays, ibool), f, "cuda", u=u)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for _ in range(4):
+            op.power_step(stream)
+    torch.cuda.synchronize()
+    ref = _oracle_power(structured_problem(3, 2, 3, ngll=ngll, dtype=np.float64, assembled=True,
+                                           seed=55), 4)
+    assert osem.rel_l2([x.cpu().numpy() for x in u], ref) < 1e-12

@@ -127,3 +127,61 @@ def test_gloo_ranks_reproduce_the_whole_mesh(world, tmp_path):
         got = np.load(tmp_path / f"f{r}.npy")
         want = np.stack([x[p.node_first:p.node_first + p.nglob] for x in ref])
         assert osem.rel_l2(list(got), list(want)) < 1e-12, r
+
+
+def _power_worker(rank, world, port, out_dir, steps):
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        nex, ney, nez = MESH
+        part = SlabPartition(nex, ney, nez, N, world, rank)
+        prob = slab_problem(part, np.float64, SEED)
+        u = [x.copy() for x in prob.u]
+        faces = part.interfaces()
+        for _ in range(steps):
+            prob.u = u
+            f = _local_contribution(prob, 0, part.nelem)
+            sends = [torch.from_numpy(np.concatenate([f[c][off:off + part.plane] for c in range(3)]))
+                     for _, off in faces]
+            recvs = [torch.empty(3 * part.plane, dtype=torch.float64) for _ in faces]
+            exchange_planes(part, sends, recvs)
+            for (_, off), r in zip(faces, recvs):
+                rv = r.numpy()
+                for c in range(3):
+                    f[c][off:off + part.plane] += rv[c * part.plane:(c + 1) * part.plane]
+            o = part.owned_first
+            ss = torch.tensor([sum(float(np.dot(x[o:], x[o:])) for x in f)], dtype=torch.float64)
+            dist.all_reduce(ss)
+            u = [x / np.sqrt(float(ss[0])) for x in f]
+        np.save(os.path.join(out_dir, f"u{rank}.npy"), np.stack(u))
+    finally:
+        dist.destroy_process_group()
+
+
+def whole_mesh_power(steps, seed=SEED, dtype=np.float64):
+    nex, ney, nez = MESH
+    whole = structured_problem(nex, ney, nez, ngll=N, dtype=dtype, assembled=True, seed=seed)
+    u = whole.u
+    for _ in range(steps):
+        f = osem.assembled(whole.nelem, N, whole.nglob, whole.ibool, u, whole.arrays, whole.H,
+                           whole.Hw, whole.w, dtype)
+        nrm = np.sqrt(sum(float(np.dot(x, x)) for x in f))
+        u = [x / nrm for x in f]
+    return u
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_gloo_power_iteration_counts_shared_planes_once(world, tmp_path):
+    steps = 3
+    mp.start_processes(_power_worker, args=(world, _free_port(), str(tmp_path), steps),
+                       nprocs=world, join=True, start_method="spawn")
+    ref = whole_mesh_power(steps)
+    nex, ney, nez = MESH
+    for r in range(world):
+        p = SlabPartition(nex, ney, nez, N, world, r)
+        got = np.load(tmp_path / f"u{r}.npy")
+        want = [x[p.node_first:p.node_first + p.nglob] for x in ref]
+        assert osem.rel_l2(list(got), want) < 1e-12, r

@@ -129,3 +129,30 @@ def test_nccl_ranks_reproduce_the_whole_mesh(tmp_path):
         got = list(np.load(tmp_path / f"f{rk}.npy"))
         want = [x[p.node_first:p.node_first + p.nglob] for x in ref]
         assert osem.rel_l2(got, want) < TOL, rk
+
+
+def test_nccl_power_iteration_ngll8_f64(tmp_path):
+    torch = _torch()
+    world = min(torch.cuda.device_count(), 4)
+    if world < 2:
+        pytest.skip("needs 2 GPUs")
+    nex, ney, nez, seed, steps = 3, 2, 2 * world, 17, 3
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run",
+           "--nnodes=1", f"--nproc-per-node={world}", "--master-addr", "127.0.0.1",
+           "--master-port", str(_free_port()), str(ROOT / "tests" / "slab_mgpu_check.py"),
+           str(tmp_path), str(nex), str(ney), str(nez), str(seed), "power", "8"]
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=300)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    whole = structured_problem(nex, ney, nez, ngll=8, dtype=np.float64, assembled=True, seed=seed)
+    u = whole.u
+    for _ in range(steps):
+        f = osem.assembled(whole.nelem, 8, whole.nglob, whole.ibool, u, whole.arrays, whole.H,
+                           whole.Hw, whole.w, np.float64)
+        nrm = np.sqrt(sum(float(np.dot(x, x)) for x in f))
+        u = [x / nrm for x in f]
+    for rk in range(world):
+        p = SlabPartition(nex, ney, nez, 8, world, rk)
+        got = list(np.load(tmp_path / f"u{rk}.npy"))
+        want = [x[p.node_first:p.node_first + p.nglob] for x in u]
+        assert osem.rel_l2(got, want) < 1e-12, rk
