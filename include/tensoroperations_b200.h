@@ -219,6 +219,28 @@ size_t to_sumsq3_workspace_bytes(int64_t n);
 int to_sumsq3(int32_t dtype, const void* const x[3], int64_t first, int64_t n, double* result,
               void* workspace, size_t workspace_bytes, void* stream);
 
+/* to_sumsq3 without a workspace argument, for callers that may not allocate
+ * device memory: for example a solver step running inside an application
+ * that owns the GPU's memory through its own pool (a cudaMalloc of ours
+ * would fail or bypass its accounting), or a loop that must not stall the
+ * device the way cudaFree does.  No counterpart in the reference.
+ *   - The block partials live in one fixed array inside the library (256 KiB
+ *     per GPU, kept until the process exits); nothing is allocated per call.
+ *   - The first call on a device looks up that array's device address (with
+ *     the device current); make that first call before any stream capture.
+ *   - n per component is limited to to_sumsq3_noalloc_max_n()
+ *     (1,431,655,765); a larger n is rejected with TO_ERR_INVALID_ARGUMENT
+ *     before anything is launched.
+ *   - Every call shares the array and it keeps the last call's partials.
+ *     Nothing in it needs to start at zero (a call writes every partial it
+ *     later reads), but calls whose kernels overlap on the GPU -- on
+ *     different streams, or from different host threads -- race on it and
+ *     give wrong sums.  Order such calls on one stream.
+ * Same result, bit for bit, as to_sumsq3 on the same inputs. */
+int to_sumsq3_noalloc(int32_t dtype, const void* const x[3], int64_t first, int64_t n,
+                      double* result, void* stream);
+int64_t to_sumsq3_noalloc_max_n(void);
+
 /* y[c][i] = x[c][i] / sqrt(*sumsq) for i < n (sumsq read on the device, so no
  * host synchronisation); y may equal x. */
 int to_scale3(int32_t dtype, void* const y[3], const void* const x[3], int64_t n,

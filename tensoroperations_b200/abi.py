@@ -93,6 +93,9 @@ _sig("to_sem3d_halo_accumulate", C.c_int, [C.c_int32, C.c_void_p, C.c_int64, C.c
 _sig("to_sumsq3_workspace_bytes", C.c_size_t, [C.c_int64])
 _sig("to_sumsq3", C.c_int, [C.c_int32, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p,
                             C.c_size_t, C.c_void_p])
+_sig("to_sumsq3_noalloc", C.c_int, [C.c_int32, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p,
+                                    C.c_void_p])
+_sig("to_sumsq3_noalloc_max_n", C.c_int64, [])
 _sig("to_scale3", C.c_int, [C.c_int32, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p])
 _sig("to_sem3d_plan_create", C.c_int, [C.POINTER(Sem3dDesc), C.POINTER(C.c_void_p)])
 _sig("to_sem3d_plan_destroy", C.c_int, [C.c_void_p])
@@ -189,6 +192,13 @@ def sumsq3(dtype, x, first: int, n: int, result, workspace, stream: int = 0):
     nbytes = workspace.numel() * workspace.element_size()
     check(lib.to_sumsq3(_dcode(dtype), _fptrs(x), first, n, _ptr(result), _ptr(workspace), nbytes,
                         stream), "to_sumsq3")
+
+
+def sumsq3_noalloc(dtype, x, first: int, n: int, result, stream: int = 0):
+    """sumsq3 with the library's fixed scratch instead of a workspace (no
+    allocation; calls that overlap on the GPU race on that scratch)."""
+    check(lib.to_sumsq3_noalloc(_dcode(dtype), _fptrs(x), first, n, _ptr(result), stream),
+          "to_sumsq3_noalloc")
 
 
 def scale3(dtype, y, x, n: int, sumsq, stream: int = 0):

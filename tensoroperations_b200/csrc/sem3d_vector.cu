@@ -10,6 +10,8 @@
 // The chunk size is fixed, so the grouping -- and the rounding -- depends
 // only on n, never on the GPU's SM count: the same inputs give the same bits
 // on any device.  Accumulation is in double for every dtype.
+#include <mutex>
+
 #include "common.hpp"
 
 namespace to_b200 {
@@ -108,6 +110,45 @@ int sumsq_common(int32_t dtype, const void* const x[3], int64_t first, int64_t n
   return set_error(TO_ERR_INVALID_ARGUMENT, "%s: dtype %d", who, dtype);
 }
 
+// ---- the allocation-free variant ----------------------------------------------
+// Block partials of to_sumsq3_noalloc live in this file-scope array: 32768
+// doubles (256 KiB), held by every GPU that loads the library until the
+// process exits.  One partial covers kSumChunk values, so one call handles at
+// most 32768 * 131072 values, i.e. n <= kNoAllocMaxN per component.
+constexpr long long kNoAllocMaxPartials = 32768;
+constexpr long long kNoAllocMaxN = kNoAllocMaxPartials * kSumChunk / 3;
+static __device__ __align__(256) double g_noalloc_partials[kNoAllocMaxPartials];
+
+// Device address of g_noalloc_partials, looked up once per device.  In host
+// code the array's name only stands in for the symbol, so the address comes
+// from cudaGetSymbolAddress with that device current.
+double* noalloc_partials(int* status) {
+  static std::mutex mu;
+  static double* ptr[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    *status = cuda_fail(e, "to_sumsq3_noalloc: cudaGetDevice");
+    return nullptr;
+  }
+  if (dev < 0 || dev >= 64) {
+    *status = set_error(TO_ERR_UNSUPPORTED, "to_sumsq3_noalloc: device id %d >= 64", dev);
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptr[dev]) {
+    double* p = nullptr;
+    e = cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_noalloc_partials);
+    if (e != cudaSuccess) {
+      *status = cuda_fail(e, "to_sumsq3_noalloc: cudaGetSymbolAddress");
+      return nullptr;
+    }
+    ptr[dev] = p;
+  }
+  *status = TO_OK;
+  return ptr[dev];
+}
+
 }  // namespace to_b200
 
 using namespace to_b200;
@@ -127,6 +168,24 @@ int to_sumsq3(int32_t dtype, const void* const x[3], int64_t first, int64_t n, d
   return sumsq_common(dtype, x, first, n, result, static_cast<double*>(workspace),
                       static_cast<cudaStream_t>(stream), "to_sumsq3");
 }
+
+int to_sumsq3_noalloc(int32_t dtype, const void* const x[3], int64_t first, int64_t n,
+                      double* result, void* stream) {
+  if (n > kNoAllocMaxN)
+    return set_error(TO_ERR_INVALID_ARGUMENT,
+                     "to_sumsq3_noalloc: n = %lld values per component exceeds this entry "
+                     "point's fixed scratch (at most %lld); use to_sumsq3 with a workspace",
+                     static_cast<long long>(n), kNoAllocMaxN);
+  if (!x || !result || first < 0 || n < 0)
+    return set_error(TO_ERR_INVALID_ARGUMENT, "to_sumsq3_noalloc: bad argument");
+  int st = TO_OK;
+  double* partial = noalloc_partials(&st);
+  if (!partial) return st;
+  return sumsq_common(dtype, x, first, n, result, partial, static_cast<cudaStream_t>(stream),
+                      "to_sumsq3_noalloc");
+}
+
+int64_t to_sumsq3_noalloc_max_n(void) { return kNoAllocMaxN; }
 
 int to_scale3(int32_t dtype, void* const y[3], const void* const x[3], int64_t n,
               const double* sumsq, void* stream) {
