@@ -49,13 +49,17 @@ NGLL = 5
 FALLBACK_HBM_GBS = 6650.0
 # DRAM bytes (read + write) per launch of the kernel, from one ncu capture of the
 # 32^3 case scaled by elements to the 64^3 launch
-# (profiles/sem3d_elastic_v3_32cube_full.md); None where not captured.
-NCU_TRAFFIC_PER_LAUNCH = {"0": 276.76e6 * 8}
+# (profiles/sem3d_elastic_v3_32cube_full.md, sem3d_elastic_v5_32cube_full.md);
+# None where not captured.
+NCU_TRAFFIC_PER_LAUNCH = {"0": 276.76e6 * 8, "5": 275.32e6 * 8}
+DEFAULT_VARIANT = "5"
 KERNEL_NAMES = {"0": "sem3d_elastic_v3_kernel<5,8,2,true>",
                 "1": "sem3d_elastic_tma_kernel<float,5,8,2,true>",
                 "2": "sem3d_elastic_kernel<float,5,32,true>",
                 "3": "sem3d_elastic_v3_kernel<5,4,4,true>",
-                "4": "sem3d_elastic_v3_kernel<5,16,1,true>"}
+                "4": "sem3d_elastic_v3_kernel<5,16,1,true>",
+                "5": "sem3d_elastic_v5_kernel<8,3,true>",
+                "6": "sem3d_elastic_v5_kernel<4,5,true>"}
 
 
 def measured_peak_hbm():
@@ -246,7 +250,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--variant", type=int, default=None,
                     help="f32 kernel variant (TO_SEM3D_VARIANT): 0 point-pair 8x2, 1 TMA 8x2, "
-                         "2 streaming, 3 point-pair 4x4, 4 point-pair 16x1")
+                         "2 streaming, 3 point-pair 4x4, 4 point-pair 16x1, 5 line-owner 8x3, 6 line-owner 4x5")
     ap.add_argument("--mesh", type=int, nargs=3, default=[64, 64, 64],
                     metavar=("NEX", "NEY", "NEZ"), help="hexes per GPU (profiling runs)")
     args = ap.parse_args()
@@ -358,12 +362,12 @@ def main():
             "config": config_dict(prob, world),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
-                         "traffic": (NCU_TRAFFIC_PER_LAUNCH.get(os.environ.get("TO_SEM3D_VARIANT", "0"))
+                         "traffic": (NCU_TRAFFIC_PER_LAUNCH.get(os.environ.get("TO_SEM3D_VARIANT", DEFAULT_VARIANT))
                                      if tuple(MESH_PER_GPU) == (64, 64, 64) else None),
                          "traffic_source": "ncu dram__bytes_read+write of the 32^3 case x8",
                          "peak_source": peak_src,
                          "algorithmic_bytes_per_launch": alg, "kernel_ms": kern_ms,
-                         "kernel": KERNEL_NAMES.get(os.environ.get("TO_SEM3D_VARIANT", "0"))},
+                         "kernel": KERNEL_NAMES.get(os.environ.get("TO_SEM3D_VARIANT", DEFAULT_VARIANT))},
             "cpu_baseline": cpu,
             "e2e": None if not e2e_steps else
                    {"value": prob.nelem * world / (e2e_ms * 1e-3) / 1e6, "unit": "Melem/s",

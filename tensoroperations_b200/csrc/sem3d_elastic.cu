@@ -15,6 +15,7 @@ __device__ int g_to_device_status = 0;
 
 #include "sem3d_elastic_tma.cuh"
 #include "sem3d_elastic_v3.cuh"
+#include "sem3d_elastic_v5.cuh"
 
 struct to_sem3d_plan {
   to_sem3d_desc desc;
@@ -185,16 +186,38 @@ int launch_v3(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t
   return ok();
 }
 
-// Kernel variant for f32 NGLL 5 (TO_SEM3D_VARIANT):
-//   0 point-pair pipelined kernel, 8 elements x 2 CTAs/SM (default)
+// The line-owner kernel (f32 NGLL 5, staged arrays 16-byte aligned).
+template <int EB, int MINB, bool ASM>
+int launch_v5(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t stream,
+              int dev, int sms) {
+  constexpr int NT = EB * 25;
+  const size_t smem = Sem3dV5Layout<EB, ASM>::kTotal;
+  auto kernel = sem3d_elastic_v5_kernel<EB, MINB, ASM>;
+  static KernelSlot slot;
+  int nb = 0;
+  if (int st = configure(slot, kernel, dev, NT, smem, &nb)) return st;
+  Sem3dArgs<float, 5> a = make_args<float, 5>(plan, fl);
+  a.prefetch = 1;
+  const long long nbatch = (plan->desc.nelem + EB - 1) / EB;
+  const long long cap = static_cast<long long>(sms) * nb;
+  const int grid = static_cast<int>(nbatch < cap ? nbatch : cap);
+  kernel<<<grid, NT, smem, stream>>>(a);
+  TO_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
+// Kernel variant for f32 NGLL 5 (TO_SEM3D_VARIANT; default 5):
+//   0 point-pair pipelined kernel, 8 elements x 2 CTAs/SM
 //   1 TMA-staged kernel, 8 elements x 2 CTAs/SM
 //   2 register-streaming kernel
 //   3 point-pair pipelined kernel, 4 elements x 4 CTAs/SM
 //   4 point-pair pipelined kernel, 16 elements x 1 CTA/SM
+//   5 line-owner kernel, 8 elements x 3 CTAs/SM
+//   6 line-owner kernel, 4 elements x 5 CTAs/SM
 int sem3d_f32_variant() {
   static const int v = [] {
     const char* e = std::getenv("TO_SEM3D_VARIANT");
-    return e ? std::atoi(e) : 0;
+    return e ? std::atoi(e) : 5;
   }();
   return v;
 }
@@ -210,7 +233,9 @@ int launch_sem3d(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStrea
       if (v == 1) return launch_tma<T, N, 8, 2, ASM>(plan, fl, stream, dev, sms);
       if (v == 3) return launch_v3<N, 4, 4, ASM>(plan, fl, stream, dev, sms);
       if (v == 4) return launch_v3<N, 16, 1, ASM>(plan, fl, stream, dev, sms);
-      return launch_v3<N, 8, 2, ASM>(plan, fl, stream, dev, sms);
+      if (v == 6) return launch_v5<4, ASM ? 5 : 4, ASM>(plan, fl, stream, dev, sms);
+      if (v == 0) return launch_v3<N, 8, 2, ASM>(plan, fl, stream, dev, sms);
+      return launch_v5<8, ASM ? 3 : 2, ASM>(plan, fl, stream, dev, sms);
     }
   }
   return launch_ldg<T, N, ASM>(plan, fl, stream, dev, sms);

@@ -1,0 +1,363 @@
+// sem3d_elastic_v5.cuh -- f32 fused SEM 3D elastic kernel, "line owner" design.
+//
+// Measured on the point-pair kernel: the SM's L1 / shared-memory pipe was the
+// limiter (about 630 wavefronts per element against about 710 cycles), and
+// most shared-memory traffic was the xi / eta contractions: every thread of
+// an i-row read the same five neighbours and produced one output, so each
+// row was read five times.  Here every thread holds three roles at once:
+//
+//   column owner   (le, j=a, i=b), the N points k = 0..N-1: gathers u,
+//                  contracts along k in registers (gamma), evaluates the
+//                  Integrand9 physics at its points, scatters f;
+//   xi-line owner  (le, k=b, j=a), the N points i = 0..N-1: reads the row
+//                  once and produces all N xi-derivatives (and later all N
+//                  xi-divergences) of that row;
+//   eta-line owner (le, k=a, i=b): the same along j.
+//
+// A thread's lane is t = le*25 + a*5 + b.  Shared buffers keep one word per
+// point, k-major: word (k*SK + le*25 + j*5 + i).  The k-stride SK is
+// 25*EB + 25 for the buffers the xi-lines read or write and 25*EB + 29 for
+// the eta-side ones (129 and 101 for EB = 4); with these strides every access
+// of every phase -- a column at fixed k (consecutive words), a xi-row at fixed
+// i, an eta-row at fixed j -- touches 32 distinct banks (checked exhaustively
+// for EB = 4, 8, 12, 16), so u is written twice, once in each layout.  Per thread and batch of 5 points:
+// 120 shared stores + 120 exchange loads + 60 geometry loads, all
+// conflict-free.
+//
+// Phases per batch (4 barriers), all in two buffers X (xi side) and E (eta
+// side), each value overwriting its input in place -- a row's words are read
+// and written only by its line owner, a column's only by its column owner:
+//   A  column: u -> X, E; gamma-gradients in registers
+//   B1 lines:  X rows -> xi-gradients (in place), E rows -> eta-gradients
+//   B2 column: gradients + gamma -> Integrand9 (geometry from the staged
+//              arrays) -> F^xi into X, F^eta into E (in place); gamma fluxes
+//              stay in registers
+//   C1 lines:  F rows -> xi- / eta-divergences (in place)
+//   C2 column: divergences + gamma-divergence -> WeightedSum -> scatter-add /
+//              store
+// Two buffers instead of four keep a CTA of 8 elements at about 74 KB of
+// shared memory, so three CTAs (600 threads) fit on an SM.
+// The 12 per-point arrays stream global -> shared with bulk copies (as in the
+// point-pair kernel) and the next batch's ibool / u gathers are in flight
+// during C1 / C2.
+#pragma once
+
+#include <cstdint>
+
+#include "sem3d_elastic.cuh"
+#include "sem3d_elastic_tma.cuh"
+#include "sm100_primitives.cuh"
+
+namespace to_b200 {
+
+template <int EB, bool ASM>
+struct Sem3dV5Layout {
+  static constexpr int N = 5, NN = 25, P = 125, NT = EB * NN, EP = EB * P;
+  // k-strides of the xi- and eta-side buffers: the smallest strides >= NT with
+  // every access pattern conflict-free for this batch size (exhaustive search)
+  static_assert(EB == 4 || EB == 8 || EB == 12 || EB == 16, "strides searched for EB 4/8/12/16");
+  static constexpr int SKX = EB == 4 ? 129 : NT + 25;
+  static constexpr int SKE = EB == 4 ? 101 : NT + 29;
+  static constexpr int kStaged = kNumPointArrays + (ASM ? 0 : 3);
+  static constexpr size_t kHeader = 128;
+  static constexpr size_t kStageBytes = size_t(kStaged) * EP * 4;
+  static constexpr size_t kXBytes = (size_t(3) * N * SKX * 4 + 15) & ~size_t(15);
+  static constexpr size_t kEBytes = (size_t(3) * N * SKE * 4 + 15) & ~size_t(15);
+  static constexpr size_t kTotal = kHeader + kStageBytes + kXBytes + kEBytes;
+};
+
+template <int EB, int MINB, bool ASM>
+__global__ void __launch_bounds__(EB * 25, MINB)
+    sem3d_elastic_v5_kernel(const __grid_constant__ Sem3dArgs<float, 5> a) {
+  using LY = Sem3dV5Layout<EB, ASM>;
+  constexpr int N = 5, NN = 25, P = 125, NT = LY::NT, EP = LY::EP;
+  constexpr int SKX = LY::SKX, SKE = LY::SKE;
+  constexpr int CX = N * SKX, CE = N * SKE;  // component strides
+  constexpr int kStaged = LY::kStaged;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);
+  float* stage = reinterpret_cast<float*>(smem_raw + LY::kHeader);
+  float* RX = reinterpret_cast<float*>(smem_raw + LY::kHeader + LY::kStageBytes);  // xi side
+  float* RE = RX + LY::kXBytes / 4;                                               // eta side
+  float* RDX = RX;  // the same words, named by what they hold in B1 / C1 outputs
+  float* RDE = RE;
+
+  const int tid = threadIdx.x;
+  const int le = tid / NN;
+  const int ab = tid - le * NN;
+  const int ra = ab / N;  // column j / xi-line j / eta-line k
+  const int rb = ab - ra * N;  // column i / xi-line k / eta-line i
+  const int lx = rb * SKX + le * NN + ra * N;  // xi-line (k=b, j=a): + i
+  const int ly = ra * SKE + le * NN + rb;      // eta-line (k=a, i=b): + 5 j
+  const int spt = le * P + ab;                  // staged point (k=0, j=a, i=b): + k*NN
+
+  const long long nbatch = (a.nelem + EB - 1) / EB;
+  const long long G = gridDim.x;
+  const uint64_t pol_stream = l2_policy_evict_first();
+
+  auto batch_words = [&](long long bb) {
+    const long long e0 = bb * EB;
+    const long long ne = (a.nelem - e0 < EB) ? (a.nelem - e0) : EB;
+    return ne * P;
+  };
+  auto issue_stage = [&](long long bb) {
+    const long long e0 = bb * EB;
+    const uint32_t bytes = static_cast<uint32_t>(batch_words(bb) * 4) & ~15u;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    mbar_arrive_expect_tx(bar, kStaged * bytes);
+#pragma unroll
+    for (int q = 0; q < kNumPointArrays; ++q)
+      bulk_g2s_hint(stage + size_t(q) * EP, a.m[q] + e0 * P, bytes, bar, pol_stream);
+    if (!ASM) {
+#pragma unroll
+      for (int c = 0; c < 3; ++c)
+        bulk_g2s_hint(stage + size_t(kNumPointArrays + c) * EP, a.u[c] + e0 * P, bytes, bar,
+                      pol_stream);
+    }
+  };
+  auto prefetch_batch = [&](long long bb) {
+    if (bb >= nbatch) return;
+    const long long e0 = bb * EB;
+    const uint32_t bytes = static_cast<uint32_t>(batch_words(bb) * 4);
+#pragma unroll
+    for (int q = 0; q < kNumPointArrays; ++q) l2_prefetch_bulk(a.m[q] + e0 * P, bytes);
+    if (ASM)
+      l2_prefetch_bulk(a.ibool + e0 * P, bytes);
+    else
+#pragma unroll
+      for (int c = 0; c < 3; ++c) l2_prefetch_bulk(a.u[c] + e0 * P, bytes);
+  };
+
+  const long long b0 = blockIdx.x;
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (tid == 0 && b0 < nbatch) {
+    issue_stage(b0);
+    prefetch_batch(b0 + G);
+  }
+
+  const float wi = a.ops.w[rb];
+  const float wj = a.ops.w[ra];
+  const float wij = wi * wj;
+  uint32_t parity = 0;
+
+  // gather pipeline registers: ibool and u of the NEXT batch to run
+  int node_n[N];
+  float uc_n[3][N];
+  auto gather = [&](long long bb) {
+    const long long e = bb * EB + le;
+    const bool v = (bb < nbatch) && (e < a.nelem);
+    const long long base = e * P + ab;
+#pragma unroll
+    for (int k = 0; k < N; ++k) node_n[k] = v ? __ldg(a.ibool + base + k * NN) : 0;
+#pragma unroll
+    for (int k = 0; k < N; ++k)
+#pragma unroll
+      for (int c = 0; c < 3; ++c) uc_n[c][k] = v ? __ldg(a.u[c] + node_n[k]) : 0.f;
+  };
+  if (ASM) gather(b0);
+
+  for (long long b = b0; b < nbatch; b += G) {
+    if (tid == 0) prefetch_batch(b + 2 * G);
+    const long long e0 = b * EB;
+    const long long e = e0 + le;
+    const bool valid = e < a.nelem;
+
+    int node[N];
+#pragma unroll
+    for (int k = 0; k < N; ++k) node[k] = ASM ? node_n[k] : 0;
+    const bool ok = mbar_wait_bounded(bar, parity, kMbarMaxPolls);
+    if (__syncthreads_or(!ok)) {
+      if (tid == 0) atomicExch(&g_to_device_status, int(TO_ERR_TIMEOUT));
+      mbar_wait_bounded(bar, parity, kMbarMaxPolls);
+      return;
+    }
+    parity ^= 1u;
+    {
+      // tail of the launch: words past the last 16-byte boundary of each run
+      const long long words = batch_words(b);
+      const long long bw = ((words * 4) & ~15ll) / 4;
+      if (bw < words) {
+        for (int t = tid; t < kStaged * 4; t += NT) {
+          const int q = t >> 2;
+          const long long x = bw + (t & 3);
+          if (x < words)
+            stage[size_t(q) * EP + x] =
+                q < kNumPointArrays ? a.m[q][e0 * P + x] : a.u[q - kNumPointArrays][e0 * P + x];
+        }
+        __syncthreads();
+      }
+    }
+
+    // ---- A: column u -> UX, UE; gamma-gradients in registers ----
+    float dgm[3][N];
+    {
+      float uc[3][N];
+#pragma unroll
+      for (int k = 0; k < N; ++k)
+#pragma unroll
+        for (int c = 0; c < 3; ++c)
+          uc[c][k] = ASM ? uc_n[c][k]
+                         : (valid ? stage[size_t(kNumPointArrays + c) * EP + spt + k * NN] : 0.f);
+#pragma unroll
+      for (int c = 0; c < 3; ++c)
+#pragma unroll
+        for (int k = 0; k < N; ++k) {
+          RX[c * CX + k * SKX + tid] = uc[c][k];
+          RE[c * CE + k * SKE + tid] = uc[c][k];
+        }
+#pragma unroll
+      for (int c = 0; c < 3; ++c)
+#pragma unroll
+        for (int k = 0; k < N; ++k) {
+          float s = 0.f;
+#pragma unroll
+          for (int p = 0; p < N; ++p) s = fmaf(a.ops.H[k][p], uc[c][p], s);
+          dgm[c][k] = s;
+        }
+    }
+    __syncthreads();
+
+    // ---- B1: line owners -> xi- and eta-gradients of their rows ----
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+      float v[N], w[N];
+#pragma unroll
+      for (int p = 0; p < N; ++p) {
+        v[p] = RX[c * CX + lx + p];
+        w[p] = RE[c * CE + ly + p * N];
+      }
+#pragma unroll
+      for (int o = 0; o < N; ++o) {
+        float sx = 0.f, se = 0.f;
+#pragma unroll
+        for (int p = 0; p < N; ++p) {
+          sx = fmaf(a.ops.H[o][p], v[p], sx);
+          se = fmaf(a.ops.H[o][p], w[p], se);
+        }
+        RDX[c * CX + lx + o] = sx;
+        RDE[c * CE + ly + o * N] = se;
+      }
+    }
+    __syncthreads();
+
+    // ---- B2: column Integrand9 (k-pairs in packed lanes) -> FX, FE ----
+    float Fg[3][N];
+    {
+      auto point_pair = [&](int k0, int k1) {
+        V2<float> dxi[3], det[3], dg[3], J[3][3];
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+          dxi[c] = mk2(RDX[c * CX + k0 * SKX + tid], RDX[c * CX + k1 * SKX + tid]);
+          det[c] = mk2(RDE[c * CE + k0 * SKE + tid], RDE[c * CE + k1 * SKE + tid]);
+          dg[c] = mk2(dgm[c][k0], dgm[c][k1]);
+        }
+#pragma unroll
+        for (int r = 0; r < 3; ++r)
+#pragma unroll
+          for (int d = 0; d < 3; ++d) {
+            const float* q = stage + size_t(kXIX + 3 * r + d) * EP + spt;
+            J[r][d] = mk2(q[k0 * NN], q[k1 * NN]);
+          }
+        const float* qj = stage + size_t(kJAC) * EP + spt;
+        const float* ql = stage + size_t(kL2M) * EP + spt;
+        const float* qm = stage + size_t(kMU) * EP + spt;
+        V2<float> F[3][3];
+        integrand9_lanes<V2<float>, float>(dxi, det, dg, J, mk2(ql[k0 * NN], ql[k1 * NN]),
+                                           mk2(qm[k0 * NN], qm[k1 * NN]),
+                                           mk2(qj[k0 * NN], qj[k1 * NN]), F);
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+          RX[c * CX + k0 * SKX + tid] = F[0][c].v.x;
+          RX[c * CX + k1 * SKX + tid] = F[0][c].v.y;
+          RE[c * CE + k0 * SKE + tid] = F[1][c].v.x;
+          RE[c * CE + k1 * SKE + tid] = F[1][c].v.y;
+          Fg[c][k0] = F[2][c].v.x;
+          Fg[c][k1] = F[2][c].v.y;
+        }
+      };
+      point_pair(0, 1);
+      point_pair(2, 3);
+      {
+        constexpr int k = N - 1;
+        float dxi[3], det[3], dg[3], J[3][3];
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+          dxi[c] = RDX[c * CX + k * SKX + tid];
+          det[c] = RDE[c * CE + k * SKE + tid];
+          dg[c] = dgm[c][k];
+        }
+#pragma unroll
+        for (int r = 0; r < 3; ++r)
+#pragma unroll
+          for (int d = 0; d < 3; ++d) J[r][d] = stage[size_t(kXIX + 3 * r + d) * EP + spt + k * NN];
+        float F[3][3];
+        integrand9_lanes<float, float>(dxi, det, dg, J, stage[size_t(kL2M) * EP + spt + k * NN],
+                                       stage[size_t(kMU) * EP + spt + k * NN],
+                                       stage[size_t(kJAC) * EP + spt + k * NN], F);
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+          RX[c * CX + k * SKX + tid] = F[0][c];
+          RE[c * CE + k * SKE + tid] = F[1][c];
+          Fg[c][k] = F[2][c];
+        }
+      }
+    }
+    __syncthreads();  // stage reads and flux writes of this batch are done
+
+    if (tid == 0 && b + G < nbatch) issue_stage(b + G);
+    if (ASM) gather(b + G);  // lands while the divergences run
+
+    // ---- C1: line owners -> xi- and eta-divergences of their rows ----
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+      float v[N], w[N];
+#pragma unroll
+      for (int q = 0; q < N; ++q) {
+        v[q] = RX[c * CX + lx + q];
+        w[q] = RE[c * CE + ly + q * N];
+      }
+#pragma unroll
+      for (int o = 0; o < N; ++o) {
+        float sx = 0.f, se = 0.f;
+#pragma unroll
+        for (int q = 0; q < N; ++q) {
+          sx = fmaf(a.ops.Hw[q][o], v[q], sx);
+          se = fmaf(a.ops.Hw[q][o], w[q], se);
+        }
+        RDX[c * CX + lx + o] = sx;
+        RDE[c * CE + ly + o * N] = se;
+      }
+    }
+    __syncthreads();
+
+    // ---- C2: column WeightedSum -> scatter-add / store ----
+    {
+      const long long obase = e * P + ab;
+#pragma unroll
+      for (int k = 0; k < N; ++k) {
+        const float wjk = wj * a.ops.w[k], wik = wi * a.ops.w[k];
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+          float g = 0.f;
+#pragma unroll
+          for (int q = 0; q < N; ++q) g = fmaf(a.ops.Hw[q][k], Fg[c][q], g);
+          const float tx = RDX[c * CX + k * SKX + tid];
+          const float te = RDE[c * CE + k * SKE + tid];
+          const float fc = fmaf(wij, g, fmaf(wik, te, wjk * tx));
+          if (valid) {
+            if (ASM)
+              atomicAdd(a.f[c] + node[k], fc);
+            else
+              a.f[c][obase + k * NN] = fc;
+          }
+        }
+      }
+    }
+  }
+}
+
+}  // namespace to_b200
