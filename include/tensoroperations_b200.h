@@ -247,6 +247,29 @@ int to_scale3(int32_t dtype, void* const y[3], const void* const x[3], int64_t n
               const double* sumsq, void* stream);
 
 /* ---------------------------------------------------------------------- */
+/* Permuted multilevel contraction chain on the tensor cores               */
+/* ---------------------------------------------------------------------- */
+/*
+ *   T[a,b,c,d] = sum_{e,f} A[a,e,c,f] * B[f,b,e,d]
+ *   R[a,d]     = sum_{b,c} T[a,b,c,d] * C[c,b]
+ * All six extents equal E (32, 64 or 128); row-major fp32 tensors in device
+ * memory (A, B and the workspace 16-byte aligned).  The chain the reference
+ * builds from ContractionNodes over permuted operands
+ * (benchmarks/permuted_contraction/bench_permuted_contraction.cpp,
+ * benchmarks/multilevel_contraction/bench_multilevel_contraction.cpp).  Step 1
+ * runs on tcgen05 (TF32 x3 split, fp32 accumulation in TMEM) with TMA reading
+ * the permuted operands in place; step 2 is fused into its epilogue, so T
+ * never reaches memory unless `T` is non-NULL (then it is also stored, for
+ * checking).  R is overwritten.  `workspace` holds the split operands:
+ * to_chain_workspace_bytes(E) bytes.  Asynchronous on `stream`.
+ */
+size_t to_chain_workspace_bytes(int32_t E);
+int to_chain_f32(int32_t E, const float* A, const float* B, const float* C, float* R, float* T,
+                 void* workspace, size_t workspace_bytes, void* stream);
+/* Useful flops of one chain: 2 E^6 + 2 E^4. */
+double to_chain_flops(int32_t E);
+
+/* ---------------------------------------------------------------------- */
 /* Level-graph lowering                                                    */
 /* ---------------------------------------------------------------------- */
 /*

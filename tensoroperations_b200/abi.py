@@ -97,6 +97,9 @@ _sig("to_sumsq3_noalloc", C.c_int, [C.c_int32, C.c_void_p, C.c_int64, C.c_int64,
                                     C.c_void_p])
 _sig("to_sumsq3_noalloc_max_n", C.c_int64, [])
 _sig("to_scale3", C.c_int, [C.c_int32, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p])
+_sig("to_chain_workspace_bytes", C.c_size_t, [C.c_int32])
+_sig("to_chain_f32", C.c_int, [C.c_int32] + [C.c_void_p] * 6 + [C.c_size_t, C.c_void_p])
+_sig("to_chain_flops", C.c_double, [C.c_int32])
 _sig("to_sem3d_plan_create", C.c_int, [C.POINTER(Sem3dDesc), C.POINTER(C.c_void_p)])
 _sig("to_sem3d_plan_destroy", C.c_int, [C.c_void_p])
 _sig("to_sem3d_apply", C.c_int, [C.c_void_p, C.POINTER(Sem3dFields), C.c_int32, C.c_void_p])
@@ -204,6 +207,13 @@ def sumsq3_noalloc(dtype, x, first: int, n: int, result, stream: int = 0):
 def scale3(dtype, y, x, n: int, sumsq, stream: int = 0):
     """y[c][:n] = x[c][:n] / sqrt(sumsq[0]) on the device."""
     check(lib.to_scale3(_dcode(dtype), _fptrs(y), _fptrs(x), n, _ptr(sumsq), stream), "to_scale3")
+
+
+def chain_f32(E: int, A, B, Cm, R, workspace, T=None, stream: int = 0):
+    """R[a,d] = sum_{b,c} (sum_{e,f} A[a,e,c,f] B[f,b,e,d]) C[c,b] on the tensor cores."""
+    nbytes = workspace.numel() * workspace.element_size()
+    check(lib.to_chain_f32(E, _ptr(A), _ptr(B), _ptr(Cm), _ptr(R), _ptr(T), _ptr(workspace), nbytes,
+                           stream), "to_chain_f32")
 
 
 def sm_count() -> int:

@@ -32,6 +32,10 @@ inline int cuda_fail(cudaError_t e, const char* what) {
 // SM count of the current device (cached per device id), or <0 on failure.
 int device_sm_count(int* device_out);
 
+// Status word of the tensor-core contraction kernels (their translation unit's
+// own device symbol): *value = 0 or a to_status; reset clears it.
+int chain_device_status(int reset, int* value);
+
 inline bool aligned(const void* p, size_t a) {
   return (reinterpret_cast<uintptr_t>(p) % a) == 0;
 }

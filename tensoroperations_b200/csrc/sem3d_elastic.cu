@@ -378,6 +378,9 @@ int to_device_status(int32_t reset) {
     const int z = 0;
     TO_CUDA_TRY(cudaMemcpyToSymbol(g_to_device_status, &z, sizeof(int)));
   }
+  int w = 0;
+  if (int st = chain_device_status(reset, &w)) return st;
+  if (!v) v = w;
   if (v) return set_error(v, "a kernel reported %s", to_status_string(v));
   return ok();
 }
