@@ -231,6 +231,91 @@ def run_reference(args):
     return 0
 
 
+def run_chain(args):
+    """Config 4: the permuted multilevel contraction chain (E = 64) on the tensor cores.
+
+    Not the headline line (that is the SEM operator); printed when asked for
+    with --workload chain.  One step = one to_chain_f32 call: the TF32 split /
+    regroup pre-pass, the tcgen05 GEMM with the fused second contraction, R
+    zeroed first.  Inputs 4 x 64 MB, above L2."""
+    import torch
+    from tensoroperations_b200 import abi
+    E = args.chain_extent
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(4)
+    A = torch.randn((E,) * 4, generator=g, device=dev)
+    B = torch.randn((E,) * 4, generator=g, device=dev)
+    Cm = torch.randn((E, E), generator=g, device=dev)
+    R = torch.empty((E, E), device=dev)
+    ws = torch.empty(abi.lib.to_chain_workspace_bytes(E), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    s = stream.cuda_stream
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            abi.chain_f32(E, A, B, Cm, R, ws, stream=s)
+    torch.cuda.synchronize()
+    steps = args.steps
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    with ClockSampler(gpu_id_for(dev)) as clocks:
+        ev[0].record(stream)
+        for _ in range(steps):
+            abi.chain_f32(E, A, B, Cm, R, ws, stream=s)
+        ev[1].record(stream)
+        torch.cuda.synchronize()
+    ms = ev[0].elapsed_time(ev[1]) / steps
+    useful = abi.lib.to_chain_flops(E)
+    tensor_flops = 3 * 2.0 * E ** 6
+    # library comparison: torch fp32 (TF32 off) on the same permuted problem
+    torch.backends.cuda.matmul.allow_tf32 = False
+    def torch_chain():
+        Am = A.permute(0, 2, 1, 3).reshape(E * E, E * E)
+        Bm = B.permute(2, 0, 1, 3).reshape(E * E, E * E)
+        T = (Am @ Bm).reshape(E, E, E, E).permute(0, 2, 1, 3)
+        return torch.einsum("abcd,cb->ad", T, Cm)
+    for _ in range(2):
+        torch_chain()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(5):
+        Rt = torch_chain()
+    e1.record()
+    torch.cuda.synchronize()
+    torch_ms = e0.elapsed_time(e1) / 5
+    rel = float((R - Rt).norm() / Rt.norm())
+    # CPU baseline: numpy float32 on the host's BLAS threads, one chain
+    An, Bn, Cn = (x.cpu().numpy() for x in (A, B, Cm))
+    t0 = time.perf_counter()
+    Tn = (An.transpose(0, 2, 1, 3).reshape(E * E, E * E) @
+          Bn.transpose(2, 0, 1, 3).reshape(E * E, E * E)).reshape(E, E, E, E)
+    np.einsum("acbd,cb->ad", Tn, Cn, optimize=True)
+    cpu_s = time.perf_counter() - t0
+    mp_path = ROOT / "MEASURED_PEAKS.json"
+    mp = json.loads(mp_path.read_text()) if mp_path.exists() else {}
+    peak = float(mp.get("bf16_tflops", 1590.0)) / 2
+    achieved = tensor_flops / (ms * 1e-3) / 1e12
+    line = {"metric": "permuted multilevel contraction chain (config 4), useful TFLOP/s",
+            "value": useful / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "n_gpus": 1, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32 (3xTF32 on tcgen05)",
+            "data": "synthetic N(0,1), seeded",
+            "config": {"workload": f"T=sum_ef A[a,e,c,f]B[f,b,e,d]; R=sum_bc T C[c,b]; all extents {E}",
+                       "extent": E, "l2": "inputs 4 x 64 MB + workspace 256 MB, above L2"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": None,
+                         "peak_source": "measured bf16_tflops / 2 (TF32 rate is half the bf16 rate)",
+                         "tensor_flops_per_step": tensor_flops},
+            "library_fp32": {"torch_fp32_ms": torch_ms, "speedup": torch_ms / ms,
+                             "rel_l2_vs_torch_fp32": rel},
+            "cpu_baseline": {"value": useful / cpu_s / 1e12, "unit": "TFLOP/s",
+                             "cores": os.cpu_count(), "kind": "port",
+                             "sample": "one chain in numpy float32 (host BLAS, all threads)"},
+            "gpu_launches": steps * 3, "clocks": clocks.summary()}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def config_dict(prob, world):
     nex, ney, nez = prob.mesh
     return {"workload": ("3D SEM isotropic elastic stiffness, NGLL=5, f32, structured "
@@ -252,6 +337,9 @@ def main():
     ap.add_argument("--variant", type=int, default=None,
                     help="f32 kernel variant (TO_SEM3D_VARIANT): 0 point-pair 8x2, 1 TMA 8x2, "
                          "2 streaming, 3 point-pair 4x4, 4 point-pair 16x1, 5 line-owner 8x3, 6 line-owner 4x5")
+    ap.add_argument("--workload", default="sem3d", choices=["sem3d", "chain"],
+                    help="sem3d: the headline SEM operator (default); chain: config 4 contraction")
+    ap.add_argument("--chain-extent", type=int, default=64)
     ap.add_argument("--mesh", type=int, nargs=3, default=[64, 64, 64],
                     metavar=("NEX", "NEY", "NEZ"), help="hexes per GPU (profiling runs)")
     args = ap.parse_args()
@@ -260,6 +348,8 @@ def main():
         os.environ["TO_SEM3D_VARIANT"] = str(args.variant)
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "chain":
+        return run_chain(args)
 
     import torch
     import torch.distributed as dist
