@@ -316,6 +316,77 @@ def run_chain(args):
     return 0
 
 
+def run_batched_gemm(args):
+    """Config 2: C[b] = A B[b], A 5x5 shared, B[b] 5x25, batch 65536, f32 and f64.
+
+    Printed with --workload batched-gemm.  HBM-bound (read B, write C once:
+    65.5 MB in f32); 100 back-to-back launches are captured in one CUDA graph
+    and the graph is replayed, so launch latency does not dominate a 10 us
+    kernel."""
+    import torch
+    from tensoroperations_b200 import abi
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    batch, M, N, reps = 65536, 5, 25, 100
+    rng = np.random.default_rng(2)
+    A = rng.standard_normal((M, M))
+    results = {}
+    peak, peak_src = measured_peak_hbm()
+    for name, tdt in (("f32", torch.float32), ("f64", torch.float64)):
+        g = torch.Generator(device=dev).manual_seed(3)
+        # four input / output sets rotate (>= 262 MB, twice L2) so no launch reads
+        # what an earlier one left in L2
+        nset = 4
+        Bs = [torch.randn((batch, M, N), generator=g, dtype=tdt, device=dev) for _ in range(nset)]
+        Cs = [torch.empty((batch, M, N), dtype=tdt, device=dev) for _ in range(nset)]
+        stream = torch.cuda.Stream(device=dev)
+        with torch.cuda.stream(stream):
+            for k in range(4):
+                abi.batched_small_gemm(A, Bs[k % nset], Cs[k % nset], stream=stream.cuda_stream)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for k in range(reps):
+                abi.batched_small_gemm(A, Bs[k % nset], Cs[k % nset],
+                                       stream=torch.cuda.current_stream().cuda_stream)
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (args.steps * reps)
+        nbytes = 2 * batch * M * N * Bs[0].element_size()
+        results[name] = {"us_per_launch": us, "gb_s": nbytes / (us * 1e-6) / 1e9,
+                         "frac": nbytes / (us * 1e-6) / 1e9 / peak, "bytes": nbytes}
+        del graph
+    # host baseline: numpy einsum over the batch, f32
+    Bn = rng.standard_normal((batch, M, N)).astype(np.float32)
+    t0 = time.perf_counter()
+    for _ in range(5):
+        np.matmul(A.astype(np.float32)[None], Bn)
+    cpu_us = (time.perf_counter() - t0) / 5 * 1e6
+    r = results["f32"]
+    line = {"metric": "batched small GEMM (config 2) GB/s", "value": r["gb_s"], "unit": "GB/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": 3, "ms_per_step": r["us_per_launch"] * 1e-3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic N(0,1), seeded",
+            "config": {"workload": "C[b] = A B[b], A 5x5 shared, B[b] 5x25, batch 65536",
+                       "graph": f"{reps} launches per CUDA graph, 4 input/output sets rotate (262 MB f32)"},
+            "roofline": {"bound": "hbm", "achieved": r["gb_s"], "peak": peak, "unit": "GB/s",
+                         "frac": r["frac"], "traffic": None, "peak_source": peak_src},
+            "f64": results["f64"],
+            "cpu_baseline": {"value": r["bytes"] / (cpu_us * 1e-6) / 1e9, "unit": "GB/s",
+                             "cores": os.cpu_count(), "kind": "port",
+                             "sample": "numpy matmul over the batch, f32, 5 runs"},
+            "gpu_launches": args.steps * reps}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def config_dict(prob, world):
     nex, ney, nez = prob.mesh
     return {"workload": ("3D SEM isotropic elastic stiffness, NGLL=5, f32, structured "
@@ -337,8 +408,9 @@ def main():
     ap.add_argument("--variant", type=int, default=None,
                     help="f32 kernel variant (TO_SEM3D_VARIANT): 0 point-pair 8x2, 1 TMA 8x2, "
                          "2 streaming, 3 point-pair 4x4, 4 point-pair 16x1, 5 line-owner 8x3, 6 line-owner 4x5")
-    ap.add_argument("--workload", default="sem3d", choices=["sem3d", "chain"],
-                    help="sem3d: the headline SEM operator (default); chain: config 4 contraction")
+    ap.add_argument("--workload", default="sem3d", choices=["sem3d", "chain", "batched-gemm"],
+                    help="sem3d: the headline SEM operator (default); chain: config 4 "
+                         "contraction; batched-gemm: config 2")
     ap.add_argument("--chain-extent", type=int, default=64)
     ap.add_argument("--mesh", type=int, nargs=3, default=[64, 64, 64],
                     metavar=("NEX", "NEY", "NEZ"), help="hexes per GPU (profiling runs)")
@@ -350,6 +422,8 @@ def main():
         return run_reference(args)
     if args.workload == "chain":
         return run_chain(args)
+    if args.workload == "batched-gemm":
+        return run_batched_gemm(args)
 
     import torch
     import torch.distributed as dist

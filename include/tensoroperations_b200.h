@@ -247,6 +247,21 @@ int to_scale3(int32_t dtype, void* const y[3], const void* const x[3], int64_t n
               const double* sumsq, void* stream);
 
 /* ---------------------------------------------------------------------- */
+/* Batched small GEMM with a shared left operand                           */
+/* ---------------------------------------------------------------------- */
+/*
+ *   C[b][i][j] = sum_k A[i][k] * B[b][k][j],  b < batch, i < M, k < K, j < N
+ * A: HOST double [M][K] (shared by every batch entry, converted to dtype);
+ * B: device [batch][K][N], C: device [batch][M][N], row-major, dtype TO_F32
+ * or TO_F64.  Built for (M, K) = (5, 5) and (8, 8), any N.  The batched form
+ * of one gradient contraction of the SEM operator (the reference's analogue:
+ * benchmarks/sem_stiffness/bench_sem_stiffness.cpp:884-896).  One kernel on
+ * `stream`.
+ */
+int to_batched_small_gemm(int32_t dtype, int32_t M, int32_t K, int32_t N, int64_t batch,
+                          const double* A, const void* B, void* C, void* stream);
+
+/* ---------------------------------------------------------------------- */
 /* Permuted multilevel contraction chain on the tensor cores               */
 /* ---------------------------------------------------------------------- */
 /*

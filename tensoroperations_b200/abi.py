@@ -97,6 +97,8 @@ _sig("to_sumsq3_noalloc", C.c_int, [C.c_int32, C.c_void_p, C.c_int64, C.c_int64,
                                     C.c_void_p])
 _sig("to_sumsq3_noalloc_max_n", C.c_int64, [])
 _sig("to_scale3", C.c_int, [C.c_int32, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p])
+_sig("to_batched_small_gemm", C.c_int, [C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int64,
+                                        C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p])
 _sig("to_chain_workspace_bytes", C.c_size_t, [C.c_int32])
 _sig("to_chain_f32", C.c_int, [C.c_int32] + [C.c_void_p] * 6 + [C.c_size_t, C.c_void_p])
 _sig("to_chain_flops", C.c_double, [C.c_int32])
@@ -207,6 +209,17 @@ def sumsq3_noalloc(dtype, x, first: int, n: int, result, stream: int = 0):
 def scale3(dtype, y, x, n: int, sumsq, stream: int = 0):
     """y[c][:n] = x[c][:n] / sqrt(sumsq[0]) on the device."""
     check(lib.to_scale3(_dcode(dtype), _fptrs(y), _fptrs(x), n, _ptr(sumsq), stream), "to_scale3")
+
+
+def batched_small_gemm(A, B, Cout, stream: int = 0):
+    """Cout[b] = A @ B[b] on the device; A is a host (M, K) array, B (batch, K, N)."""
+    Ah = np.ascontiguousarray(A, dtype=np.float64)
+    M, K = Ah.shape
+    batch, K2, N = B.shape
+    assert K2 == K and tuple(Cout.shape) == (batch, M, N)
+    code = TO_F64 if str(B.dtype).endswith("float64") else TO_F32
+    check(lib.to_batched_small_gemm(code, M, K, N, batch, Ah.ctypes.data, _ptr(B), _ptr(Cout), stream),
+          "to_batched_small_gemm")
 
 
 def chain_f32(E: int, A, B, Cm, R, workspace, T=None, stream: int = 0):
