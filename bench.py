@@ -387,6 +387,81 @@ def run_batched_gemm(args):
     return 0
 
 
+def run_large(args):
+    """Config 5: 128^3 hexes, NGLL 8, f64, z-slabs over the ranks (strong
+    scaling), 10 power-iteration steps u <- K u / ||K u|| timed.
+
+    Printed with --workload large.  Inputs are generated on the device (142 GB
+    on one GPU).  A step = one application (boundary layers, NCCL exchange of
+    the shared planes overlapped with the interior), the owner-counted sum of
+    squares, one NCCL all-reduce, the device-side rescale."""
+    import torch
+    import torch.distributed as dist
+    from tensoroperations_b200.slab import SlabOperator, SlabPartition, slab_problem_device
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    n = args.large_mesh
+    part = SlabPartition(n, n, n, 8, world, rank)
+    prob, u, f, arrays, ibool = slab_problem_device(part, np.float64, dev)
+    plan = prob.plan()
+    op = SlabOperator(part, plan, plan.fields(u, f, arrays, ibool), f, dev, u=u)
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 1)):
+            op.power_step(stream)
+    torch.cuda.synchronize()
+    steps = args.steps
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(gpu_id_for(dev)) as clocks:
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(steps):
+                op.power_step(stream)
+            e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t[0])
+    nelem = n ** 3
+    alg = plan.algorithmic_bytes()  # this rank's share
+    ta = torch.tensor([alg], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ta)
+    alg_total = float(ta[0])
+    peak, peak_src = measured_peak_hbm()
+    if rank == 0:
+        line = {"metric": "SEM stiffness Melem/s (config 5: 128^3, NGLL 8, f64, power iteration)",
+                "value": nelem / (ms * 1e-3) / 1e6, "unit": "Melem/s", "n_gpus": world,
+                "steps": steps, "warmup": args.warmup, "ms_per_step": ms,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
+                "data": "synthetic, generated on the device (same seeded streams as the host fill)",
+                "config": {"workload": f"{n}^3 hexes, NGLL 8, f64, assembled; 10-step u <- Ku/|Ku|",
+                           "parallelism": f"z-slabs x{world}", "nelem": nelem,
+                           "nglob": part.plane * (n * 7 + 1)},
+                "roofline": {"bound": "hbm", "achieved": alg_total / world / (ms * 1e-3) / 1e9,
+                             "peak": peak, "unit": "GB/s",
+                             "frac": alg_total / world / (ms * 1e-3) / 1e9 / peak, "traffic": None,
+                             "peak_source": peak_src, "algorithmic_bytes_per_step_all_ranks": alg_total},
+                "clocks": clocks.summary()}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def config_dict(prob, world):
     nex, ney, nez = prob.mesh
     return {"workload": ("3D SEM isotropic elastic stiffness, NGLL=5, f32, structured "
@@ -408,9 +483,10 @@ def main():
     ap.add_argument("--variant", type=int, default=None,
                     help="f32 kernel variant (TO_SEM3D_VARIANT): 0 point-pair 8x2, 1 TMA 8x2, "
                          "2 streaming, 3 point-pair 4x4, 4 point-pair 16x1, 5 line-owner 8x3, 6 line-owner 4x5")
-    ap.add_argument("--workload", default="sem3d", choices=["sem3d", "chain", "batched-gemm"],
+    ap.add_argument("--workload", default="sem3d", choices=["sem3d", "chain", "batched-gemm", "large"],
                     help="sem3d: the headline SEM operator (default); chain: config 4 "
-                         "contraction; batched-gemm: config 2")
+                         "contraction; batched-gemm: config 2; large: config 5")
+    ap.add_argument("--large-mesh", type=int, default=128, help="hexes per side for --workload large")
     ap.add_argument("--chain-extent", type=int, default=64)
     ap.add_argument("--mesh", type=int, nargs=3, default=[64, 64, 64],
                     metavar=("NEX", "NEY", "NEZ"), help="hexes per GPU (profiling runs)")
@@ -424,6 +500,8 @@ def main():
         return run_chain(args)
     if args.workload == "batched-gemm":
         return run_batched_gemm(args)
+    if args.workload == "large":
+        return run_large(args)
 
     import torch
     import torch.distributed as dist

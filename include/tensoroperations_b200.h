@@ -101,6 +101,17 @@ int to_synth_fill(void* dst, int32_t dtype, int64_t n, uint64_t seed,
 int to_synth_fill_at(void* dst, int32_t dtype, int64_t first, int64_t n, uint64_t seed,
                      int32_t dist, double a, double b);
 
+/* The same generators on the DEVICE, for problems too large for host memory:
+ * dst[i] = (element first + i of the sequence) + add, converted to dtype, and
+ * the structured numbering written to a device int32 buffer.  Uniform values
+ * equal the host's bit for bit; normal values use the device's log / cos.
+ * to_axpy2_device: y += 2 x (l2m = lambda + 2 mu in place).  Asynchronous. */
+int to_synth_fill_device(void* dst, int32_t dtype, int64_t first, int64_t n, uint64_t seed,
+                         int32_t dist, double a, double b, double add, void* stream);
+int to_axpy2_device(void* y, const void* x, int32_t dtype, int64_t n, void* stream);
+int to_mesh_structured_ibool_device(int32_t nex, int32_t ney, int32_t nez, int32_t ngll,
+                                    int32_t* ibool, void* stream);
+
 /* ---------------------------------------------------------------------- */
 /* SEM 3D isotropic-elastic stiffness operator                             */
 /* ---------------------------------------------------------------------- */

@@ -102,6 +102,10 @@ _sig("to_batched_small_gemm", C.c_int, [C.c_int32, C.c_int32, C.c_int32, C.c_int
 _sig("to_chain_workspace_bytes", C.c_size_t, [C.c_int32])
 _sig("to_chain_f32", C.c_int, [C.c_int32] + [C.c_void_p] * 6 + [C.c_size_t, C.c_void_p])
 _sig("to_chain_flops", C.c_double, [C.c_int32])
+_sig("to_synth_fill_device", C.c_int, [C.c_void_p, C.c_int32, C.c_int64, C.c_int64, C.c_uint64,
+                                       C.c_int32, C.c_double, C.c_double, C.c_double, C.c_void_p])
+_sig("to_axpy2_device", C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int64, C.c_void_p])
+_sig("to_mesh_structured_ibool_device", C.c_int, [C.c_int32] * 4 + [C.c_void_p, C.c_void_p])
 _sig("to_sem3d_plan_create", C.c_int, [C.POINTER(Sem3dDesc), C.POINTER(C.c_void_p)])
 _sig("to_sem3d_plan_destroy", C.c_int, [C.c_void_p])
 _sig("to_sem3d_apply", C.c_int, [C.c_void_p, C.POINTER(Sem3dFields), C.c_int32, C.c_void_p])

@@ -139,6 +139,56 @@ def slab_problem(part: SlabPartition, dtype=np.float32, seed: int = DEFAULT_SEED
                         (part.nex, part.ney, part.nez_local))
 
 
+def slab_problem_device(part: SlabPartition, dtype, device, seed: int = DEFAULT_SEED,
+                        stream: int = 0):
+    """slab_problem generated directly in device memory (no host arrays).
+
+    Returns (problem, u, f, arrays, ibool): the problem carries the operators
+    and sizes only (its host arrays are empty); the tensors are on `device`.
+    Uniform inputs equal slab_problem's bit for bit; u (normal) may differ in
+    the last bits (device log / cos)."""
+    import torch
+    dt = np.dtype(dtype)
+    code = abi.TO_F32 if dt == np.float32 else abi.TO_F64
+    tdt = torch.float32 if dt == np.float32 else torch.float64
+    N = part.ngll
+    P = N ** 3
+    npts = part.nelem * P
+    first = part.elem_first * P
+    _, w, H, Hw = abi.gll_operators(N)
+
+    def fill(t, seed_, dist, a, b, add=0.0, first_=first):
+        abi.check(abi.lib.to_synth_fill_device(t.data_ptr(), code, first_, t.numel(), seed_, dist,
+                                                a, b, add, stream), "to_synth_fill_device")
+
+    arrays = {}
+    for r, name in enumerate(abi.POINT_ARRAYS[:9]):
+        t = torch.empty(npts, dtype=tdt, device=device)
+        fill(t, seed + 3 + r, 0, 0.5, 1.5, 1.0 if name in ("xix", "etay", "gamz") else 0.0)
+        arrays[name] = t
+    arrays["jac"] = torch.empty(npts, dtype=tdt, device=device)
+    fill(arrays["jac"], seed + 12, 0, 0.5, 2.0)
+    arrays["l2m"] = torch.empty(npts, dtype=tdt, device=device)
+    fill(arrays["l2m"], seed + 13, 0, 1.0, 3.0)  # lambda, then + 2 mu in place
+    arrays["mu"] = torch.empty(npts, dtype=tdt, device=device)
+    fill(arrays["mu"], seed + 14, 0, 0.5, 2.0)
+    abi.check(abi.lib.to_axpy2_device(arrays["l2m"].data_ptr(), arrays["mu"].data_ptr(), code, npts,
+                                      stream), "to_axpy2_device")
+    ibool = torch.empty(npts, dtype=torch.int32, device=device)
+    abi.check(abi.lib.to_mesh_structured_ibool_device(part.nex, part.ney, part.nez_local, N,
+                                                      ibool.data_ptr(), stream),
+              "to_mesh_structured_ibool_device")
+    u = []
+    for c in range(3):
+        t = torch.empty(part.nglob, dtype=tdt, device=device)
+        fill(t, seed + c, 1, 0.0, 1.0, first_=part.node_first)
+        u.append(t)
+    f = [torch.zeros(part.nglob, dtype=tdt, device=device) for _ in range(3)]
+    prob = Sem3dProblem(N, part.nelem, dt, H, Hw, w, {}, [], np.empty(0, np.int32), part.nglob,
+                        (part.nex, part.ney, part.nez_local))
+    return prob, u, f, arrays, ibool
+
+
 def exchange_planes(part: SlabPartition, sends, recvs, group=None):
     """Send sends[i] to and receive recvs[i] from neighbour i of part.interfaces().
 

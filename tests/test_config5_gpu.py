@@ -99,3 +99,22 @@ def test_power_iteration_single_gpu(ngll):
     ref = _oracle_power(structured_problem(3, 2, 3, ngll=ngll, dtype=np.float64, assembled=True,
                                            seed=55), 4)
     assert osem.rel_l2([x.cpu().numpy() for x in u], ref) < 1e-12
+
+
+@pytest.mark.parametrize("dtype,ngll,world,rank", [(np.float64, 8, 3, 1), (np.float32, 5, 2, 0)])
+def test_device_generated_slab_matches_host(dtype, ngll, world, rank):
+    """slab_problem_device == slab_problem: uniform arrays and ibool bit for bit,
+    u (normal: device log / cos) to 1e-14."""
+    torch = _torch()
+    from tensoroperations_b200.slab import slab_problem_device
+    part = SlabPartition(3, 2, 4, ngll, world, rank)
+    host = slab_problem(part, dtype, 91)
+    prob, u, f, arrays, ibool = slab_problem_device(part, dtype, "cuda", 91)
+    torch.cuda.synchronize()
+    for name, a in host.arrays.items():
+        assert np.array_equal(arrays[name].cpu().numpy(), a), name
+    assert np.array_equal(ibool.cpu().numpy(), host.ibool)
+    for c in range(3):
+        got = u[c].cpu().numpy()
+        assert np.max(np.abs(got - host.u[c])) <= 1e-6 * (np.max(np.abs(host.u[c])) if dtype == np.float32 else 1e-8)
+    assert prob.nglob == host.nglob and prob.nelem == host.nelem
