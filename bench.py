@@ -462,6 +462,79 @@ def run_large(args):
     return 0
 
 
+def run_sem2d(args):
+    """The reference's 2D benchmark operator: elastic P-SV, NGLL 8, f32,
+    element-local, E = 2,621,440 elements (7.4 GB moved per application).
+
+    Printed with --workload sem2d.  Inputs generated on the device (seeded
+    streams, the 3D configuration's distributions).  Algorithmic bytes per
+    element: 9 input arrays + 2 outputs, 64 points each, 4 B."""
+    import torch
+    from tensoroperations_b200 import abi
+    from tensoroperations_b200.sem2d import ARRAYS
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    E = args.sem2d_elements
+    npts = E * 64
+    _, w, H, Hw = abi.gll_operators(8)
+
+    def gen(seed, dist, a, b, add=0.0):
+        t = torch.empty(npts, dtype=torch.float32, device=dev)
+        abi.check(abi.lib.to_synth_fill_device(t.data_ptr(), abi.TO_F32, 0, npts, seed, dist, a, b,
+                                                add, 0), "to_synth_fill_device")
+        return t
+    seed = 0x2D5EED
+    arrays = {"xix": gen(seed + 3, 0, 0.5, 1.5, 1.0), "xiz": gen(seed + 4, 0, 0.5, 1.5),
+              "gamx": gen(seed + 5, 0, 0.5, 1.5), "gamz": gen(seed + 6, 0, 0.5, 1.5, 1.0),
+              "jac": gen(seed + 12, 0, 0.5, 2.0), "l2m": gen(seed + 13, 0, 1.0, 3.0),
+              "mu": gen(seed + 14, 0, 0.5, 2.0)}
+    abi.check(abi.lib.to_axpy2_device(arrays["l2m"].data_ptr(), arrays["mu"].data_ptr(), abi.TO_F32,
+                                      npts, 0), "to_axpy2_device")
+    u = [gen(seed + c, 1, 0.0, 1.0) for c in range(2)]
+    f = [torch.empty(npts, dtype=torch.float32, device=dev) for _ in range(2)]
+    stream = torch.cuda.Stream(device=dev)
+    s = stream.cuda_stream
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            abi.sem2d_elastic_local(8, E, H, Hw, w, u, f, arrays, stream=s)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpu_id_for(dev)) as clocks:
+        e0.record(stream)
+        for _ in range(args.steps):
+            abi.sem2d_elastic_local(8, E, H, Hw, w, u, f, arrays, stream=s)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    alg = E * 64 * 4 * 11.0
+    peak, peak_src = measured_peak_hbm()
+    # CPU: the restated host loop (one thread) on a bounded sample
+    from oracle import sem as osem
+    from tensoroperations_b200.sem2d import synthetic_2d
+    ns = 20000
+    us, arr, Hh, Hwh, wh = synthetic_2d(ns)
+    t0 = time.perf_counter()
+    osem.sem2d_local(ns, 8, us, arr, Hh.astype(np.float32), Hwh.astype(np.float32),
+                     wh.astype(np.float32), np.float32)
+    cpu_s = time.perf_counter() - t0
+    line = {"metric": "SEM 2D elastic P-SV stiffness Melem/s (NGLL 8, f32, element-local)",
+            "value": E / (ms * 1e-3) / 1e6, "unit": "Melem/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic, generated on the device",
+            "config": {"workload": f"2D elastic P-SV, NGLL 8, {E} elements, element-local",
+                       "l2": f"{alg / 1e9:.1f} GB per application, no flush needed"},
+            "roofline": {"bound": "hbm", "achieved": alg / (ms * 1e-3) / 1e9, "peak": peak,
+                         "unit": "GB/s", "frac": alg / (ms * 1e-3) / 1e9 / peak, "traffic": None,
+                         "peak_source": peak_src, "algorithmic_bytes_per_launch": alg},
+            "cpu_baseline": {"value": ns / cpu_s / 1e6, "unit": "Melem/s", "cores": 1,
+                             "kind": "port",
+                             "sample": f"{ns} elements through the restated host loop "
+                                       "(bench_sem_stiffness.cpp:1335-1385), one thread"},
+            "gpu_launches": args.steps, "clocks": clocks.summary()}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def config_dict(prob, world):
     nex, ney, nez = prob.mesh
     return {"workload": ("3D SEM isotropic elastic stiffness, NGLL=5, f32, structured "
@@ -483,9 +556,12 @@ def main():
     ap.add_argument("--variant", type=int, default=None,
                     help="f32 kernel variant (TO_SEM3D_VARIANT): 0 point-pair 8x2, 1 TMA 8x2, "
                          "2 streaming, 3 point-pair 4x4, 4 point-pair 16x1, 5 line-owner 8x3, 6 line-owner 4x5")
-    ap.add_argument("--workload", default="sem3d", choices=["sem3d", "chain", "batched-gemm", "large"],
+    ap.add_argument("--workload", default="sem3d",
+                    choices=["sem3d", "chain", "batched-gemm", "large", "sem2d"],
                     help="sem3d: the headline SEM operator (default); chain: config 4 "
-                         "contraction; batched-gemm: config 2; large: config 5")
+                         "contraction; batched-gemm: config 2; large: config 5; sem2d: the "
+                         "reference's 2D elastic operator")
+    ap.add_argument("--sem2d-elements", type=int, default=2621440)
     ap.add_argument("--large-mesh", type=int, default=128, help="hexes per side for --workload large")
     ap.add_argument("--chain-extent", type=int, default=64)
     ap.add_argument("--mesh", type=int, nargs=3, default=[64, 64, 64],
@@ -502,6 +578,8 @@ def main():
         return run_batched_gemm(args)
     if args.workload == "large":
         return run_large(args)
+    if args.workload == "sem2d":
+        return run_sem2d(args)
 
     import torch
     import torch.distributed as dist

@@ -258,6 +258,31 @@ int to_scale3(int32_t dtype, void* const y[3], const void* const x[3], int64_t n
               const double* sumsq, void* stream);
 
 /* ---------------------------------------------------------------------- */
+/* SEM 2D elastic P-SV stiffness operator (element-local)                  */
+/* ---------------------------------------------------------------------- */
+/*
+ * The operator of the reference's 2D benchmark
+ * (benchmarks/sem_stiffness/bench_sem_stiffness.cpp: physics :319-357, host
+ * loop :1335-1385), f32, NGLL 8, two components, element-local:
+ *   a_c = sum_p H(i,p) u_c(j,p),  g_c = sum_p H(j,p) u_c(p,i)
+ *   ds = grad u through (xix, xiz, gamx, gamz); sigma = isotropic P-SV stress
+ *   Fx_c = jac (s_c0 xix + s_c1 xiz),  Fg_c = jac (s_c0 gamx + s_c1 gamz)
+ *   f_c(j,i) = w_j sum_q Hw(q,i) Fx_c(j,q) + w_i sum_q Hw(q,j) Fg_c(q,i)
+ * Per-point arrays [E][j][i] (i fastest), 16-byte aligned device pointers.
+ * H, Hw, w: HOST doubles ([8][8], [8][8], [8]).  f is overwritten.
+ */
+typedef struct to_sem2d_fields {
+  const void* u[2];
+  void* f[2];
+  const void* xix; const void* xiz; const void* gamx; const void* gamz;
+  const void* jac; const void* l2m; const void* mu;
+} to_sem2d_fields;
+
+int to_sem2d_elastic_local(int32_t ngll, int64_t nelem, const double* hprime,
+                           const double* hprimewgll, const double* wgll,
+                           const to_sem2d_fields* fields, void* stream);
+
+/* ---------------------------------------------------------------------- */
 /* Batched small GEMM with a shared left operand                           */
 /* ---------------------------------------------------------------------- */
 /*

@@ -63,6 +63,23 @@ def assembled(nelem, ngll, nglob, ibool, u, arrays, H, Hw, w, dtype):
     return f
 
 
+SEM2D_POINT_ORDER = ("xix", "xiz", "gamx", "gamz", "jac", "l2m", "mu")
+
+
+def sem2d_local(nelem, ngll, u, arrays, H, Hw, w, dtype):
+    """2D elastic P-SV element-local operator: u[c] and the result are [E*N^2] (c = 0, 1)."""
+    dt = np.dtype(dtype)
+    m = [np.ascontiguousarray(arrays[n], dtype=dt) for n in SEM2D_POINT_ORDER]
+    uu = [np.ascontiguousarray(x, dtype=dt) for x in u]
+    f = [np.zeros(nelem * ngll * ngll, dtype=dt) for _ in range(2)]
+    ops = [np.ascontiguousarray(x, dtype=dt) for x in (H, Hw, w)]
+    name = "oracle_sem2d_local_f32" if dt == np.float32 else "oracle_sem2d_local_f64"
+    _cfun(_exact, name)(C.c_int64(nelem), C.c_int(ngll), _pp(uu), _pp(m),
+                        ops[0].ctypes.data_as(C.c_void_p), ops[1].ctypes.data_as(C.c_void_p),
+                        ops[2].ctypes.data_as(C.c_void_p), _pp(f))
+    return f
+
+
 def colouring(nelem, ngll, nglob, ibool):
     """(ncolours, colour_start[ncol+1], colour_elems[E]) of a greedy element colouring."""
     col = np.empty(nelem, dtype=np.int32)

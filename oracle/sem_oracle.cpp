@@ -175,7 +175,69 @@ void sem3d_assembled_omp(int64_t E, int N, int64_t nglob, const int32_t* ibool,
 
 }  // namespace
 
+// 2D elastic P-SV, element-local, the reference's host loop restated
+// (benchmarks/sem_stiffness/bench_sem_stiffness.cpp:1335-1385, compute_stress
+// :319-331): gradients with sums over p in order, chain rule, stress,
+// integrands, then divergences with sums over q in order and the weighted sum.
+// m = {xix, xiz, gamx, gamz, jac, l2m, mu}; arrays [E][j][i].
+template <typename T>
+void sem2d_local(int64_t E, int N, const T* const* u, const T* const* m, const T* H,
+                 const T* Hw, const T* w, T* const* f) {
+  const int P = N * N;
+  std::vector<T> Fx0(P), Fg0(P), Fx1(P), Fg1(P);
+  for (int64_t e = 0; e < E; ++e) {
+    const T* U0 = u[0] + e * P;
+    const T* U1 = u[1] + e * P;
+    for (int j = 0; j < N; ++j)
+      for (int i = 0; i < N; ++i) {
+        T a0 = 0, a1 = 0, g0 = 0, g1 = 0;
+        for (int p = 0; p < N; ++p) {
+          a0 += H[i * N + p] * U0[j * N + p];
+          a1 += H[i * N + p] * U1[j * N + p];
+          g0 += H[j * N + p] * U0[p * N + i];
+          g1 += H[j * N + p] * U1[p * N + i];
+        }
+        const int64_t q = e * P + j * N + i;
+        const T ax = m[0][q], az = m[1][q], px = m[2][q], pz = m[3][q];
+        const T jac = m[4][q], l2m = m[5][q], mu = m[6][q];
+        const T ds00 = a0 * ax + g0 * px, ds01 = a0 * az + g0 * pz;
+        const T ds10 = a1 * ax + g1 * px, ds11 = a1 * az + g1 * pz;
+        const T lambda = l2m - T(2) * mu;
+        const T s00 = l2m * ds00 + lambda * ds11;
+        const T s11 = lambda * ds00 + l2m * ds11;
+        const T s01 = mu * (ds01 + ds10);
+        const T s10 = s01;
+        Fx0[j * N + i] = jac * (s00 * ax + s01 * az);
+        Fg0[j * N + i] = jac * (s00 * px + s01 * pz);
+        Fx1[j * N + i] = jac * (s10 * ax + s11 * az);
+        Fg1[j * N + i] = jac * (s10 * px + s11 * pz);
+      }
+    for (int j = 0; j < N; ++j)
+      for (int i = 0; i < N; ++i) {
+        T s0 = 0, s1 = 0, t0 = 0, t1 = 0;
+        for (int q = 0; q < N; ++q) {
+          s0 += Hw[q * N + i] * Fx0[j * N + q];
+          s1 += Hw[q * N + i] * Fx1[j * N + q];
+          t0 += Hw[q * N + j] * Fg0[q * N + i];
+          t1 += Hw[q * N + j] * Fg1[q * N + i];
+        }
+        f[0][e * P + j * N + i] = w[j] * s0 + w[i] * t0;
+        f[1][e * P + j * N + i] = w[j] * s1 + w[i] * t1;
+      }
+  }
+}
+
 extern "C" {
+
+void oracle_sem2d_local_f32(int64_t E, int N, const float* const* u, const float* const* m,
+                            const float* H, const float* Hw, const float* w, float* const* f) {
+  sem2d_local<float>(E, N, u, m, H, Hw, w, f);
+}
+void oracle_sem2d_local_f64(int64_t E, int N, const double* const* u, const double* const* m,
+                            const double* H, const double* Hw, const double* w, double* const* f) {
+  sem2d_local<double>(E, N, u, m, H, Hw, w, f);
+}
+
 
 int oracle_num_threads(void) {
 #ifdef _OPENMP

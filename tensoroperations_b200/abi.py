@@ -66,6 +66,14 @@ class Sem3dFields(C.Structure):
         [(n, C.c_void_p) for n in POINT_ARRAYS]
 
 
+class Sem2dFields(C.Structure):
+    _fields_ = [("u", C.c_void_p * 2), ("f", C.c_void_p * 2)] + \
+        [(n, C.c_void_p) for n in ("xix", "xiz", "gamx", "gamz", "jac", "l2m", "mu")]
+
+
+SEM2D_ARRAYS = ("xix", "xiz", "gamx", "gamz", "jac", "l2m", "mu")
+
+
 def _sig(name, restype, argtypes):
     fn = getattr(lib, name)
     fn.restype = restype
@@ -97,6 +105,8 @@ _sig("to_sumsq3_noalloc", C.c_int, [C.c_int32, C.c_void_p, C.c_int64, C.c_int64,
                                     C.c_void_p])
 _sig("to_sumsq3_noalloc_max_n", C.c_int64, [])
 _sig("to_scale3", C.c_int, [C.c_int32, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p])
+_sig("to_sem2d_elastic_local", C.c_int, [C.c_int32, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p,
+                                         C.POINTER(Sem2dFields), C.c_void_p])
 _sig("to_batched_small_gemm", C.c_int, [C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int64,
                                         C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p])
 _sig("to_chain_workspace_bytes", C.c_size_t, [C.c_int32])
@@ -213,6 +223,20 @@ def sumsq3_noalloc(dtype, x, first: int, n: int, result, stream: int = 0):
 def scale3(dtype, y, x, n: int, sumsq, stream: int = 0):
     """y[c][:n] = x[c][:n] / sqrt(sumsq[0]) on the device."""
     check(lib.to_scale3(_dcode(dtype), _fptrs(y), _fptrs(x), n, _ptr(sumsq), stream), "to_scale3")
+
+
+def sem2d_elastic_local(ngll: int, nelem: int, H, Hw, w, u, f, arrays, stream: int = 0):
+    """f[c] = K u (2D elastic P-SV, element-local) on the device; H, Hw, w host arrays."""
+    ops = [np.ascontiguousarray(x, dtype=np.float64) for x in (H, Hw, w)]
+    fl = Sem2dFields()
+    for c in range(2):
+        fl.u[c] = _ptr(u[c])
+        fl.f[c] = _ptr(f[c])
+    for n in SEM2D_ARRAYS:
+        setattr(fl, n, _ptr(arrays[n]))
+    check(lib.to_sem2d_elastic_local(ngll, nelem, ops[0].ctypes.data, ops[1].ctypes.data,
+                                     ops[2].ctypes.data, C.byref(fl), stream),
+          "to_sem2d_elastic_local")
 
 
 def batched_small_gemm(A, B, Cout, stream: int = 0):
