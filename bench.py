@@ -74,7 +74,12 @@ def measured_peak_hbm():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms in the background."""
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms in the background.
+
+    Start it before the warm-up (nvidia-smi needs a moment to start); mark the
+    timed region with begin() / end(); summary() keeps the samples taken inside
+    it, or -- when the region was shorter than the sampling interval -- the
+    samples of the warm-up and the region together, and says which."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -83,7 +88,8 @@ class ClockSampler:
     def __init__(self, gpu_id: str):
         self.gpu_id = gpu_id
         self.proc = None
-        self.lines = []
+        self.lines = []  # (host time, line)
+        self.t0 = self.t1 = None
 
     def __enter__(self):
         try:
@@ -99,7 +105,19 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.time(), line.strip()))
+
+    def wait_first(self, timeout: float = 3.0):
+        """Block until nvidia-smi has produced a sample (or timeout)."""
+        t_end = time.time() + timeout
+        while self.proc is not None and not self.lines and time.time() < t_end:
+            time.sleep(0.02)
+
+    def begin(self):
+        self.t0 = time.time()
+
+    def end(self):
+        self.t1 = time.time()
 
     def __exit__(self, *exc):
         if self.proc is not None:
@@ -111,9 +129,15 @@ class ClockSampler:
             self.t.join(timeout=2)
 
     def summary(self):
+        inside = [ln for t, ln in self.lines
+                  if self.t0 is None or (self.t0 <= t <= (self.t1 or t))]
+        window = "timed region"
+        if not inside:
+            inside = [ln for _, ln in self.lines]
+            window = "warm-up and timed region (timed region shorter than the 200 ms interval)"
         sm, smax, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in inside:
             parts = [x.strip() for x in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -128,7 +152,7 @@ class ClockSampler:
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax),
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "window": window}
 
 
 def gpu_id_for(dev) -> str:
@@ -603,6 +627,9 @@ def main():
     fields = plan.fields(u, f, arrays, ibool)
     op = SlabOperator(part, plan, fields, f, dev)
 
+    clocks = ClockSampler(gpu_id_for(dev))
+    clocks.__enter__()
+    clocks.wait_first()
     with torch.cuda.stream(stream):
         for _ in range(max(args.warmup, 3)):
             op.apply(stream)
@@ -616,13 +643,15 @@ def main():
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    with ClockSampler(gpu_id_for(dev)) as clocks:
-        with torch.cuda.stream(stream):
-            e_start.record(stream)
-            for it in range(args.steps):
-                op.apply(stream, (kstarts[it], kends[it]))
-            e_end.record(stream)
-        torch.cuda.synchronize()
+    clocks.begin()
+    with torch.cuda.stream(stream):
+        e_start.record(stream)
+        for it in range(args.steps):
+            op.apply(stream, (kstarts[it], kends[it]))
+        e_end.record(stream)
+    torch.cuda.synchronize()
+    clocks.end()
+    clocks.__exit__(None, None, None)
     if world > 1:
         dist.barrier()
     total_ms = e_start.elapsed_time(e_end)
