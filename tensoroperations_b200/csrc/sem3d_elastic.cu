@@ -16,6 +16,7 @@ __device__ int g_to_device_status = 0;
 #include "sem3d_elastic_tma.cuh"
 #include "sem3d_elastic_v3.cuh"
 #include "sem3d_elastic_v5.cuh"
+#include "sem3d_elastic_lo.cuh"
 
 struct to_sem3d_plan {
   to_sem3d_desc desc;
@@ -206,6 +207,26 @@ int launch_v5(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t
   return ok();
 }
 
+// The line-owner kernel with geometry from global memory (NGLL 8).
+template <typename T, int N, int EB, int MINB, bool ASM>
+int launch_lo(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t stream,
+              int dev, int sms) {
+  constexpr int NT = EB * N * N;
+  const size_t smem = Sem3dLoLayout<T, N, EB>::kTotal;
+  auto kernel = sem3d_elastic_lo_kernel<T, N, EB, MINB, ASM>;
+  static KernelSlot slot;
+  int nb = 0;
+  if (int st = configure(slot, kernel, dev, NT, smem, &nb)) return st;
+  Sem3dArgs<T, N> a = make_args<T, N>(plan, fl);
+  a.prefetch = staged_arrays_aligned(fl, ASM) ? 1 : 0;
+  const long long nbatch = (plan->desc.nelem + EB - 1) / EB;
+  const long long cap = static_cast<long long>(sms) * nb;
+  const int grid = static_cast<int>(nbatch < cap ? nbatch : cap);
+  kernel<<<grid, NT, smem, stream>>>(a);
+  TO_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
 // Kernel variant for f32 NGLL 5 (TO_SEM3D_VARIANT; default 5):
 //   0 point-pair pipelined kernel, 8 elements x 2 CTAs/SM
 //   1 TMA-staged kernel, 8 elements x 2 CTAs/SM
@@ -237,6 +258,12 @@ int launch_sem3d(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStrea
       if (v == 0) return launch_v3<N, 8, 2, ASM>(plan, fl, stream, dev, sms);
       return launch_v5<8, ASM ? 3 : 2, ASM>(plan, fl, stream, dev, sms);
     }
+  }
+  if constexpr (N == 8) {
+    // NGLL 8 (f32 and f64): the line-owner kernel; TO_SEM3D_VARIANT=2 keeps
+    // the streaming kernel
+    if (sem3d_f32_variant() != 2)
+      return launch_lo<T, N, 2, sizeof(T) == 8 ? 2 : 3, ASM>(plan, fl, stream, dev, sms);
   }
   return launch_ldg<T, N, ASM>(plan, fl, stream, dev, sms);
 }
