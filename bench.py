@@ -559,6 +559,58 @@ def run_sem2d(args):
     return 0
 
 
+def run_acoustic2d(args):
+    """Config 1: 2D acoustic stiffness, fp64, NGLL 5, 128 x 128 quads, assembled.
+
+    Printed with --workload acoustic2d.  The problem (29 MB) is launch-bound on
+    a B200; the reference runs it on the host, so the CPU baseline (the oracle
+    restatement, one thread) is the comparison that matters here."""
+    import torch
+    from oracle import sem as osem
+    from tensoroperations_b200 import abi
+    from tensoroperations_b200.sem2d import acoustic_problem
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    uh, arrays, ibool, nglob, H, Hw, w = acoustic_problem()
+    E = len(ibool) // 25
+    du = torch.from_numpy(uh).to(dev)
+    da = {k: torch.from_numpy(v).to(dev) for k, v in arrays.items()}
+    dib = torch.from_numpy(ibool).to(dev)
+    f = torch.empty(nglob, dtype=torch.float64, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    s = stream.cuda_stream
+    for _ in range(max(args.warmup, 3)):
+        abi.sem2d_acoustic_apply(5, E, nglob, H, Hw, w, du, f, dib, da, np.float64, stream=s)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        abi.sem2d_acoustic_apply(5, E, nglob, H, Hw, w, du, f, dib, da, np.float64, stream=s)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    alg = E * 25 * (6 * 8 + 4) + nglob * 8 * 2
+    t0 = time.perf_counter()
+    for _ in range(3):
+        osem.sem2d_acoustic(E, 5, nglob, ibool, uh, arrays, H, Hw, w, np.float64)
+    cpu_s = (time.perf_counter() - t0) / 3
+    peak, peak_src = measured_peak_hbm()
+    line = {"metric": "SEM 2D acoustic stiffness Melem/s (config 1: 128x128, NGLL 5, f64)",
+            "value": E / (ms * 1e-3) / 1e6, "unit": "Melem/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f64", "data": "synthetic, seeded",
+            "config": {"workload": "2D acoustic, 128x128 quads, NGLL 5, f64, assembled (513^2 nodes)",
+                       "note": "29 MB per application: launch-bound on the GPU"},
+            "roofline": {"bound": "hbm", "achieved": alg / (ms * 1e-3) / 1e9, "peak": peak,
+                         "unit": "GB/s", "frac": alg / (ms * 1e-3) / 1e9 / peak, "traffic": None,
+                         "peak_source": peak_src, "algorithmic_bytes_per_launch": alg},
+            "cpu_baseline": {"value": E / cpu_s / 1e6, "unit": "Melem/s", "cores": 1, "kind": "port",
+                             "sample": "the full 128x128 problem through the oracle restatement, one thread, 3 runs"},
+            "gpu_launches": args.steps}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def config_dict(prob, world):
     nex, ney, nez = prob.mesh
     return {"workload": ("3D SEM isotropic elastic stiffness, NGLL=5, f32, structured "
@@ -581,10 +633,10 @@ def main():
                     help="f32 kernel variant (TO_SEM3D_VARIANT): 0 point-pair 8x2, 1 TMA 8x2, "
                          "2 streaming, 3 point-pair 4x4, 4 point-pair 16x1, 5 line-owner 8x3, 6 line-owner 4x5")
     ap.add_argument("--workload", default="sem3d",
-                    choices=["sem3d", "chain", "batched-gemm", "large", "sem2d"],
+                    choices=["sem3d", "chain", "batched-gemm", "large", "sem2d", "acoustic2d"],
                     help="sem3d: the headline SEM operator (default); chain: config 4 "
                          "contraction; batched-gemm: config 2; large: config 5; sem2d: the "
-                         "reference's 2D elastic operator")
+                         "reference's 2D elastic operator; acoustic2d: config 1")
     ap.add_argument("--sem2d-elements", type=int, default=2621440)
     ap.add_argument("--large-mesh", type=int, default=128, help="hexes per side for --workload large")
     ap.add_argument("--chain-extent", type=int, default=64)
@@ -604,6 +656,8 @@ def main():
         return run_large(args)
     if args.workload == "sem2d":
         return run_sem2d(args)
+    if args.workload == "acoustic2d":
+        return run_acoustic2d(args)
 
     import torch
     import torch.distributed as dist

@@ -283,6 +283,33 @@ int to_sem2d_elastic_local(int32_t ngll, int64_t nelem, const double* hprime,
                            const to_sem2d_fields* fields, void* stream);
 
 /* ---------------------------------------------------------------------- */
+/* SEM 2D acoustic stiffness operator (assembled)                          */
+/* ---------------------------------------------------------------------- */
+/*
+ * The scalar (acoustic) 2D operator of the first benchmark configuration;
+ * the reference has no acoustic kernel, so this is the configuration's own
+ * definition:
+ *   dxi = sum_p H(i,p) u(j,p),  dgm = sum_p H(j,p) u(p,i)   (u gathered by ibool)
+ *   du/dx = dxi xix + dgm gamx,  du/dz = dxi xiz + dgm gamz
+ *   Fx = jac/rho (du/dx xix + du/dz xiz),  Fg = jac/rho (du/dx gamx + du/dz gamz)
+ *   f(ibool(j,i)) += w_j sum_q Hw(q,i) Fx(j,q) + w_i sum_q Hw(q,j) Fg(q,i)
+ * Per-point arrays [E][j][i]; u, f [nglob]; with accumulate == 0 f is zeroed
+ * first.  NGLL 5, f64 or f32.  (kappa belongs to the mass matrix, not here.)
+ */
+typedef struct to_sem2d_acoustic_desc {
+  int32_t dtype; int32_t ngll; int64_t nelem; int64_t nglob;
+  const double* hprime; const double* hprimewgll; const double* wgll;  /* HOST */
+} to_sem2d_acoustic_desc;
+typedef struct to_sem2d_acoustic_fields {
+  const void* u; void* f; const int32_t* ibool;
+  const void* xix; const void* xiz; const void* gamx; const void* gamz;
+  const void* jac; const void* rho;
+} to_sem2d_acoustic_fields;
+int to_sem2d_acoustic_apply(const to_sem2d_acoustic_desc* desc,
+                            const to_sem2d_acoustic_fields* fields, int32_t accumulate,
+                            void* stream);
+
+/* ---------------------------------------------------------------------- */
 /* Batched small GEMM with a shared left operand                           */
 /* ---------------------------------------------------------------------- */
 /*

@@ -80,6 +80,25 @@ def sem2d_local(nelem, ngll, u, arrays, H, Hw, w, dtype):
     return f
 
 
+ACOUSTIC_ORDER = ("xix", "xiz", "gamx", "gamz", "jac", "rho")
+
+
+def sem2d_acoustic(nelem, ngll, nglob, ibool, u, arrays, H, Hw, w, dtype):
+    """2D acoustic assembled operator (scalar u[nglob] -> f[nglob])."""
+    dt = np.dtype(dtype)
+    m = [np.ascontiguousarray(arrays[n], dtype=dt) for n in ACOUSTIC_ORDER]
+    uu = np.ascontiguousarray(u, dtype=dt)
+    f = np.zeros(nglob, dtype=dt)
+    ib = np.ascontiguousarray(ibool, dtype=np.int32)
+    ops = [np.ascontiguousarray(x, dtype=dt) for x in (H, Hw, w)]
+    name = "oracle_sem2d_acoustic_f64" if dt == np.float64 else "oracle_sem2d_acoustic_f32"
+    _cfun(_exact, name)(C.c_int64(nelem), C.c_int(ngll), C.c_int64(nglob),
+                        ib.ctypes.data_as(C.c_void_p), uu.ctypes.data_as(C.c_void_p), _pp(m),
+                        ops[0].ctypes.data_as(C.c_void_p), ops[1].ctypes.data_as(C.c_void_p),
+                        ops[2].ctypes.data_as(C.c_void_p), f.ctypes.data_as(C.c_void_p))
+    return f
+
+
 def colouring(nelem, ngll, nglob, ibool):
     """(ncolours, colour_start[ncol+1], colour_elems[E]) of a greedy element colouring."""
     col = np.empty(nelem, dtype=np.int32)

@@ -227,7 +227,55 @@ void sem2d_local(int64_t E, int N, const T* const* u, const T* const* m, const T
   }
 }
 
+// 2D acoustic, assembled (the first configuration's operator; no reference
+// kernel exists -- same definition as to_sem2d_acoustic_apply).
+// m = {xix, xiz, gamx, gamz, jac, rho}.
+template <typename T>
+void sem2d_acoustic(int64_t E, int N, int64_t nglob, const int32_t* ibool, const T* u,
+                    const T* const* m, const T* H, const T* Hw, const T* w, T* f) {
+  const int P = N * N;
+  std::vector<T> ul(P), Fx(P), Fg(P);
+  for (int64_t g = 0; g < nglob; ++g) f[g] = T(0);
+  for (int64_t e = 0; e < E; ++e) {
+    for (int p = 0; p < P; ++p) ul[p] = u[ibool[e * P + p]];
+    for (int j = 0; j < N; ++j)
+      for (int i = 0; i < N; ++i) {
+        T dxi = 0, dgm = 0;
+        for (int p = 0; p < N; ++p) {
+          dxi += H[i * N + p] * ul[j * N + p];
+          dgm += H[j * N + p] * ul[p * N + i];
+        }
+        const int64_t q = e * P + j * N + i;
+        const T xix = m[0][q], xiz = m[1][q], gx = m[2][q], gz = m[3][q];
+        const T s = m[4][q] / m[5][q];
+        const T dudx = dxi * xix + dgm * gx, dudz = dxi * xiz + dgm * gz;
+        Fx[j * N + i] = s * (dudx * xix + dudz * xiz);
+        Fg[j * N + i] = s * (dudx * gx + dudz * gz);
+      }
+    for (int j = 0; j < N; ++j)
+      for (int i = 0; i < N; ++i) {
+        T tx = 0, tg = 0;
+        for (int q = 0; q < N; ++q) {
+          tx += Hw[q * N + i] * Fx[j * N + q];
+          tg += Hw[q * N + j] * Fg[q * N + i];
+        }
+        f[ibool[e * P + j * N + i]] += w[j] * tx + w[i] * tg;
+      }
+  }
+}
+
 extern "C" {
+
+void oracle_sem2d_acoustic_f64(int64_t E, int N, int64_t nglob, const int32_t* ibool,
+                               const double* u, const double* const* m, const double* H,
+                               const double* Hw, const double* w, double* f) {
+  sem2d_acoustic<double>(E, N, nglob, ibool, u, m, H, Hw, w, f);
+}
+void oracle_sem2d_acoustic_f32(int64_t E, int N, int64_t nglob, const int32_t* ibool,
+                               const float* u, const float* const* m, const float* H,
+                               const float* Hw, const float* w, float* f) {
+  sem2d_acoustic<float>(E, N, nglob, ibool, u, m, H, Hw, w, f);
+}
 
 void oracle_sem2d_local_f32(int64_t E, int N, const float* const* u, const float* const* m,
                             const float* H, const float* Hw, const float* w, float* const* f) {

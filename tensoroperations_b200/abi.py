@@ -74,6 +74,17 @@ class Sem2dFields(C.Structure):
 SEM2D_ARRAYS = ("xix", "xiz", "gamx", "gamz", "jac", "l2m", "mu")
 
 
+class Acoustic2dDesc(C.Structure):
+    _fields_ = [("dtype", C.c_int32), ("ngll", C.c_int32), ("nelem", C.c_int64),
+                ("nglob", C.c_int64), ("hprime", C.c_void_p), ("hprimewgll", C.c_void_p),
+                ("wgll", C.c_void_p)]
+
+
+class Acoustic2dFields(C.Structure):
+    _fields_ = [("u", C.c_void_p), ("f", C.c_void_p), ("ibool", C.c_void_p)] + \
+        [(n, C.c_void_p) for n in ("xix", "xiz", "gamx", "gamz", "jac", "rho")]
+
+
 def _sig(name, restype, argtypes):
     fn = getattr(lib, name)
     fn.restype = restype
@@ -107,6 +118,8 @@ _sig("to_sumsq3_noalloc_max_n", C.c_int64, [])
 _sig("to_scale3", C.c_int, [C.c_int32, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p])
 _sig("to_sem2d_elastic_local", C.c_int, [C.c_int32, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p,
                                          C.POINTER(Sem2dFields), C.c_void_p])
+_sig("to_sem2d_acoustic_apply", C.c_int, [C.POINTER(Acoustic2dDesc), C.POINTER(Acoustic2dFields),
+                                          C.c_int32, C.c_void_p])
 _sig("to_batched_small_gemm", C.c_int, [C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int64,
                                         C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p])
 _sig("to_chain_workspace_bytes", C.c_size_t, [C.c_int32])
@@ -237,6 +250,22 @@ def sem2d_elastic_local(ngll: int, nelem: int, H, Hw, w, u, f, arrays, stream: i
     check(lib.to_sem2d_elastic_local(ngll, nelem, ops[0].ctypes.data, ops[1].ctypes.data,
                                      ops[2].ctypes.data, C.byref(fl), stream),
           "to_sem2d_elastic_local")
+
+
+def sem2d_acoustic_apply(ngll, nelem, nglob, H, Hw, w, u, f, ibool, arrays, dtype,
+                         accumulate=False, stream: int = 0):
+    """f = K u for the 2D acoustic operator (assembled) on the device."""
+    ops = [np.ascontiguousarray(x, dtype=np.float64) for x in (H, Hw, w)]
+    d = Acoustic2dDesc()
+    d.dtype = TO_F64 if np.dtype(dtype) == np.float64 else TO_F32
+    d.ngll, d.nelem, d.nglob = ngll, nelem, nglob
+    d.hprime, d.hprimewgll, d.wgll = (x.ctypes.data for x in ops)
+    fl = Acoustic2dFields()
+    fl.u, fl.f, fl.ibool = _ptr(u), _ptr(f), _ptr(ibool)
+    for n in ("xix", "xiz", "gamx", "gamz", "jac", "rho"):
+        setattr(fl, n, _ptr(arrays[n]))
+    check(lib.to_sem2d_acoustic_apply(C.byref(d), C.byref(fl), 1 if accumulate else 0, stream),
+          "to_sem2d_acoustic_apply")
 
 
 def batched_small_gemm(A, B, Cout, stream: int = 0):

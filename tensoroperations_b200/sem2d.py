@@ -59,3 +59,37 @@ def synthetic_2d(nelem: int, seed: int = 0x2D5EED, dtype=np.float32):
     arrays["mu"] = mu
     u = [abi.synth_fill(npts, dt, seed + c, "normal", 0.0, 1.0) for c in range(2)]
     return u, arrays, H, Hw, w
+
+
+def structured_ibool_2d(nex: int, nez: int, ngll: int) -> np.ndarray:
+    """Shared-node numbering of an nex x nez quad mesh: element e = ez*nex + ex,
+    node(e, j, i) = (ez (N-1) + j) nx + ex (N-1) + i, nx = nex (N-1) + 1."""
+    n1 = ngll - 1
+    nx = nex * n1 + 1
+    e = np.arange(nex * nez)
+    ex, ez = e % nex, e // nex
+    j = np.arange(ngll)[None, :, None]
+    i = np.arange(ngll)[None, None, :]
+    ib = (ez[:, None, None] * n1 + j) * nx + ex[:, None, None] * n1 + i
+    return ib.reshape(-1).astype(np.int32)
+
+
+def acoustic_problem(nex: int = 128, nez: int = 128, ngll: int = 5, dtype=np.float64,
+                     seed: int = 0xAC0571C):
+    """The first configuration: structured quads, GLL operators, seeded fields:
+    xix, xiz, gamx, gamz U[0.5,1.5); jac U[0.5,2); rho, kappa U[1,3); u N(0,1)
+    per global node.  Returns (u, arrays, ibool, nglob, H, Hw, w)."""
+    dt = np.dtype(dtype)
+    P = ngll * ngll
+    E = nex * nez
+    _, w, H, Hw = abi.gll_operators(ngll)
+    arrays = {}
+    for r, name in enumerate(("xix", "xiz", "gamx", "gamz")):
+        arrays[name] = abi.synth_fill(E * P, dt, seed + 1 + r, "uniform", 0.5, 1.5)
+    arrays["jac"] = abi.synth_fill(E * P, dt, seed + 5, "uniform", 0.5, 2.0)
+    arrays["rho"] = abi.synth_fill(E * P, dt, seed + 6, "uniform", 1.0, 3.0)
+    arrays["kappa"] = abi.synth_fill(E * P, dt, seed + 7, "uniform", 1.0, 3.0)
+    n1 = ngll - 1
+    nglob = (nex * n1 + 1) * (nez * n1 + 1)
+    u = abi.synth_fill(nglob, dt, seed, "normal", 0.0, 1.0)
+    return u, arrays, structured_ibool_2d(nex, nez, ngll), nglob, H, Hw, w
