@@ -611,6 +611,78 @@ def run_acoustic2d(args):
     return 0
 
 
+def run_local(args):
+    """Element-local 3D operator at the sizes of the reference's published
+    numbers (H100 NVL; bench_sem_stiffness_3d.cpp:35-36): NGLL 5 with
+    E = 786,432 and NGLL 8 with E = 196,608, f32, u and f per point.
+
+    Printed with --workload local.  Inputs generated on the device."""
+    import torch
+    from tensoroperations_b200 import abi
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    published = {5: {"hand_ms": 3.94, "library_ms": 10.49}, 8: {"hand_ms": 13.67, "library_ms": 11.74}}
+    results = {}
+    peak, peak_src = measured_peak_hbm()
+    for N, E in ((5, 786432), (8, 196608)):
+        P = N ** 3
+        npts = E * P
+        _, w, H, Hw = abi.gll_operators(N)
+
+        def gen(seed, dist, a, b, add=0.0):
+            t = torch.empty(npts, dtype=torch.float32, device=dev)
+            abi.check(abi.lib.to_synth_fill_device(t.data_ptr(), abi.TO_F32, 0, npts, seed, dist,
+                                                    a, b, add, 0), "to_synth_fill_device")
+            return t
+        arrays = {}
+        for r, name in enumerate(abi.POINT_ARRAYS[:9]):
+            arrays[name] = gen(11 + r, 0, 0.5, 1.5, 1.0 if name in ("xix", "etay", "gamz") else 0.0)
+        arrays["jac"] = gen(30, 0, 0.5, 2.0)
+        arrays["l2m"] = gen(31, 0, 1.0, 3.0)
+        arrays["mu"] = gen(32, 0, 0.5, 2.0)
+        abi.check(abi.lib.to_axpy2_device(arrays["l2m"].data_ptr(), arrays["mu"].data_ptr(),
+                                          abi.TO_F32, npts, 0), "to_axpy2_device")
+        u = [gen(40 + c, 1, 0.0, 1.0) for c in range(3)]
+        f = [torch.empty(npts, dtype=torch.float32, device=dev) for _ in range(3)]
+        plan = abi.Sem3dPlan(np.float32, N, E, H, Hw, w)
+        fl = plan.fields(u, f, arrays)
+        stream = torch.cuda.Stream(device=dev)
+        s = stream.cuda_stream
+        for _ in range(max(args.warmup, 3)):
+            plan.apply(fl, stream=s)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        steps = max(20, args.steps // 10)
+        e0.record(stream)
+        for _ in range(steps):
+            plan.apply(fl, stream=s)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        alg = plan.algorithmic_bytes()
+        results[N] = {"nelem": E, "ms": ms, "melem_s": E / (ms * 1e-3) / 1e6,
+                      "gb_s": alg / (ms * 1e-3) / 1e9, "frac": alg / (ms * 1e-3) / 1e9 / peak,
+                      "reference_h100_hand_ms": published[N]["hand_ms"],
+                      "reference_h100_library_ms": published[N]["library_ms"],
+                      "speedup_vs_reference_library": published[N]["library_ms"] / ms}
+        del arrays, u, f
+        torch.cuda.empty_cache()
+    r5 = results[5]
+    line = {"metric": "SEM 3D stiffness Melem/s, element-local f32 (the reference's published sizes)",
+            "value": r5["melem_s"], "unit": "Melem/s", "n_gpus": 1, "steps": max(20, args.steps // 10),
+            "warmup": args.warmup, "ms_per_step": r5["ms"], "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": r5["melem_s"] / (786432 / 3.94e-3 / 1e6),
+            "dtype": "f32", "data": "synthetic, generated on the device",
+            "config": {"workload": "3D elastic, element-local, NGLL 5 E=786432 and NGLL 8 E=196608",
+                       "vs_baseline": "value / the reference's hand kernel on H100 NVL (199.6 Melem/s)"},
+            "roofline": {"bound": "hbm", "achieved": r5["gb_s"], "peak": peak, "unit": "GB/s",
+                         "frac": r5["frac"], "traffic": None, "peak_source": peak_src},
+            "ngll5": results[5], "ngll8": results[8]}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def config_dict(prob, world):
     nex, ney, nez = prob.mesh
     return {"workload": ("3D SEM isotropic elastic stiffness, NGLL=5, f32, structured "
@@ -633,10 +705,12 @@ def main():
                     help="f32 kernel variant (TO_SEM3D_VARIANT): 0 point-pair 8x2, 1 TMA 8x2, "
                          "2 streaming, 3 point-pair 4x4, 4 point-pair 16x1, 5 line-owner 8x3, 6 line-owner 4x5")
     ap.add_argument("--workload", default="sem3d",
-                    choices=["sem3d", "chain", "batched-gemm", "large", "sem2d", "acoustic2d"],
+                    choices=["sem3d", "chain", "batched-gemm", "large", "sem2d", "acoustic2d",
+                             "local"],
                     help="sem3d: the headline SEM operator (default); chain: config 4 "
                          "contraction; batched-gemm: config 2; large: config 5; sem2d: the "
-                         "reference's 2D elastic operator; acoustic2d: config 1")
+                         "reference's 2D elastic operator; acoustic2d: config 1; local: "
+                         "element-local at the reference's published sizes")
     ap.add_argument("--sem2d-elements", type=int, default=2621440)
     ap.add_argument("--large-mesh", type=int, default=128, help="hexes per side for --workload large")
     ap.add_argument("--chain-extent", type=int, default=64)
@@ -658,6 +732,8 @@ def main():
         return run_sem2d(args)
     if args.workload == "acoustic2d":
         return run_acoustic2d(args)
+    if args.workload == "local":
+        return run_local(args)
 
     import torch
     import torch.distributed as dist
