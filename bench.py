@@ -714,6 +714,9 @@ def main():
     ap.add_argument("--sem2d-elements", type=int, default=2621440)
     ap.add_argument("--large-mesh", type=int, default=128, help="hexes per side for --workload large")
     ap.add_argument("--chain-extent", type=int, default=64)
+    ap.add_argument("--layout", default="components", choices=["components", "interleaved"],
+                    help="assembled u / f: one array per component, or interleaved per node "
+                         "(x, y, z, unused; 1 GPU)")
     ap.add_argument("--mesh", type=int, nargs=3, default=[64, 64, 64],
                     metavar=("NEX", "NEY", "NEZ"), help="hexes per GPU (profiling runs)")
     args = ap.parse_args()
@@ -752,10 +755,21 @@ def main():
     from tensoroperations_b200.slab import SlabOperator
     part, prob = make_problem(rank, world)
     u, f, arrays, ibool = to_device(prob, dev)
-    plan = prob.plan()
     stream = torch.cuda.Stream(device=dev)
+    if args.layout == "interleaved":
+        if world > 1:
+            raise SystemExit("--layout interleaved runs on one GPU")
+        u4 = torch.zeros((prob.nglob, 4), dtype=torch.float32, device=dev)
+        for c in range(3):
+            u4[:, c] = u[c]
+        f4 = torch.zeros((prob.nglob, 4), dtype=torch.float32, device=dev)
+        u, f = [u4, None, None], [f4, None, None]
+        plan = abi.Sem3dPlan(np.float32, prob.ngll, prob.nelem, prob.H, prob.Hw, prob.w,
+                             nglob=prob.nglob, assembled=True, interleaved=True)
+    else:
+        plan = prob.plan()
     fields = plan.fields(u, f, arrays, ibool)
-    op = SlabOperator(part, plan, fields, f, dev)
+    op = SlabOperator(part, plan, fields, [x for x in f if x is not None], dev)
 
     clocks = ClockSampler(gpu_id_for(dev))
     clocks.__enter__()
@@ -799,19 +813,20 @@ def main():
     # i's device -> host copy run during step i+1's host -> device copy (PCIe
     # is full duplex); a set is reused only after its previous step's copies
     # and kernels are done.
-    e2e_steps = 0 if args.no_e2e else max(4, min(args.steps // 50, 20))
-    u_host = [torch.from_numpy(x).pin_memory() for x in prob.u]
-    f_host = [[torch.empty(prob.nglob, dtype=torch.float32).pin_memory() for _ in range(3)]
-              for _ in range(2)]
-    u_set = [[torch.empty_like(x) for x in u] for _ in range(2)]
-    f_set = [f, [torch.empty_like(x) for x in f]]
-    ops = [SlabOperator(part, plan, plan.fields(u_set[k], f_set[k], arrays, ibool), f_set[k], dev)
-           for k in range(2)]
-    s_in = torch.cuda.Stream(device=dev)
-    s_out = torch.cuda.Stream(device=dev)
-    ev_in = [torch.cuda.Event() for _ in range(2)]
-    ev_comp = [torch.cuda.Event() for _ in range(2)]
-    ev_out = [torch.cuda.Event() for _ in range(2)]
+    e2e_steps = 0 if (args.no_e2e or args.layout == "interleaved") else max(4, min(args.steps // 50, 20))
+    if e2e_steps:
+        u_host = [torch.from_numpy(x).pin_memory() for x in prob.u]
+        f_host = [[torch.empty(prob.nglob, dtype=torch.float32).pin_memory() for _ in range(3)]
+                  for _ in range(2)]
+        u_set = [[torch.empty_like(x) for x in u] for _ in range(2)]
+        f_set = [f, [torch.empty_like(x) for x in f]]
+        ops = [SlabOperator(part, plan, plan.fields(u_set[k], f_set[k], arrays, ibool), f_set[k],
+                            dev) for k in range(2)]
+        s_in = torch.cuda.Stream(device=dev)
+        s_out = torch.cuda.Stream(device=dev)
+        ev_in = [torch.cuda.Event() for _ in range(2)]
+        ev_comp = [torch.cuda.Event() for _ in range(2)]
+        ev_out = [torch.cuda.Event() for _ in range(2)]
 
     def e2e_step(i):
         k = i % 2
@@ -833,20 +848,22 @@ def main():
                 f_host[k][c].copy_(f_set[k][c], non_blocking=True)
         ev_out[k].record(s_out)
 
+    e2e_ms = 0.0
     if e2e_steps:
         for i in range(2):
             e2e_step(i)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    a0 = torch.cuda.Event(enable_timing=True)
-    a1 = torch.cuda.Event(enable_timing=True)
-    a0.record(s_in)
-    for i in range(e2e_steps):
-        e2e_step(i)
-    a1.record(s_out)
-    torch.cuda.synchronize()
-    e2e_ms = a0.elapsed_time(a1) / max(e2e_steps, 1)
+    if e2e_steps:
+        a0 = torch.cuda.Event(enable_timing=True)
+        a1 = torch.cuda.Event(enable_timing=True)
+        a0.record(s_in)
+        for i in range(e2e_steps):
+            e2e_step(i)
+        a1.record(s_out)
+        torch.cuda.synchronize()
+        e2e_ms = a0.elapsed_time(a1) / e2e_steps
     t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)

@@ -142,7 +142,11 @@ typedef struct to_sem3d_desc {
   int64_t nelem;            /* E                                              */
   int64_t nglob;            /* assembled: number of global nodes; else 0     */
   int32_t assembled;        /* 1 = through ibool, 0 = element-local          */
-  int32_t reserved0;
+  int32_t node_layout;      /* assembled u, f: 0 = one [nglob] array per
+                               component; 1 = interleaved [nglob][4] floats
+                               (x, y, z, unused) in u[0] / f[0], 16-byte
+                               aligned (f32, NGLL 5 only): one 128-bit gather
+                               and one 128-bit scatter-add per point         */
   const double* hprime;     /* HOST [N][N]  H(i,p)   (reference d.H)          */
   const double* hprimewgll; /* HOST [N][N]  Hw(q,i)  (reference d.Hw)         */
   const double* wgll;       /* HOST [N]     w        (reference d.w)           */

@@ -52,7 +52,7 @@ lib = _load()
 
 class Sem3dDesc(C.Structure):
     _fields_ = [("dtype", C.c_int32), ("ngll", C.c_int32), ("nelem", C.c_int64),
-                ("nglob", C.c_int64), ("assembled", C.c_int32), ("reserved0", C.c_int32),
+                ("nglob", C.c_int64), ("assembled", C.c_int32), ("node_layout", C.c_int32),
                 ("hprime", C.POINTER(C.c_double)), ("hprimewgll", C.POINTER(C.c_double)),
                 ("wgll", C.POINTER(C.c_double))]
 
@@ -299,7 +299,7 @@ class Sem3dPlan:
     """A validated operator description (host) -> launches on any stream."""
 
     def __init__(self, dtype, ngll: int, nelem: int, H, Hw, w, nglob: int = 0,
-                 assembled: bool = False):
+                 assembled: bool = False, interleaved: bool = False):
         self.dtype = np.dtype(dtype)
         self._H = np.ascontiguousarray(H, dtype=np.float64)
         self._Hw = np.ascontiguousarray(Hw, dtype=np.float64)
@@ -310,6 +310,7 @@ class Sem3dPlan:
         d.nelem = nelem
         d.nglob = nglob
         d.assembled = 1 if assembled else 0
+        d.node_layout = 1 if interleaved else 0
         d.hprime = self._H.ctypes.data_as(C.POINTER(C.c_double))
         d.hprimewgll = self._Hw.ctypes.data_as(C.POINTER(C.c_double))
         d.wgll = self._w.ctypes.data_as(C.POINTER(C.c_double))
@@ -317,6 +318,7 @@ class Sem3dPlan:
         self._h = C.c_void_p()
         check(lib.to_sem3d_plan_create(C.byref(d), C.byref(self._h)), "to_sem3d_plan_create")
         self.ngll, self.nelem, self.nglob, self.assembled = ngll, nelem, nglob, assembled
+        self.interleaved = interleaved
 
     def __del__(self):
         h = getattr(self, "_h", None)

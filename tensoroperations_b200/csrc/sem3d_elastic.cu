@@ -188,12 +188,12 @@ int launch_v3(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t
 }
 
 // The line-owner kernel (f32 NGLL 5, staged arrays 16-byte aligned).
-template <int EB, int MINB, bool ASM>
+template <int EB, int MINB, bool ASM, bool IL = false>
 int launch_v5(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t stream,
               int dev, int sms) {
   constexpr int NT = EB * 25;
   const size_t smem = Sem3dV5Layout<EB, ASM>::kTotal;
-  auto kernel = sem3d_elastic_v5_kernel<EB, MINB, ASM>;
+  auto kernel = sem3d_elastic_v5_kernel<EB, MINB, ASM, IL>;
   static KernelSlot slot;
   int nb = 0;
   if (int st = configure(slot, kernel, dev, NT, smem, &nb)) return st;
@@ -248,6 +248,14 @@ int launch_sem3d(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStrea
   int dev = 0;
   const int sms = device_sm_count(&dev);
   if (sms <= 0) return -sms;
+  if constexpr (std::is_same_v<T, float> && N == 5 && ASM) {
+    if (plan->desc.node_layout == 1) {
+      if (!staged_arrays_aligned(fl, ASM))
+        return set_error(TO_ERR_ALIGNMENT,
+                         "to_sem3d_apply: interleaved nodes need 16-byte aligned per-point arrays");
+      return launch_v5<8, 3, true, true>(plan, fl, stream, dev, sms);
+    }
+  }
   if constexpr (std::is_same_v<T, float> && N == 5) {
     const int v = sem3d_f32_variant();
     if (v != 2 && staged_arrays_aligned(fl, ASM)) {
@@ -272,23 +280,31 @@ template <typename T, int N>
 int apply_typed(const to_sem3d_plan* plan, const to_sem3d_fields* fl, int accumulate,
                 cudaStream_t stream) {
   const size_t al = sizeof(T);
+  const bool il = plan->desc.node_layout == 1;
   const void* ptrs[] = {fl->u[0], fl->u[1], fl->u[2], fl->f[0], fl->f[1], fl->f[2],
                         fl->xix,  fl->xiy,  fl->xiz,  fl->etax, fl->etay, fl->etaz,
                         fl->gamx, fl->gamy, fl->gamz, fl->jac,  fl->l2m,  fl->mu};
-  for (const void* p : ptrs) {
+  for (int q = 0; q < 18; ++q) {
+    const void* p = ptrs[q];
+    if (il && (q == 1 || q == 2 || q == 4 || q == 5)) continue;  // one interleaved array
     if (!p) return set_error(TO_ERR_INVALID_ARGUMENT, "to_sem3d_apply: null field pointer");
-    if (!aligned(p, al))
+    const size_t need = (il && (q == 0 || q == 3)) ? 16 : al;
+    if (!aligned(p, need))
       return set_error(TO_ERR_ALIGNMENT, "to_sem3d_apply: field pointer %p not %zu-byte aligned",
-                       p, al);
+                       p, need);
   }
   if (plan->desc.assembled) {
     if (!fl->ibool)
       return set_error(TO_ERR_INVALID_ARGUMENT, "to_sem3d_apply: assembled mode needs ibool");
     if (!aligned(fl->ibool, 4))
       return set_error(TO_ERR_ALIGNMENT, "to_sem3d_apply: ibool not 4-byte aligned");
-    if (!accumulate)
-      for (int c = 0; c < 3; ++c)
-        TO_CUDA_TRY(cudaMemsetAsync(fl->f[c], 0, sizeof(T) * plan->desc.nglob, stream));
+    if (!accumulate) {
+      if (il)
+        TO_CUDA_TRY(cudaMemsetAsync(fl->f[0], 0, sizeof(T) * 4 * plan->desc.nglob, stream));
+      else
+        for (int c = 0; c < 3; ++c)
+          TO_CUDA_TRY(cudaMemsetAsync(fl->f[c], 0, sizeof(T) * plan->desc.nglob, stream));
+    }
     return launch_sem3d<T, N, true>(plan, fl, stream);
   }
   return launch_sem3d<T, N, false>(plan, fl, stream);
@@ -326,6 +342,11 @@ int to_sem3d_plan_create(const to_sem3d_desc* desc, to_sem3d_plan** plan) {
   if (desc->nelem < 0)
     return set_error(TO_ERR_INVALID_ARGUMENT, "to_sem3d_plan_create: nelem %lld < 0",
                      static_cast<long long>(desc->nelem));
+  if (desc->node_layout != 0 &&
+      !(desc->node_layout == 1 && desc->assembled && desc->dtype == TO_F32 && desc->ngll == 5))
+    return set_error(TO_ERR_UNSUPPORTED,
+                     "to_sem3d_plan_create: node_layout %d (interleaved nodes: assembled f32 NGLL 5)",
+                     desc->node_layout);
   if (desc->assembled && (desc->nglob <= 0 || desc->nglob > INT32_MAX))
     return set_error(TO_ERR_INVALID_ARGUMENT,
                      "to_sem3d_plan_create: assembled mode needs 0 < nglob <= INT32_MAX");

@@ -66,7 +66,9 @@ struct Sem3dV5Layout {
   static constexpr size_t kTotal = kHeader + kStageBytes + kXBytes + kEBytes;
 };
 
-template <int EB, int MINB, bool ASM>
+// IL: assembled u and f interleaved per node (x, y, z, unused) -- one 128-bit
+// gather and one 128-bit atomicAdd per point instead of three of each.
+template <int EB, int MINB, bool ASM, bool IL = false>
 __global__ void __launch_bounds__(EB * 25, MINB)
     sem3d_elastic_v5_kernel(const __grid_constant__ Sem3dArgs<float, 5> a) {
   using LY = Sem3dV5Layout<EB, ASM>;
@@ -153,10 +155,21 @@ __global__ void __launch_bounds__(EB * 25, MINB)
     const long long base = e * P + ab;
 #pragma unroll
     for (int k = 0; k < N; ++k) node_n[k] = v ? __ldg(a.ibool + base + k * NN) : 0;
+    if constexpr (IL) {
+      const float4* u4 = reinterpret_cast<const float4*>(a.u[0]);
 #pragma unroll
-    for (int k = 0; k < N; ++k)
+      for (int k = 0; k < N; ++k) {
+        const float4 x = v ? __ldg(u4 + node_n[k]) : make_float4(0.f, 0.f, 0.f, 0.f);
+        uc_n[0][k] = x.x;
+        uc_n[1][k] = x.y;
+        uc_n[2][k] = x.z;
+      }
+    } else {
 #pragma unroll
-      for (int c = 0; c < 3; ++c) uc_n[c][k] = v ? __ldg(a.u[c] + node_n[k]) : 0.f;
+      for (int k = 0; k < N; ++k)
+#pragma unroll
+        for (int c = 0; c < 3; ++c) uc_n[c][k] = v ? __ldg(a.u[c] + node_n[k]) : 0.f;
+    }
   };
   if (ASM) gather(b0);
 
@@ -340,6 +353,7 @@ __global__ void __launch_bounds__(EB * 25, MINB)
 #pragma unroll
       for (int k = 0; k < N; ++k) {
         const float wjk = wj * a.ops.w[k], wik = wi * a.ops.w[k];
+        float fc[3];
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
           float g = 0.f;
@@ -347,12 +361,20 @@ __global__ void __launch_bounds__(EB * 25, MINB)
           for (int q = 0; q < N; ++q) g = fmaf(a.ops.Hw[q][k], Fg[c][q], g);
           const float tx = RDX[c * CX + k * SKX + tid];
           const float te = RDE[c * CE + k * SKE + tid];
-          const float fc = fmaf(wij, g, fmaf(wik, te, wjk * tx));
-          if (valid) {
-            if (ASM)
-              atomicAdd(a.f[c] + node[k], fc);
-            else
-              a.f[c][obase + k * NN] = fc;
+          fc[c] = fmaf(wij, g, fmaf(wik, te, wjk * tx));
+        }
+        if (valid) {
+          if (ASM && IL) {
+            atomicAdd(reinterpret_cast<float4*>(a.f[0]) + node[k],
+                      make_float4(fc[0], fc[1], fc[2], 0.f));
+          } else {
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+              if (ASM)
+                atomicAdd(a.f[c] + node[k], fc[c]);
+              else
+                a.f[c][obase + k * NN] = fc[c];
+            }
           }
         }
       }

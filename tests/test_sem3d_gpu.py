@@ -182,3 +182,35 @@ def test_every_kernel_variant_matches_oracle(variant):
     r = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True,
                        text=True, timeout=600)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout + r.stderr
+
+
+@pytest.mark.parametrize("mesh", [(6, 5, 4), (3, 3, 1)])
+def test_interleaved_node_layout(mesh):
+    """Assembled u and f interleaved per node (x, y, z, unused): the same result
+    as the oracle, with 128-bit gathers and scatter-adds."""
+    import torch
+    prob = structured_problem(*mesh, ngll=5, dtype=np.float32, assembled=True, seed=12)
+    u4 = np.zeros((prob.nglob, 4), dtype=np.float32)
+    for c in range(3):
+        u4[:, c] = prob.u[c]
+    du4 = torch.from_numpy(u4).cuda()
+    df4 = torch.full((prob.nglob, 4), float("nan"), device="cuda")
+    arrays = {k: torch.from_numpy(v).cuda() for k, v in prob.arrays.items()}
+    ibool = torch.from_numpy(prob.ibool).cuda()
+    plan = abi.Sem3dPlan(np.float32, 5, prob.nelem, prob.H, prob.Hw, prob.w, nglob=prob.nglob,
+                         assembled=True, interleaved=True)
+    fl = plan.fields([du4, None, None], [df4, None, None], arrays, ibool)
+    plan.apply(fl)
+    torch.cuda.synchronize()
+    got = df4.cpu().numpy()
+    ref = osem.assembled(prob.nelem, 5, prob.nglob, prob.ibool, prob.u, prob.arrays, prob.H,
+                         prob.Hw, prob.w, np.float32)
+    assert osem.rel_l2([got[:, c].copy() for c in range(3)], ref) < 1e-5
+    assert np.all(got[:, 3] == 0.0)
+
+
+def test_interleaved_layout_is_rejected_where_not_built():
+    _, w, H, Hw = abi.gll_operators(5)
+    with pytest.raises(abi.ToError) as e:
+        abi.Sem3dPlan(np.float64, 5, 4, H, Hw, w, nglob=10, assembled=True, interleaved=True)
+    assert e.value.status == abi.TO_ERR_UNSUPPORTED
