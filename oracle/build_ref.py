@@ -12,6 +12,10 @@ are what the tests use on the GPU box, which has no reference tree.
                           sm_100a against this repository's frontend headers
                           and Kokkos subset: the drop-in check (its own
                           PASS/FAIL against its own host reference).
+  bench_sem_stiffness_3d  benchmarks/sem_stiffness_3d/bench_sem_stiffness_3d.cpp
+                          (the flat-DAG route: make_dag / add / multi-output
+                          combines, its hand-written team kernel and its
+                          MDRange kernel), unmodified, the same way.
 
 The reference's own build (CMake fetching Kokkos/GoogleTest/KokkosKernels) is
 not used; Kokkos is replaced by tensoroperations_b200/include/Kokkos_Core.hpp.
@@ -28,12 +32,14 @@ ROOT = HERE.parent
 OUT = HERE / "_ref"
 REF = Path(os.environ.get("TO_REFERENCE_ROOT", "/root/reference"))
 SEM3D = REF / "benchmarks" / "sem_stiffness_3d" / "bench_sem3d_levelgraph.cpp"
+SEM3D_DAG = REF / "benchmarks" / "sem_stiffness_3d" / "bench_sem_stiffness_3d.cpp"
 INC = [f"-I{ROOT / 'include'}", f"-I{ROOT / 'tensoroperations_b200' / 'include'}"]
 LIBDIR = ROOT / "tensoroperations_b200"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 PIN = OUT / "libref_sem3d.so"
 DROPIN = OUT / "bench_sem3d_levelgraph"
+DROPIN_DAG = OUT / "bench_sem_stiffness_3d"
 
 
 def available() -> bool:
@@ -65,12 +71,17 @@ def build(force: bool = False):
               *INC, f'-DBENCH_SEM3D_SOURCE="{SEM3D}"', str(HERE / "ref_pin.cpp"),
               f"-L{LIBDIR}", "-ltensoroperations_b200", f"-Wl,-rpath,{LIBDIR}",
               "-Wl,-rpath,$ORIGIN/../../tensoroperations_b200", "-o", str(PIN)])
-    if force or _stale(DROPIN, deps + [LIBDIR / "libtensoroperations_b200.so"]):
-        _run([NVCC, "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++20",
-              "--extended-lambda", "--expt-relaxed-constexpr", "-diag-suppress", "186,20012",
-              *INC, "-x", "cu", str(SEM3D), f"-L{LIBDIR}", "-ltensoroperations_b200",
-              "-Xlinker", "-rpath,$ORIGIN/../../tensoroperations_b200", "-o", str(DROPIN)])
-    return PIN, DROPIN
+    for src, out in ((SEM3D, DROPIN), (SEM3D_DAG, DROPIN_DAG)):
+        if src.exists() and (force or _stale(out, deps + [src, LIBDIR / "libtensoroperations_b200.so"])):
+            _nvcc_program(src, out)
+    return PIN, DROPIN, DROPIN_DAG
+
+
+def _nvcc_program(src: Path, out: Path):
+    _run([NVCC, "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++20",
+          "--extended-lambda", "--expt-relaxed-constexpr", "-diag-suppress", "186,20012",
+          *INC, "-x", "cu", str(src), f"-L{LIBDIR}", "-ltensoroperations_b200",
+          "-Xlinker", "-rpath,$ORIGIN/../../tensoroperations_b200", "-o", str(out)])
 
 
 if __name__ == "__main__":

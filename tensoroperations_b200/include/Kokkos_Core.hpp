@@ -13,7 +13,8 @@
 //               zero-initialised) or unmanaged; create_mirror_view[_and_copy],
 //               deep_copy, host_mirror_type.
 //   Execution   Cuda (default when compiled by nvcc) and Serial spaces;
-//               parallel_for over RangePolicy and TeamPolicy; TeamVectorRange /
+//               parallel_for over RangePolicy, MDRangePolicy<Rank<N>> and
+//               TeamPolicy; TeamVectorRange /
 //               TeamThreadRange / ThreadVectorRange; team_barrier, team_scratch;
 //               fence, Timer, initialize / finalize, abort, Array.
 //
@@ -28,6 +29,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <initializer_list>
 #include <string>
 #include <type_traits>
 #include <utility>
@@ -700,6 +702,79 @@ class RangePolicy {
   RangePolicy(const execution_space&, std::int64_t b, std::int64_t e) : begin_(b), end_(e) {}
 };
 
+// MDRangePolicy<Rank<N>>: the box [lo, hi) of an N-dimensional index space.
+// The iteration-order and tiling arguments of Kokkos are accepted and ignored:
+// every point is visited exactly once, the last index fastest.
+enum class Iterate { Default, Left, Right };
+template <unsigned N, Iterate Outer = Iterate::Default, Iterate Inner = Iterate::Default>
+struct Rank {
+  static constexpr unsigned rank = N;
+};
+
+namespace Impl {
+template <class T>
+struct rank_of_prop : std::integral_constant<unsigned, 0> {};
+template <unsigned N, Iterate O, Iterate I>
+struct rank_of_prop<Rank<N, O, I>> : std::integral_constant<unsigned, N> {};
+}  // namespace Impl
+
+template <class... Props>
+class MDRangePolicy {
+ public:
+  using execution_space = typename PolicyExec<Props...>::type;
+  static constexpr int rank = static_cast<int>((Impl::rank_of_prop<Props>::value + ... + 0u));
+  static_assert(rank >= 1 && rank <= 6, "MDRangePolicy: give Kokkos::Rank<N> with 1 <= N <= 6");
+  Array<std::int64_t, rank> lo{}, hi{};
+
+  MDRangePolicy(std::initializer_list<std::int64_t> b, std::initializer_list<std::int64_t> e,
+                std::initializer_list<std::int64_t> = {}) {
+    assign(b, e);
+  }
+  MDRangePolicy(const execution_space&, std::initializer_list<std::int64_t> b,
+                std::initializer_list<std::int64_t> e, std::initializer_list<std::int64_t> = {}) {
+    assign(b, e);
+  }
+  template <class I>
+  MDRangePolicy(const Array<I, rank>& b, const Array<I, rank>& e) {
+    for (int d = 0; d < rank; ++d) {
+      lo[d] = static_cast<std::int64_t>(b[d]);
+      hi[d] = static_cast<std::int64_t>(e[d]);
+    }
+  }
+  std::int64_t size() const {
+    std::int64_t n = 1;
+    for (int d = 0; d < rank; ++d) n *= hi[d] > lo[d] ? hi[d] - lo[d] : 0;
+    return n;
+  }
+
+ private:
+  void assign(std::initializer_list<std::int64_t> b, std::initializer_list<std::int64_t> e) {
+    if (static_cast<int>(b.size()) != rank || static_cast<int>(e.size()) != rank) {
+      std::fprintf(stderr, "Kokkos::MDRangePolicy: give %d lower and %d upper bounds\n", rank, rank);
+      std::abort();
+    }
+    int d = 0;
+    for (std::int64_t v : b) lo[d++] = v;
+    d = 0;
+    for (std::int64_t v : e) hi[d++] = v;
+  }
+};
+
+namespace Impl {
+// Point `flat` of the box, the last index fastest, handed to f as N indices.
+template <int N, class F, std::size_t... D>
+KOKKOS_INLINE_FUNCTION void md_call(const F& f, const Array<std::int64_t, N>& lo,
+                                    const Array<std::int64_t, N>& ext, std::int64_t flat,
+                                    std::index_sequence<D...>) {
+  std::int64_t idx[N];
+  for (int d = N - 1; d >= 0; --d) {
+    idx[d] = lo[d] + flat % ext[d];
+    flat /= ext[d];
+  }
+  f(idx[D]...);
+}
+}  // namespace Impl
+
 template <class Member>
 struct TeamRange {
   const Member& member;
@@ -826,6 +901,46 @@ template <class F, class... Props>
 void parallel_for(const RangePolicy<Props...>& p, const F& f) {
   parallel_for("", p, f);
 }
+#ifdef KOKKOS_ENABLE_CUDA
+namespace Impl {
+template <int N, class F>
+__global__ void md_range_kernel(const F f, const Array<std::int64_t, N> lo,
+                                const Array<std::int64_t, N> ext, std::int64_t total) {
+  for (std::int64_t i = blockIdx.x * std::int64_t(blockDim.x) + threadIdx.x; i < total;
+       i += std::int64_t(gridDim.x) * blockDim.x)
+    md_call<N>(f, lo, ext, i, std::make_index_sequence<N>{});
+}
+}  // namespace Impl
+#endif
+
+template <class F, class... Props>
+void parallel_for(const char* label, const MDRangePolicy<Props...>& p, const F& f) {
+  using P = MDRangePolicy<Props...>;
+  using ES = typename P::execution_space;
+  constexpr int N = P::rank;
+  const std::int64_t total = p.size();
+  if (total <= 0) return;
+  Array<std::int64_t, N> ext{};
+  for (int d = 0; d < N; ++d) ext[d] = p.hi[d] - p.lo[d];
+#ifdef KOKKOS_ENABLE_CUDA
+  if constexpr (std::is_same_v<ES, Cuda>) {
+    const std::int64_t blocks = (total + 255) / 256;
+    Impl::md_range_kernel<N, F><<<static_cast<unsigned>(blocks < 65535 * 8 ? blocks : 65535 * 8), 256>>>(
+        f, p.lo, ext, total);
+    Impl::check_launch(label);
+  } else
+#endif
+  {
+    (void)label;
+    for (std::int64_t i = 0; i < total; ++i)
+      Impl::md_call<N>(f, p.lo, ext, i, std::make_index_sequence<N>{});
+  }
+}
+template <class F, class... Props>
+void parallel_for(const MDRangePolicy<Props...>& p, const F& f) {
+  parallel_for("", p, f);
+}
+
 template <class F, class I, class = std::enable_if_t<std::is_integral_v<I>>>
 void parallel_for(const char* label, I n, const F& f) {
   parallel_for(label, RangePolicy<>(0, static_cast<std::int64_t>(n)), f);

@@ -1,0 +1,217 @@
+// DagGraph.hpp -- make_dag / DagGraph / DagOutputs (B200 frontend).
+//
+// Public surface as the reference (include/TensorOperations/DagGraph.hpp:
+// DagOutputs :781-815, DagGraph :823-1005, make_dag :1006-1011):
+//
+//   auto [g0, grad]      = make_dag<float>().add(contraction, Tile<TA, TB, TC>{});
+//   auto [g1, f0, f1]    = g0.add(two_output_combine(grad.as<...>()), CombineTile<...>{});
+//   g1.outputs(f0, f1).team_size(128).execute(TeamPolicyTag<>{}, view0, view1);
+//
+// add() returns the new graph followed by one handle per output, so definition
+// order is the topological order.  execute() lowers the graph onto the level
+// plan (b200/Dag.hpp) and launches one kernel; it returns the league size.
+// Where the reference asserts (index_consistent) or traps, this build throws
+// TensorOperations::LevelGraphError with a one-line reason.
+//
+// Scratch accounting.  The reference stages each node's input operands in a
+// per-node arena next to the slot store.  Here a staged input is a slot of the
+// lowered plan, pooled by liveness with everything else, so
+// DagOutputs::slot_bytes() is the whole request and operand_bytes() is 0;
+// DagGraph::slot_bytes() / operand_bytes() keep the reference's un-pooled
+// bounds (one tile per node output / per staged operand).
+#pragma once
+
+#include <TensorOperations/LabelTiles.hpp>
+#include <TensorOperations/LevelGraph.hpp>
+#include <TensorOperations/Tiling.hpp>
+#include <TensorOperations/b200/Dag.hpp>
+
+namespace TensorOperations {
+
+template <typename Dag, std::size_t... Roots>
+struct DagOutputs;
+
+template <typename ValueType, typename ExecSpace, typename NodesT, typename TilesL>
+struct DagGraph {
+  static constexpr std::size_t N = tuple_size_v<NodesT>;
+  using value_type = ValueType;
+  using exec_space = ExecSpace;
+  using nodes_type = NodesT;
+  using tiles_type = TilesL;
+
+  NodesT nodes;
+
+  template <typename Node, typename TileSpec>
+  auto add(const Node& node, const TileSpec&) const {
+    static_assert(b200::dag_is_contraction_v<Node> || b200::dag_is_combine_v<Node>,
+                  "DagGraph::add: a node is a contraction or a combine (an input is an operand "
+                  "of the nodes that read it)");
+    static_assert(b200::dag_operands_supported<Node>(),
+                  "DagGraph::add: every operand must be an input node or a handle returned by "
+                  "DagGraph::add (as<>() of it)");
+    static_assert(b200::dag_operand_tiles_agree<Node, TileSpec>(),
+                  "DagGraph::add: a handle operand's tile in this node's tile spec differs "
+                  "from the tile its producer was given");
+    static_assert(b200::dag_contracted_tiles_agree<Node, TileSpec>(),
+                  "DagGraph::add: a contracted label has different tile extents in A and B");
+    constexpr auto named = b200::dag_storage_tile<Node, TileSpec>();
+    constexpr auto implied = b200::dag_implied_tile<Node, TileSpec>();
+    static_assert(b200::arrays_equal(named, implied, std::make_index_sequence<Node::Rank>{}),
+                  "DagGraph::add: the node's output tile differs from the tile its operands' "
+                  "tiles give it");
+    constexpr std::size_t M = static_cast<std::size_t>(b200::output_arity<Node>());
+    return add_impl<Node, TileSpec>(node, std::make_index_sequence<M>{});
+  }
+
+  // Designate graph outputs; the order matches the views given to execute().
+  template <typename... Handles>
+  auto outputs(const Handles&...) const {
+    return DagOutputs<DagGraph, Handles::slot_index...>{*this};
+  }
+
+  // Un-pooled bounds, as the reference reports them: one storage tile per
+  // node output, and one tile per staged input operand.
+  std::size_t slot_bytes() const { return slot_bytes_impl(std::make_index_sequence<N>{}); }
+  std::size_t operand_bytes() const {
+    using Low = lowering;
+    std::size_t b = 0;
+    for (std::size_t s = 0; s < Low::NS; ++s) {
+      std::size_t e = 1;
+      for (int d = 0; d < Low::srows[s].rank; ++d) e *= static_cast<std::size_t>(Low::srows[s].tile[d]);
+      b += round16(e * sizeof(ValueType));
+    }
+    return b;
+  }
+  std::size_t scratch_bytes() const { return slot_bytes() + operand_bytes(); }
+  // Staged operands live in the pooled store: there is no separate arena.
+  std::size_t arena_bytes() const { return 0; }
+  std::size_t arena_elems() const { return 0; }
+
+  // The store of the lowered plan, pooled by liveness for these roots.
+  template <std::size_t... Roots>
+  std::size_t pooled_slot_bytes() const {
+    using Low = lowering;
+    return b200::Layout<ValueType, typename Low::levels_t, Low::level_slot(Roots)...>::scratch_bytes;
+  }
+
+  // The reference's precondition for gathering every node's tile index from
+  // the grid node's by label: a mode the grid (last) node carries is tiled
+  // identically and has the same extent there; any other mode has one tile.
+  bool index_consistent() const {
+    using Low = lowering;
+    if constexpr (!Low::nodes_tiled_like_root) return false;
+    const auto gshape = nodes.template get<N - 1>().shape();
+    bool ok = true;
+    for_each_node([&]<std::size_t K>(const auto& node) {
+      constexpr auto& r = Low::rows[K];
+      const auto sh = node.shape();
+      for (int d = 0; d < r.rank; ++d) {
+        int g = -1;
+        for (int q = 0; q < Low::root_rank; ++q)
+          if (Low::root_labels[q] == r.lab[d]) g = q;
+        if (g >= 0) {
+          if (sh[d] != gshape[g]) ok = false;
+        } else if (sh[d] > r.tile[d]) {
+          ok = false;
+        }
+      }
+    });
+    // a grid-node mode no input carries cannot be gridded by the level plan
+    for (int q = 0; q < Low::root_rank; ++q)
+      if (!Low::root_label_staged[q] && gshape[q] > Low::root_tile[q]) ok = false;
+    return ok;
+  }
+
+  template <typename ES, std::size_t... Roots, typename... ViewTs>
+  int launch(int team_size, const ViewTs&... views) const {
+    static_assert(sizeof...(Roots) == sizeof...(ViewTs),
+                  "DagGraph::execute needs one view per designated output");
+    static_assert(std::is_same_v<ES, ExecSpace>,
+                  "DagGraph::execute policy tag must match the graph's execution space");
+    using ViewT = std::tuple_element_t<0, std::tuple<ViewTs...>>;
+    static_assert((std::is_same_v<ViewT, ViewTs> && ...),
+                  "DagGraph::execute: output views must share one type");
+    using Low = lowering;
+    if (!index_consistent())
+      throw LevelGraphError(
+          TO_ERR_INVALID_ARGUMENT,
+          "DagGraph: a node's mode is either tiled differently from the grid node's or is "
+          "multi-tiled and absent from it, so its tile index cannot be gathered from the grid "
+          "node's. Retile so every shared mode matches and every unshared mode has one tile.");
+    const typename Low::graph_t g{Low::make_levels(nodes)};
+    return g.template launch<ES, Low::level_slot(Roots)...>(team_size, views...);
+  }
+
+  using lowering = b200::DagLowering<ValueType, ExecSpace, NodesT, TilesL>;
+
+ private:
+  static constexpr std::size_t round16(std::size_t b) { return (b + 15) & ~std::size_t(15); }
+
+  template <typename Node, typename TileSpec, std::size_t... Ms>
+  auto add_impl(const Node& node, std::index_sequence<Ms...>) const {
+    using NewNodes = decltype(tuple_append(nodes, node));
+    using NewTiles = typename b200::tl_append<TilesL, TileSpec>::type;
+    constexpr std::size_t Base = num_slots();
+    constexpr auto st = b200::dag_storage_tile<Node, TileSpec>();
+    using SL = b200::dag_storage_labels_t<Node>;
+    using ST = b200::array_tile_t<st>;
+    const auto shape = node.shape();
+    return std::make_tuple(DagGraph<ValueType, ExecSpace, NewNodes, NewTiles>{tuple_append(nodes, node)},
+                           b200::DagSlotHandle<Base + Ms, ValueType, ExecSpace, SL, ST>{shape}...);
+  }
+
+  static constexpr std::size_t num_slots() {
+    return [&]<std::size_t... K>(std::index_sequence<K...>) {
+      return (std::size_t{0} + ... +
+              static_cast<std::size_t>(b200::output_arity<tuple_element_t<K, NodesT>>()));
+    }(std::make_index_sequence<N>{});
+  }
+
+  template <std::size_t... K>
+  std::size_t slot_bytes_impl(std::index_sequence<K...>) const {
+    return (std::size_t{0} + ... +
+            [&] {
+              using Node = tuple_element_t<K, NodesT>;
+              constexpr auto st =
+                  b200::dag_storage_tile<Node, typename b200::tl_at<K, TilesL>::type>();
+              std::size_t e = 1;
+              for (int d = 0; d < Node::Rank; ++d) e *= static_cast<std::size_t>(st[d]);
+              return static_cast<std::size_t>(b200::output_arity<Node>()) *
+                     round16(e * sizeof(ValueType));
+            }());
+  }
+
+  template <typename F>
+  void for_each_node(F&& f) const {
+    [&]<std::size_t... K>(std::index_sequence<K...>) {
+      (f.template operator()<K>(nodes.template get<K>()), ...);
+    }(std::make_index_sequence<N>{});
+  }
+};
+
+template <typename Dag, std::size_t... Roots>
+struct DagOutputs {
+  Dag dag;
+  int team = -1;  // threads per team; <= 0 picks a size from the tile
+
+  DagOutputs team_size(int n) const { return {dag, n}; }
+
+  std::size_t slot_bytes() const { return dag.template pooled_slot_bytes<Roots...>(); }
+  std::size_t operand_bytes() const { return dag.arena_bytes(); }
+  std::size_t scratch_bytes() const { return slot_bytes() + operand_bytes(); }
+
+  static constexpr std::size_t num_pools =
+      b200::Pooling<typename Dag::lowering::levels_t, Dag::lowering::level_slot(Roots)...>::num_pools;
+
+  template <typename ES, TensorLike... Ts>
+  int execute(const TeamPolicyTag<ES>&, const Ts&... ts) const {
+    return dag.template launch<ES, Roots...>(team, ts...);
+  }
+};
+
+template <typename ValueType, typename ExecSpace = Kokkos::DefaultExecutionSpace>
+auto make_dag() {
+  return DagGraph<ValueType, ExecSpace, DeviceTuple<>, b200::TypeList<>>{DeviceTuple<>{}};
+}
+
+}  // namespace TensorOperations

@@ -11,6 +11,12 @@
   as host code, one thread per CTA, run on a SEM-shaped graph under
   AddressSanitizer/UBSan and compared with a direct loop -- every pooled-slot
   offset, stride and root store stays inside its buffer.
+* dag_host_check.cpp: the flat-DAG route (make_dag / add / as<> / three-output
+  combines) lowered onto the level plan -- 6 levels, 57 slots, the grid from
+  the last node -- and run through the same host-compiled evaluator under
+  AddressSanitizer/UBSan against a direct loop, with a partial last tile.
+* dag_guard_negative.cpp: each DagGraph diagnostic fires on the graph it
+  forbids; the control graph compiles.
 """
 import shutil
 import subprocess
@@ -73,3 +79,39 @@ def test_evaluator_host_emulation_under_sanitizers(tmp_path, elements):
     run = subprocess.run([str(exe), str(elements)], capture_output=True, text=True, timeout=120)
     assert run.returncode == 0, run.stdout + run.stderr
     assert "max abs error" in run.stdout
+
+
+DAG_GUARDS = {
+    1: "a contraction node's tile must be Tile<TileA, TileB, TileC>",
+    2: "names a slot that no earlier node of this graph produced",
+    3: "the node's output tile differs from the tile its operands' tiles give it",
+    4: "a handle operand's tile in this node's tile spec differs from the tile its producer",
+}
+
+
+@pytest.mark.parametrize("case", [0, *DAG_GUARDS])
+def test_dag_guard(case):
+    r = _compile(["-fsyntax-only", f"-DNEG_CASE={case}", str(CPP / "dag_guard_negative.cpp")])
+    if case == 0:
+        assert r.returncode == 0, r.stderr[-3000:]
+        return
+    assert r.returncode != 0
+    fired = {m for m in DAG_GUARDS.values() if m in r.stderr}
+    assert fired == {DAG_GUARDS[case]}, (case, fired, r.stderr[-2000:])
+
+
+@pytest.fixture(scope="module")
+def dag_host_exe(tmp_path_factory):
+    exe = tmp_path_factory.mktemp("dag") / "dag_host"
+    r = _compile(["-O1", "-g", "-fsanitize=address,undefined", "-fno-sanitize-recover=all",
+                  str(CPP / "dag_host_check.cpp"), "-o", str(exe)], timeout=600)
+    assert r.returncode == 0, r.stderr[-3000:]
+    return exe
+
+
+@pytest.mark.parametrize("elements", [1, 5, 6])
+def test_dag_lowering_host_emulation_under_sanitizers(dag_host_exe, elements):
+    run = subprocess.run([str(dag_host_exe), str(elements)], capture_output=True, text=True,
+                         timeout=120)
+    assert run.returncode == 0, run.stdout + run.stderr
+    assert "max abs error" in run.stdout and "pools" in run.stdout
