@@ -16,6 +16,14 @@ are what the tests use on the GPU box, which has no reference tree.
                           (the flat-DAG route: make_dag / add / multi-output
                           combines, its hand-written team kernel and its
                           MDRange kernel), unmodified, the same way.
+  bench_sem_stiffness_2d  benchmarks/sem_stiffness/bench_sem_stiffness.cpp (the
+                          2D P-SV program: the tree route make_graph().ops /
+                          nested bundles, the DAG and multi-output DAG routes,
+                          its hand-written and CONTROL kernels), the same way.
+  libref_sem2d.so         that 2D source compiled host-only through
+                          oracle/ref_pin2d.cpp: its fill_field(),
+                          fill_operators() and host_reference() behind a C
+                          ABI, to pin the 2D oracle.
 
 The reference's own build (CMake fetching Kokkos/GoogleTest/KokkosKernels) is
 not used; Kokkos is replaced by tensoroperations_b200/include/Kokkos_Core.hpp.
@@ -33,6 +41,7 @@ OUT = HERE / "_ref"
 REF = Path(os.environ.get("TO_REFERENCE_ROOT", "/root/reference"))
 SEM3D = REF / "benchmarks" / "sem_stiffness_3d" / "bench_sem3d_levelgraph.cpp"
 SEM3D_DAG = REF / "benchmarks" / "sem_stiffness_3d" / "bench_sem_stiffness_3d.cpp"
+SEM2D = REF / "benchmarks" / "sem_stiffness" / "bench_sem_stiffness.cpp"
 INC = [f"-I{ROOT / 'include'}", f"-I{ROOT / 'tensoroperations_b200' / 'include'}"]
 LIBDIR = ROOT / "tensoroperations_b200"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
@@ -40,6 +49,8 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 PIN = OUT / "libref_sem3d.so"
 DROPIN = OUT / "bench_sem3d_levelgraph"
 DROPIN_DAG = OUT / "bench_sem_stiffness_3d"
+DROPIN_2D = OUT / "bench_sem_stiffness_2d"
+PIN2D = OUT / "libref_sem2d.so"
 
 
 def available() -> bool:
@@ -71,10 +82,15 @@ def build(force: bool = False):
               *INC, f'-DBENCH_SEM3D_SOURCE="{SEM3D}"', str(HERE / "ref_pin.cpp"),
               f"-L{LIBDIR}", "-ltensoroperations_b200", f"-Wl,-rpath,{LIBDIR}",
               "-Wl,-rpath,$ORIGIN/../../tensoroperations_b200", "-o", str(PIN)])
-    for src, out in ((SEM3D, DROPIN), (SEM3D_DAG, DROPIN_DAG)):
+    if SEM2D.exists() and (force or _stale(PIN2D, deps + [SEM2D, HERE / "ref_pin2d.cpp"])):
+        _run(["g++", "-std=c++20", "-O2", "-ffp-contract=off", "-fno-fast-math", "-fPIC", "-shared",
+              *INC, f'-DBENCH_SEM2D_SOURCE="{SEM2D}"', str(HERE / "ref_pin2d.cpp"),
+              f"-L{LIBDIR}", "-ltensoroperations_b200", f"-Wl,-rpath,{LIBDIR}",
+              "-Wl,-rpath,$ORIGIN/../../tensoroperations_b200", "-o", str(PIN2D)])
+    for src, out in ((SEM3D, DROPIN), (SEM3D_DAG, DROPIN_DAG), (SEM2D, DROPIN_2D)):
         if src.exists() and (force or _stale(out, deps + [src, LIBDIR / "libtensoroperations_b200.so"])):
             _nvcc_program(src, out)
-    return PIN, DROPIN, DROPIN_DAG
+    return PIN, DROPIN, DROPIN_DAG, DROPIN_2D, PIN2D
 
 
 def _nvcc_program(src: Path, out: Path):

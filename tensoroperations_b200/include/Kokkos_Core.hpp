@@ -604,6 +604,7 @@ auto create_mirror_view_and_copy(const HostSpace&, const View<D, P...>& v) {
 // ---------------------------------------------------------------------------
 struct AUTO_t {};
 inline constexpr AUTO_t AUTO{};
+struct ParallelForTag {};
 
 struct PerTeamValue {
   std::size_t value;
@@ -689,6 +690,16 @@ class TeamPolicy {
   }
   int league_size() const { return league_; }
   int team_size() const { return team_; }
+  // The team size parallel_for launches with AUTO (128 threads): the shim
+  // does not size teams from occupancy.
+  template <class F>
+  int team_size_recommended(const F&, ParallelForTag) const {
+    return team_ > 0 ? team_ : 128;
+  }
+  template <class F>
+  int team_size_max(const F&, ParallelForTag) const {
+    return 1024;
+  }
   bool auto_team() const { return team_ <= 0; }
   std::size_t scratch_size(int level) const { return scratch_[level ? 1 : 0]; }
 };

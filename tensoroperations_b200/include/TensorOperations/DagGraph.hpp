@@ -144,6 +144,14 @@ struct DagGraph {
 
   using lowering = b200::DagLowering<ValueType, ExecSpace, NodesT, TilesL>;
 
+  // Slots of the flat DAG (one per node output).
+  static constexpr std::size_t num_slots() {
+    return [&]<std::size_t... K>(std::index_sequence<K...>) {
+      return (std::size_t{0} + ... +
+              static_cast<std::size_t>(b200::output_arity<tuple_element_t<K, NodesT>>()));
+    }(std::make_index_sequence<N>{});
+  }
+
  private:
   static constexpr std::size_t round16(std::size_t b) { return (b + 15) & ~std::size_t(15); }
 
@@ -158,13 +166,6 @@ struct DagGraph {
     const auto shape = node.shape();
     return std::make_tuple(DagGraph<ValueType, ExecSpace, NewNodes, NewTiles>{tuple_append(nodes, node)},
                            b200::DagSlotHandle<Base + Ms, ValueType, ExecSpace, SL, ST>{shape}...);
-  }
-
-  static constexpr std::size_t num_slots() {
-    return [&]<std::size_t... K>(std::index_sequence<K...>) {
-      return (std::size_t{0} + ... +
-              static_cast<std::size_t>(b200::output_arity<tuple_element_t<K, NodesT>>()));
-    }(std::make_index_sequence<N>{});
   }
 
   template <std::size_t... K>

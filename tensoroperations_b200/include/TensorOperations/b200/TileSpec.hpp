@@ -9,9 +9,14 @@
 //                             (an operand's tile in that operand's label order);
 //   a plain StaticTile        a combine's output tile, every operand staged in
 //                             the output's order.
+// On the tree route (Graph::execute) the bundles nest like the expression: an
+// operand that is itself a node carries that node's bundle (a Tile<...> for a
+// contraction, a CombineTile<...> for a combine) in place of its plain tile.
 // Only static extents exist on this route: every tile is a compile-time
 // constant of the device evaluator.
 #pragma once
+
+#include <tuple>
 
 #include <TensorOperations/b200/Labels.hpp>
 
@@ -30,12 +35,20 @@ struct Tile {
 template <typename OutTile, typename... OpTiles>
 struct CombineTile {
   using out_type = OutTile;
+  using op_types = std::tuple<OpTiles...>;
   static constexpr int rank = OutTile::rank;
   static constexpr bool is_static = true;
   static constexpr int num_ops = static_cast<int>(sizeof...(OpTiles));
   OutTile out{};
   KOKKOS_INLINE_FUNCTION static constexpr int extent(int i) { return OutTile::extent(i); }
 };
+
+// make_combine_tile(out, op_tiles...) -- the bundle for a combine whose
+// operands are nested nodes (reference Tiling.hpp:1070-1074).
+template <typename OutTile, typename... OpTiles>
+constexpr CombineTile<OutTile, OpTiles...> make_combine_tile(const OutTile&, const OpTiles&...) {
+  return CombineTile<OutTile, OpTiles...>{};
+}
 
 template <typename TileA, typename TileB, typename TileC>
 KOKKOS_INLINE_FUNCTION constexpr TileC output_tile(const Tile<TileA, TileB, TileC>&) noexcept {

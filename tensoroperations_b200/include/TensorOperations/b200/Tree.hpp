@@ -1,0 +1,318 @@
+// Tree.hpp -- the tree route: make_graph().ops(nodes...) / Graph::execute with
+// a nested tile bundle, lowered onto the flat DAG and from there onto the level
+// plan and the level evaluator.
+//
+// Public surface as the reference (include/TensorOperations/Graph.hpp:
+// Graph::ops :283-293 returning the new graph and one handle per output,
+// execute(TeamPolicyTag, tile, views...) :295-310 -- one launch per output
+// node, the league sizes summed --, the flat tile-list execute :316-327 whose
+// Tile<A,B,C> bundles are taken in pre-order, make_graph :337; Evaluator<
+// TeamPolicyTag, Node, Tile>::scratch_size_per_team, Evaluator.hpp:452).
+//
+// A tree nests its operands: a contraction's A or B, or a combine's operand,
+// may itself be a contraction or a combine, and the tile bundle nests the same
+// way (Tile<A,B,C> for a contraction, CombineTile<Out, Ops...> for a combine,
+// the plain tile for an input).  Lowering walks the tree in post-order and adds
+// every inner node to a DagGraph with its own bundle; a nested node becomes a
+// slot operand of its parent, read under the labels it was DECLARED with (a
+// contraction's declared order, through its storage permutation).  A subtree
+// reached twice in a tree is two subtrees, so it is evaluated twice, as in the
+// reference; sharing is what the DagGraph route is for.
+#pragma once
+
+#include <tuple>
+
+#include <TensorOperations/b200/Dag.hpp>
+
+namespace TensorOperations {
+
+template <typename ValueType, typename ExecSpace, typename NodesT, typename TilesL>
+struct DagGraph;
+template <typename Dag, std::size_t... Roots>
+struct DagOutputs;
+
+namespace b200 {
+
+// The plain tile of a bundle: what the node's parent sees as its operand tile.
+template <class S>
+struct plain_tile {
+  using type = S;
+};
+template <class A, class B, class C>
+struct plain_tile<Tile<A, B, C>> {
+  using type = C;
+};
+template <class O, class... Ops>
+struct plain_tile<CombineTile<O, Ops...>> {
+  using type = O;
+};
+
+// The bundle of operand M of a combine: its own entry of a CombineTile, else
+// the output tile (an input operand staged in the output's order).
+template <class Spec, std::size_t M, bool = is_combine_tile<Spec>::value>
+struct combine_op_spec {
+  using type = typename combine_out_tile<Spec>::type;
+};
+template <class Spec, std::size_t M>
+struct combine_op_spec<Spec, M, true> {
+  using ops = typename Spec::op_types;
+  using type = typename std::conditional_t<(M < std::tuple_size_v<ops>),
+                                           std::tuple_element<M < std::tuple_size_v<ops> ? M : 0, ops>,
+                                           std::type_identity<typename Spec::out_type>>::type;
+};
+
+// The operand a parent reads for a node lowered into slot `Slot` with bundle
+// TS: its declared labels over its storage tile.
+template <class V, class ES, std::size_t Slot, class Node, class TS>
+auto declared_operand(const Node& node) {
+  constexpr auto st = dag_storage_tile<Node, TS>();
+  using STile = array_tile_t<st>;
+  if constexpr (dag_is_contraction_v<Node>) {
+    constexpr auto perm = label_positions<typename Node::decl_seq, typename Node::canon_seq>();
+    using Op = SlotNode<V, ES, Slot, typename Node::decl_seq, STile, array_iseq_t<perm>>;
+    const auto sh = node.shape();  // canonical
+    Kokkos::Array<int, Node::Rank> decl{};
+    for (int d = 0; d < Node::Rank; ++d) decl[d] = sh[perm[d]];
+    return Op{decl};
+  } else {
+    static_assert(Node::NumOut == 1,
+                  "Graph: a multi-output combine cannot be an operand of another node on the "
+                  "tree route (name its outputs through DagGraph instead)");
+    using Op = SlotNode<V, ES, Slot, typename Node::modes_seq, STile,
+                        std::make_integer_sequence<int, Node::Rank>>;
+    return Op{node.shape()};
+  }
+}
+
+template <class V, class ES>
+struct TreeLowering {
+  // Lower `node` (bundle Spec) into `dag`; returns (new dag, the operand a
+  // parent reads: the input node itself, or a slot operand).
+  template <class Spec, class Dag, class Node>
+  static auto run(const Dag& dag, const Node& node) {
+    if constexpr (dag_is_input_v<Node>) {
+      return std::make_tuple(dag, node);
+    } else if constexpr (dag_is_contraction_v<Node>) {
+      static_assert(is_contraction_tile<Spec>::value,
+                    "Graph::execute: a contraction node's tile must be a Tile<TileA, TileB, "
+                    "TileC> bundle");
+      const auto ra = run<typename Spec::a_type>(dag, node.node_a);
+      const auto rb = run<typename Spec::b_type>(std::get<0>(ra), node.node_b);
+      using A = std::decay_t<decltype(std::get<1>(ra))>;
+      using B = std::decay_t<decltype(std::get<1>(rb))>;
+      using C = NodeHandle<ContractionTag, A, B, typename Node::decl_seq, typename Node::value_type,
+                           typename Node::exec_space, typename Node::hook_type>;
+      const C c{std::get<1>(ra), std::get<1>(rb), node.shape_};
+      using TS = Tile<typename plain_tile<typename Spec::a_type>::type,
+                      typename plain_tile<typename Spec::b_type>::type, typename Spec::c_type>;
+      return finish(std::get<0>(rb), c, TS{});
+    } else {
+      static_assert(dag_is_combine_v<Node>,
+                    "Graph::execute: a node is an input, a contraction or a combine");
+      return run_combine<Spec, 0>(dag, node);
+    }
+  }
+
+  template <class Spec, std::size_t M, class Dag, class Node, class... Done>
+  static auto run_combine(const Dag& dag, const Node& node, const Done&... done) {
+    if constexpr (M == static_cast<std::size_t>(Node::NumOps)) {
+      using C = NodeHandle<CombineTag, typename Node::combine_type, typename Node::modes_seq,
+                           typename Node::value_type, typename Node::exec_space,
+                           std::integral_constant<int, Node::NumOut>, Done...>;
+      const C c{node.fn, DeviceTuple<Done...>(done...), node.shape_};
+      return finish(dag, c, typename combine_out_tile<Spec>::type{});
+    } else {
+      const auto r = run<typename combine_op_spec<Spec, M>::type>(
+          dag, node.operands.template get<M>());
+      return run_combine<Spec, M + 1>(std::get<0>(r), node, done..., std::get<1>(r));
+    }
+  }
+
+  template <class Dag, class Node, class TS>
+  static auto finish(const Dag& dag, const Node& node, const TS& ts) {
+    const auto added = dag.add(node, ts);
+    constexpr std::size_t slot = std::decay_t<decltype(std::get<1>(added))>::slot_index;
+    if constexpr (output_arity<Node>() == 1)
+      return std::make_tuple(std::get<0>(added), declared_operand<V, ES, slot, Node, TS>(node));
+    else
+      return std::make_tuple(std::get<0>(added), 0);  // a multi-output root: no operand
+  }
+
+  // The DAG of one output node: the root is the last node added.
+  template <class Spec, class Node>
+  static auto dag_of(const Node& node) {
+    return std::get<0>(run<Spec>(make_dag_empty(), node));
+  }
+  static auto make_dag_empty() {
+    return DagGraph<V, ES, DeviceTuple<>, TypeList<>>{DeviceTuple<>{}};
+  }
+};
+
+// Roots of the lowered tree: the root node's slots, the last ones of the DAG.
+template <class Dag, class Seq>
+struct tree_outputs;
+template <class Dag, std::size_t... M>
+struct tree_outputs<Dag, std::index_sequence<M...>> {
+  static constexpr std::size_t NS = Dag::num_slots();
+  static constexpr std::size_t arity = sizeof...(M);
+  using type = DagOutputs<Dag, (NS - arity + M)...>;
+};
+template <class Node, class Spec>
+struct tree_types {
+  using V = typename Node::value_type;
+  using ES = typename Node::exec_space;
+  using dag_t = decltype(TreeLowering<V, ES>::template dag_of<Spec>(std::declval<const Node&>()));
+  using outputs_t = typename tree_outputs<
+      dag_t, std::make_index_sequence<static_cast<std::size_t>(output_arity<Node>())>>::type;
+};
+
+// ---- the flat tile list (pre-order Tile<A,B,C> bundles of a contraction chain)
+template <class Node>
+constexpr std::size_t count_contractions() {
+  if constexpr (dag_is_contraction_v<Node>)
+    return 1 + count_contractions<typename Node::node_a_type>() +
+           count_contractions<typename Node::node_b_type>();
+  else
+    return 0;
+}
+template <std::size_t Offset, class Node, class Tuple>
+struct assembled_tile;
+template <std::size_t Offset, class Op, class Leaf, class Tuple>
+struct assembled_operand {
+  static_assert(dag_is_input_v<Op> || dag_is_contraction_v<Op>,
+                "flat tile list: a non-contraction operand must be an input node; a fused "
+                "combine operand needs its own nested bundle (make_combine_tile) and the "
+                "execute overload taking one assembled tile");
+  using type = Leaf;
+};
+template <std::size_t Offset, class Op, class Leaf, class Tuple>
+  requires dag_is_contraction_v<Op>
+struct assembled_operand<Offset, Op, Leaf, Tuple> {
+  using type = typename assembled_tile<Offset, Op, Tuple>::type;
+  static_assert(std::is_same_v<Leaf, typename type::c_type>,
+                "flat tile list: a parent's operand tile must equal the fused sub-contraction's "
+                "output tile (bundle.c)");
+};
+template <std::size_t Offset, class Node, class Tuple>
+struct assembled_tile {
+  static_assert(dag_is_contraction_v<Node>, "flat tile list: the output node must be a contraction");
+  static_assert(Offset < std::tuple_size_v<Tuple>,
+                "flat tile list: fewer Tile<A,B,C> bundles than contraction nodes");
+  using bundle = std::tuple_element_t<Offset, Tuple>;
+  static constexpr std::size_t offB = Offset + 1 + count_contractions<typename Node::node_a_type>();
+  using type = Tile<typename assembled_operand<Offset + 1, typename Node::node_a_type,
+                                               typename bundle::a_type, Tuple>::type,
+                    typename assembled_operand<offB, typename Node::node_b_type,
+                                               typename bundle::b_type, Tuple>::type,
+                    typename bundle::c_type>;
+};
+
+}  // namespace b200
+
+// ---------------------------------------------------------------------------
+// Graph: the tree builder.  OutputTuple holds the nodes of the last ops().
+// ---------------------------------------------------------------------------
+template <typename OutputTuple = std::tuple<>>
+struct Graph {
+  OutputTuple outputs{};
+
+  // Register output nodes; returns {new graph, one handle per output}: the node
+  // itself for a single-output node (usable as an operand downstream), its
+  // output index for each output of a multi-output combine.
+  template <typename... Nodes>
+  auto ops(const Nodes&... nodes) const {
+    using G = Graph<std::tuple<Nodes...>>;
+    return std::tuple_cat(std::make_tuple(G{std::make_tuple(nodes...)}), handles_of(nodes)...);
+  }
+
+  // One launch per output node, every node with the same bundle; one view per
+  // output (the sum of the nodes' output arities).  Returns the summed league.
+  template <typename ES, typename Spec, TensorLike... Ts>
+  int execute(const TeamPolicyTag<ES>&, const Spec&, const Ts&... ts) const {
+    constexpr std::size_t N = std::tuple_size_v<OutputTuple>;
+    static_assert(total_arity(std::make_index_sequence<N>{}) == static_cast<int>(sizeof...(Ts)),
+                  "execute needs one view per output (sum of output arities)");
+    const auto views = std::tie(ts...);
+    int league = 0;
+    [&]<std::size_t... I>(std::index_sequence<I...>) {
+      ((league += run_output<I, Spec>(views)), ...);
+    }(std::make_index_sequence<N>{});
+    return league;
+  }
+
+  // The flat tile-list form of a contraction chain: one Tile<A,B,C> per
+  // contraction node in pre-order (node, A subtree, B subtree); single output.
+  template <typename ES, typename... Bundles, TensorLike... Ts>
+  int execute(const TeamPolicyTag<ES>& tag, const std::tuple<Bundles...>&, const Ts&... ts) const {
+    static_assert(std::tuple_size_v<OutputTuple> == 1,
+                  "flat tile-list execute supports a single output node");
+    static_assert(sizeof...(Ts) == 1, "exactly one output view is required");
+    using Node = std::tuple_element_t<0, OutputTuple>;
+    using Spec = typename b200::assembled_tile<0, Node, std::tuple<Bundles...>>::type;
+    return execute(tag, Spec{}, ts...);
+  }
+
+ private:
+  template <typename Node>
+  static auto handles_of(const Node& n) {
+    constexpr int M = b200::output_arity<Node>();
+    if constexpr (M == 1)
+      return std::make_tuple(n);
+    else
+      return [&]<std::size_t... Ms>(std::index_sequence<Ms...>) {
+        return std::make_tuple(std::integral_constant<std::size_t, Ms>{}...);
+      }(std::make_index_sequence<static_cast<std::size_t>(M)>{});
+  }
+
+  template <std::size_t... I>
+  static constexpr int total_arity(std::index_sequence<I...>) {
+    return (0 + ... + b200::output_arity<std::tuple_element_t<I, OutputTuple>>());
+  }
+  template <std::size_t I>
+  static constexpr int view_offset() {
+    int o = 0;
+    [&]<std::size_t... K>(std::index_sequence<K...>) {
+      ((o += b200::output_arity<std::tuple_element_t<K, OutputTuple>>()), ...);
+    }(std::make_index_sequence<I>{});
+    return o;
+  }
+
+  template <std::size_t I, typename Spec, typename Views>
+  int run_output(const Views& views) const {
+    using Node = std::tuple_element_t<I, OutputTuple>;
+    using V = typename Node::value_type;
+    using ES = typename Node::exec_space;
+    using TT = b200::tree_types<Node, Spec>;
+    const auto dag = b200::TreeLowering<V, ES>::template dag_of<Spec>(std::get<I>(outputs));
+    const typename TT::outputs_t outs{dag};
+    constexpr int off = view_offset<I>();
+    return [&]<std::size_t... K>(std::index_sequence<K...>) {
+      return outs.execute(TeamPolicyTag<ES>{}, std::get<off + K>(views)...);
+    }(std::make_index_sequence<static_cast<std::size_t>(b200::output_arity<Node>())>{});
+  }
+};
+
+inline Graph<> make_graph() { return {}; }
+
+// Evaluator<TeamPolicyTag<ES>, Node, Spec>: the scratch one team of the tree
+// route requests for `Node` under bundle `Spec` (reference Evaluator.hpp:452,
+// scratch_size_per_team).  Everything is a compile-time constant of the plan.
+template <typename Policy, typename Node, typename Spec>
+struct Evaluator;
+template <typename ES, typename Node, typename Spec>
+struct Evaluator<TeamPolicyTag<ES>, Node, Spec> {
+  using outputs_t = typename b200::tree_types<Node, Spec>::outputs_t;
+  static std::size_t scratch_size_per_team(const Spec&) {
+    return scratch_of(static_cast<outputs_t*>(nullptr));
+  }
+
+ private:
+  template <typename Dag, std::size_t... R>
+  static std::size_t scratch_of(DagOutputs<Dag, R...>*) {
+    using Low = typename Dag::lowering;
+    return b200::Layout<typename Dag::value_type, typename Low::levels_t,
+                        Low::level_slot(R)...>::scratch_bytes;
+  }
+};
+
+}  // namespace TensorOperations

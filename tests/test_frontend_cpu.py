@@ -17,6 +17,9 @@
   AddressSanitizer/UBSan against a direct loop, with a partial last tile.
 * dag_guard_negative.cpp: each DagGraph diagnostic fires on the graph it
   forbids; the control graph compiles.
+* tree_host_check.cpp: the tree route (make_graph().ops with nested Tile /
+  CombineTile bundles, and a flat pre-order tile list of a contraction chain)
+  lowered through the DAG onto the level plan and run the same way.
 """
 import shutil
 import subprocess
@@ -115,3 +118,20 @@ def test_dag_lowering_host_emulation_under_sanitizers(dag_host_exe, elements):
                          timeout=120)
     assert run.returncode == 0, run.stdout + run.stderr
     assert "max abs error" in run.stdout and "pools" in run.stdout
+
+
+@pytest.fixture(scope="module")
+def tree_host_exe(tmp_path_factory):
+    exe = tmp_path_factory.mktemp("tree") / "tree_host"
+    r = _compile(["-O1", "-g", "-fsanitize=address,undefined", "-fno-sanitize-recover=all",
+                  str(CPP / "tree_host_check.cpp"), "-o", str(exe)], timeout=600)
+    assert r.returncode == 0, r.stderr[-3000:]
+    return exe
+
+
+@pytest.mark.parametrize("elements", [1, 5, 6])
+def test_tree_lowering_host_emulation_under_sanitizers(tree_host_exe, elements):
+    run = subprocess.run([str(tree_host_exe), str(elements)], capture_output=True, text=True,
+                         timeout=120)
+    assert run.returncode == 0, run.stdout + run.stderr
+    assert "tree max abs error" in run.stdout and "chain max abs error" in run.stdout
