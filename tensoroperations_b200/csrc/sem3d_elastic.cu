@@ -17,6 +17,7 @@ __device__ int g_to_device_status = 0;
 #include "sem3d_elastic_v3.cuh"
 #include "sem3d_elastic_v5.cuh"
 #include "sem3d_elastic_lo.cuh"
+#include "sem3d_elastic_hc.cuh"
 
 struct to_sem3d_plan {
   to_sem3d_desc desc;
@@ -188,17 +189,23 @@ int launch_v3(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t
 }
 
 // The line-owner kernel (f32 NGLL 5, staged arrays 16-byte aligned).
-template <int EB, int MINB, bool ASM, bool IL = false>
+template <int EB, int MINB, bool ASM, bool IL = false, int OPT = kV5Packed>
 int launch_v5(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t stream,
               int dev, int sms) {
   constexpr int NT = EB * 25;
   const size_t smem = Sem3dV5Layout<EB, ASM>::kTotal;
-  auto kernel = sem3d_elastic_v5_kernel<EB, MINB, ASM, IL>;
+  auto kernel = sem3d_elastic_v5_kernel<EB, MINB, ASM, IL, OPT>;
   static KernelSlot slot;
   int nb = 0;
   if (int st = configure(slot, kernel, dev, NT, smem, &nb)) return st;
-  Sem3dArgs<float, 5> a = make_args<float, 5>(plan, fl);
-  a.prefetch = 1;
+  Sem3dV5Args a{};
+  a.a = make_args<float, 5>(plan, fl);
+  a.a.prefetch = 1;
+  for (int i = 0; i < 5; ++i)
+    for (int p = 0; p < 5; ++p) {
+      a.H2[i][p] = make_float2(a.a.ops.H[i][p], a.a.ops.H[i][p]);
+      a.Hw2[i][p] = make_float2(a.a.ops.Hw[i][p], a.a.ops.Hw[i][p]);
+    }
   const long long nbatch = (plan->desc.nelem + EB - 1) / EB;
   const long long cap = static_cast<long long>(sms) * nb;
   const int grid = static_cast<int>(nbatch < cap ? nbatch : cap);
@@ -227,6 +234,26 @@ int launch_lo(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t
   return ok();
 }
 
+// The half-column line-owner kernel (NGLL 8): two owners per column.
+template <typename T, int EB, int MINB, bool ASM>
+int launch_hc(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t stream,
+              int dev, int sms) {
+  constexpr int NT = EB * 128;
+  const size_t smem = Sem3dHcLayout<T, EB>::kTotal;
+  auto kernel = sem3d_elastic_hc_kernel<T, EB, MINB, ASM>;
+  static KernelSlot slot;
+  int nb = 0;
+  if (int st = configure(slot, kernel, dev, NT, smem, &nb)) return st;
+  Sem3dArgs<T, 8> a = make_args<T, 8>(plan, fl);
+  a.prefetch = staged_arrays_aligned(fl, ASM) ? 1 : 0;
+  const long long nbatch = (plan->desc.nelem + EB - 1) / EB;
+  const long long cap = static_cast<long long>(sms) * nb;
+  const int grid = static_cast<int>(nbatch < cap ? nbatch : cap);
+  kernel<<<grid, NT, smem, stream>>>(a);
+  TO_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
 // Kernel variant for f32 NGLL 5 (TO_SEM3D_VARIANT; default 5):
 //   0 point-pair pipelined kernel, 8 elements x 2 CTAs/SM
 //   1 TMA-staged kernel, 8 elements x 2 CTAs/SM
@@ -235,6 +262,7 @@ int launch_lo(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t
 //   4 point-pair pipelined kernel, 16 elements x 1 CTA/SM
 //   5 line-owner kernel, 8 elements x 3 CTAs/SM
 //   6 line-owner kernel, 4 elements x 5 CTAs/SM
+//   7 line-owner kernel with scalar (unpacked) contractions
 int sem3d_f32_variant() {
   static const int v = [] {
     const char* e = std::getenv("TO_SEM3D_VARIANT");
@@ -264,13 +292,20 @@ int launch_sem3d(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStrea
       if (v == 4) return launch_v3<N, 16, 1, ASM>(plan, fl, stream, dev, sms);
       if (v == 6) return launch_v5<4, ASM ? 5 : 4, ASM>(plan, fl, stream, dev, sms);
       if (v == 0) return launch_v3<N, 8, 2, ASM>(plan, fl, stream, dev, sms);
+      if (v == 7) return launch_v5<8, ASM ? 3 : 2, ASM, false, 0>(plan, fl, stream, dev, sms);
       return launch_v5<8, ASM ? 3 : 2, ASM>(plan, fl, stream, dev, sms);
     }
   }
   if constexpr (N == 8) {
-    // NGLL 8 (f32 and f64): the line-owner kernel; TO_SEM3D_VARIANT=2 keeps
-    // the streaming kernel
-    if (sem3d_f32_variant() != 2)
+    // NGLL 8: fp64 takes the half-column kernel (2 owners per column, 16
+    // resident warps per SM: 59.5 vs 66.6 ms per 128^3 power step), fp32 the
+    // whole-column one (the half-column kernel measured 1.91 vs 1.59 ms at
+    // E=196,608); TO_SEM3D_VARIANT 10 / 12 force one or the other, 2 the
+    // streaming kernel
+    const int v = sem3d_f32_variant();
+    if (v == 10 || (sizeof(T) == 8 && v != 2 && v != 12))
+      return launch_hc<T, 2, sizeof(T) == 8 ? 2 : 3, ASM>(plan, fl, stream, dev, sms);
+    if (v != 2)
       return launch_lo<T, N, 2, sizeof(T) == 8 ? 2 : 3, ASM>(plan, fl, stream, dev, sms);
   }
   return launch_ldg<T, N, ASM>(plan, fl, stream, dev, sms);

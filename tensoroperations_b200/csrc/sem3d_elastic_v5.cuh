@@ -66,11 +66,32 @@ struct Sem3dV5Layout {
   static constexpr size_t kTotal = kHeader + kStageBytes + kXBytes + kEBytes;
 };
 
+// The kernel's parameters: the common arguments plus the operators splatted
+// into f32 pairs, so a packed FMA takes both lanes' coefficient from one
+// 64-bit constant.
+struct Sem3dV5Args {
+  Sem3dArgs<float, 5> a;
+  float2 H2[5][5];   // (H(i,p), H(i,p))
+  float2 Hw2[5][5];  // (Hw(q,i), Hw(q,i))
+};
+
+// Options of the line-owner kernel (OPT bit mask):
+//   kV5Packed    the contractions in packed f32x2 FMAs: each line owner pairs
+//                its xi and eta rows, each column owner pairs components 0
+//                and 1 (element-local NGLL 5 at E=786,432: 1.491 vs 1.518 ms;
+//                assembled 64^3: unchanged).
+// (Waiting for the staged geometry just before B2 instead of before A, so the
+// bulk copies also overlap A and B1, measured 0.597 vs 0.592 ms and was
+// removed.)
+enum : int { kV5Packed = 2 };
+
 // IL: assembled u and f interleaved per node (x, y, z, unused) -- one 128-bit
 // gather and one 128-bit atomicAdd per point instead of three of each.
-template <int EB, int MINB, bool ASM, bool IL = false>
+template <int EB, int MINB, bool ASM, bool IL = false, int OPT = kV5Packed>
 __global__ void __launch_bounds__(EB * 25, MINB)
-    sem3d_elastic_v5_kernel(const __grid_constant__ Sem3dArgs<float, 5> a) {
+    sem3d_elastic_v5_kernel(const __grid_constant__ Sem3dV5Args args) {
+  const Sem3dArgs<float, 5>& a = args.a;
+  constexpr bool kPk = (OPT & kV5Packed) != 0;
   using LY = Sem3dV5Layout<EB, ASM>;
   constexpr int N = 5, NN = 25, P = 125, NT = LY::NT, EP = LY::EP;
   constexpr int SKX = LY::SKX, SKE = LY::SKE;
@@ -182,6 +203,8 @@ __global__ void __launch_bounds__(EB * 25, MINB)
     int node[N];
 #pragma unroll
     for (int k = 0; k < N; ++k) node[k] = ASM ? node_n[k] : 0;
+    // Wait for this batch's staged arrays (bounded; on a timeout every thread
+    // leaves together after the copies have landed or the second wait ends).
     const bool ok = mbar_wait_bounded(bar, parity, kMbarMaxPolls);
     if (__syncthreads_or(!ok)) {
       if (tid == 0) atomicExch(&g_to_device_status, int(TO_ERR_TIMEOUT));
@@ -222,15 +245,31 @@ __global__ void __launch_bounds__(EB * 25, MINB)
           RX[c * CX + k * SKX + tid] = uc[c][k];
           RE[c * CE + k * SKE + tid] = uc[c][k];
         }
-#pragma unroll
-      for (int c = 0; c < 3; ++c)
+      if constexpr (kPk) {
 #pragma unroll
         for (int k = 0; k < N; ++k) {
-          float s = 0.f;
+          float2 s01 = make_float2(0.f, 0.f);
+          float s2 = 0.f;
 #pragma unroll
-          for (int p = 0; p < N; ++p) s = fmaf(a.ops.H[k][p], uc[c][p], s);
-          dgm[c][k] = s;
+          for (int p = 0; p < N; ++p) {
+            s01 = __ffma2_rn(args.H2[k][p], make_float2(uc[0][p], uc[1][p]), s01);
+            s2 = fmaf(a.ops.H[k][p], uc[2][p], s2);
+          }
+          dgm[0][k] = s01.x;
+          dgm[1][k] = s01.y;
+          dgm[2][k] = s2;
         }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 3; ++c)
+#pragma unroll
+          for (int k = 0; k < N; ++k) {
+            float s = 0.f;
+#pragma unroll
+            for (int p = 0; p < N; ++p) s = fmaf(a.ops.H[k][p], uc[c][p], s);
+            dgm[c][k] = s;
+          }
+      }
     }
     __syncthreads();
 
@@ -246,10 +285,18 @@ __global__ void __launch_bounds__(EB * 25, MINB)
 #pragma unroll
       for (int o = 0; o < N; ++o) {
         float sx = 0.f, se = 0.f;
+        if constexpr (kPk) {
+          float2 s = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int p = 0; p < N; ++p) {
-          sx = fmaf(a.ops.H[o][p], v[p], sx);
-          se = fmaf(a.ops.H[o][p], w[p], se);
+          for (int p = 0; p < N; ++p) s = __ffma2_rn(args.H2[o][p], make_float2(v[p], w[p]), s);
+          sx = s.x;
+          se = s.y;
+        } else {
+#pragma unroll
+          for (int p = 0; p < N; ++p) {
+            sx = fmaf(a.ops.H[o][p], v[p], sx);
+            se = fmaf(a.ops.H[o][p], w[p], se);
+          }
         }
         RDX[c * CX + lx + o] = sx;
         RDE[c * CE + ly + o * N] = se;
@@ -336,10 +383,18 @@ __global__ void __launch_bounds__(EB * 25, MINB)
 #pragma unroll
       for (int o = 0; o < N; ++o) {
         float sx = 0.f, se = 0.f;
+        if constexpr (kPk) {
+          float2 s = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int q = 0; q < N; ++q) {
-          sx = fmaf(a.ops.Hw[q][o], v[q], sx);
-          se = fmaf(a.ops.Hw[q][o], w[q], se);
+          for (int q = 0; q < N; ++q) s = __ffma2_rn(args.Hw2[q][o], make_float2(v[q], w[q]), s);
+          sx = s.x;
+          se = s.y;
+        } else {
+#pragma unroll
+          for (int q = 0; q < N; ++q) {
+            sx = fmaf(a.ops.Hw[q][o], v[q], sx);
+            se = fmaf(a.ops.Hw[q][o], w[q], se);
+          }
         }
         RDX[c * CX + lx + o] = sx;
         RDE[c * CE + ly + o * N] = se;
@@ -354,11 +409,30 @@ __global__ void __launch_bounds__(EB * 25, MINB)
       for (int k = 0; k < N; ++k) {
         const float wjk = wj * a.ops.w[k], wik = wi * a.ops.w[k];
         float fc[3];
+        float gg[3];
+        if constexpr (kPk) {
+          float2 g01 = make_float2(0.f, 0.f);
+          float g2 = 0.f;
+#pragma unroll
+          for (int q = 0; q < N; ++q) {
+            g01 = __ffma2_rn(args.Hw2[q][k], make_float2(Fg[0][q], Fg[1][q]), g01);
+            g2 = fmaf(a.ops.Hw[q][k], Fg[2][q], g2);
+          }
+          gg[0] = g01.x;
+          gg[1] = g01.y;
+          gg[2] = g2;
+        } else {
+#pragma unroll
+          for (int c = 0; c < 3; ++c) {
+            float g = 0.f;
+#pragma unroll
+            for (int q = 0; q < N; ++q) g = fmaf(a.ops.Hw[q][k], Fg[c][q], g);
+            gg[c] = g;
+          }
+        }
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
-          float g = 0.f;
-#pragma unroll
-          for (int q = 0; q < N; ++q) g = fmaf(a.ops.Hw[q][k], Fg[c][q], g);
+          const float g = gg[c];
           const float tx = RDX[c * CX + k * SKX + tid];
           const float te = RDE[c * CE + k * SKE + tid];
           fc[c] = fmaf(wij, g, fmaf(wik, te, wjk * tx));

@@ -44,6 +44,39 @@ def test_ngll8_operator(dtype, assembled):
     assert osem.rel_l2(got, ref) < TOL[dtype]
 
 
+@pytest.mark.parametrize("variant", ["10", "12", "2"])
+def test_every_ngll8_kernel_matches_oracle(variant):
+    """TO_SEM3D_VARIANT forces the NGLL-8 kernel (10: half-column, the fp64
+    default; 12: whole-column, the fp32 default; 2: register streaming); each is
+    checked in a fresh process for both precisions, assembled and element-local,
+    with a partial last batch."""
+    import os
+    import subprocess
+    import sys
+    code = (
+        "import numpy as np, torch\n"
+        "from oracle import sem as osem\n"
+        "from tensoroperations_b200 import abi\n"
+        "from tensoroperations_b200.sem3d import structured_problem, to_device\n"
+        "for dt, tol in ((np.float64, 1e-12), (np.float32, 1e-5)):\n"
+        "    for asm, mesh in ((True, (3, 2, 3)), (False, (5, 1, 1))):\n"
+        "        p = structured_problem(*mesh, ngll=8, dtype=dt, assembled=asm, seed=5)\n"
+        "        u, f, a, ib = to_device(p, 'cuda')\n"
+        "        pl = p.plan(); pl.apply(pl.fields(u, f, a, ib)); torch.cuda.synchronize()\n"
+        "        got = [x.cpu().numpy() for x in f]\n"
+        "        ref = (osem.assembled(p.nelem, 8, p.nglob, p.ibool, p.u, p.arrays, p.H, p.Hw, p.w, dt)\n"
+        "               if asm else osem.local(p.nelem, 8, p.u, p.arrays, p.H, p.Hw, p.w, dt))\n"
+        "        err = osem.rel_l2(got, ref)\n"
+        "        assert err <= tol, (dt, asm, err)\n"
+        "abi.check(abi.lib.to_device_status(0), 'status')\n"
+        "print('ok')\n")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, TO_SEM3D_VARIANT=variant, PYTHONPATH=root)
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True,
+                       text=True, timeout=600)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout + r.stderr
+
+
 @pytest.mark.parametrize("dtype", [np.float64, np.float32])
 @pytest.mark.parametrize("n,first", [(1, 0), (1000, 7), (200_003, 11), (131072, 0)])
 def test_sumsq3(dtype, n, first):

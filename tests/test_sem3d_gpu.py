@@ -152,7 +152,7 @@ def test_unaligned_arrays_take_the_streaming_kernel_and_match():
     assert osem.rel_l2([x.cpu().numpy() for x in f], _oracle(prob)) <= 1e-5
 
 
-@pytest.mark.parametrize("variant", ["0", "1", "2", "3", "4", "5", "6"])
+@pytest.mark.parametrize("variant", ["0", "1", "2", "3", "4", "5", "6", "7"])
 def test_every_kernel_variant_matches_oracle(variant):
     """TO_SEM3D_VARIANT selects the f32 kernel (0: point-pair pipelined 8 elements x
     2 CTAs/SM, 1: TMA-staged 8 x 2, 2: register streaming, 3: point-pair 4 x 4,
