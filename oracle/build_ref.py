@@ -20,6 +20,11 @@ are what the tests use on the GPU box, which has no reference tree.
                           2D P-SV program: the tree route make_graph().ops /
                           nested bundles, the DAG and multi-output DAG routes,
                           its hand-written and CONTROL kernels), the same way.
+  bench_permuted_contraction, bench_multilevel_contraction,
+  bench_permuted_combine, bench_team_contraction
+                          the contraction benchmarks (tree route, nested and
+                          flat tile bundles, hooks, LayoutLeft views), the
+                          same way.
   libref_sem2d.so         that 2D source compiled host-only through
                           oracle/ref_pin2d.cpp: its fill_field(),
                           fill_operators() and host_reference() behind a C
@@ -42,6 +47,8 @@ REF = Path(os.environ.get("TO_REFERENCE_ROOT", "/root/reference"))
 SEM3D = REF / "benchmarks" / "sem_stiffness_3d" / "bench_sem3d_levelgraph.cpp"
 SEM3D_DAG = REF / "benchmarks" / "sem_stiffness_3d" / "bench_sem_stiffness_3d.cpp"
 SEM2D = REF / "benchmarks" / "sem_stiffness" / "bench_sem_stiffness.cpp"
+CONTRACTION_BENCHES = ("permuted_contraction", "multilevel_contraction", "permuted_combine",
+                       "team_contraction")
 INC = [f"-I{ROOT / 'include'}", f"-I{ROOT / 'tensoroperations_b200' / 'include'}"]
 LIBDIR = ROOT / "tensoroperations_b200"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
@@ -87,7 +94,9 @@ def build(force: bool = False):
               *INC, f'-DBENCH_SEM2D_SOURCE="{SEM2D}"', str(HERE / "ref_pin2d.cpp"),
               f"-L{LIBDIR}", "-ltensoroperations_b200", f"-Wl,-rpath,{LIBDIR}",
               "-Wl,-rpath,$ORIGIN/../../tensoroperations_b200", "-o", str(PIN2D)])
-    for src, out in ((SEM3D, DROPIN), (SEM3D_DAG, DROPIN_DAG), (SEM2D, DROPIN_2D)):
+    progs = [(SEM3D, DROPIN), (SEM3D_DAG, DROPIN_DAG), (SEM2D, DROPIN_2D)]
+    progs += [(REF / "benchmarks" / b / f"bench_{b}.cpp", OUT / f"bench_{b}") for b in CONTRACTION_BENCHES]
+    for src, out in progs:
         if src.exists() and (force or _stale(out, deps + [src, LIBDIR / "libtensoroperations_b200.so"])):
             _nvcc_program(src, out)
     return PIN, DROPIN, DROPIN_DAG, DROPIN_2D, PIN2D

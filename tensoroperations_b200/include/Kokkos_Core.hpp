@@ -7,7 +7,7 @@
 // <Kokkos_Core.hpp> and declares its tensors as Kokkos::View -- compiles
 // unchanged against the B200 frontend.  What it provides:
 //
-//   Views       View<DataType, Props...> with LayoutRight, mixed static and
+//   Views       View<DataType, Props...> with LayoutRight or LayoutLeft, mixed static and
 //               dynamic extents ("float*[5][5][5]", "float****"), HostSpace /
 //               CudaSpace / team-scratch memory, managed (reference counted,
 //               zero-initialised) or unmanaged; create_mirror_view[_and_copy],
@@ -204,11 +204,16 @@ struct ScratchMemorySpace {
   ScratchMemorySpace() = default;
   KOKKOS_INLINE_FUNCTION ScratchMemorySpace(void* base, std::size_t size)
       : base_(static_cast<char*>(base)), size_(size), used_(0) {}
+  // A request past the size set on the policy is reported and answered with
+  // the start of the team's region when the request alone fits there (the
+  // results are then wrong, and the message says why), so that an
+  // under-sized policy never sends the kernel outside its shared memory; a
+  // request larger than the whole region gets a null pointer.
   KOKKOS_INLINE_FUNCTION void* get_shmem(std::size_t bytes) const {
     const std::size_t b = (bytes + align - 1) & ~(align - 1);
     if (used_ + b > size_) {
       Kokkos::abort("team scratch request exceeds the size set on the policy");
-      return nullptr;
+      return b <= size_ ? static_cast<void*>(base_) : nullptr;
     }
     void* p = base_ + used_;
     used_ += b;
@@ -340,7 +345,7 @@ template <class DataType, class... Props>
 class View {
   using DA = Impl::DataAnalysis<DataType>;
   using PA = Impl::PropsAnalysis<Props...>;
-  static_assert(!PA::layout_left, "this Kokkos subset implements LayoutRight only");
+  static constexpr bool kLeft = PA::layout_left;
 
  public:
   using data_type = DataType;
@@ -349,7 +354,7 @@ class View {
   using non_const_value_type = std::remove_const_t<value_type>;
   using pointer_type = value_type*;
   using reference_type = value_type&;
-  using array_layout = LayoutRight;
+  using array_layout = std::conditional_t<kLeft, LayoutLeft, LayoutRight>;
   using memory_space = typename PA::memory_space;
   using execution_space = typename memory_space::execution_space;
   using device_type = View;
@@ -361,7 +366,7 @@ class View {
   using non_const_data_type = std::remove_const_t<DataType>;
   using host_mirror_type =
       std::conditional_t<std::is_same_v<memory_space, HostSpace>, View<DataType, Props...>,
-                         View<non_const_data_type, LayoutRight, HostSpace>>;
+                         View<non_const_data_type, array_layout, HostSpace>>;
   using HostMirror = host_mirror_type;
 
  private:
@@ -484,7 +489,11 @@ class View {
   }
   KOKKOS_INLINE_FUNCTION std::size_t stride(int d) const {
     std::size_t s = 1;
-    for (int q = rank - 1; q > d; --q) s *= extent(q);
+    if constexpr (kLeft) {
+      for (int q = 0; q < d; ++q) s *= extent(q);
+    } else {
+      for (int q = rank - 1; q > d; --q) s *= extent(q);
+    }
     return s;
   }
   KOKKOS_INLINE_FUNCTION std::size_t size() const {
@@ -504,8 +513,14 @@ class View {
     static_assert(sizeof...(I) == rank || (rank == 0 && sizeof...(I) == 0),
                   "View: one index per rank");
     std::size_t off = 0;
-    int d = 0;
-    ((off = off * extent(d++) + static_cast<std::size_t>(idx)), ...);
+    if constexpr (kLeft) {
+      // first index fastest: fold from the last index down
+      const std::size_t ix[] = {static_cast<std::size_t>(idx)..., 0};
+      for (int d = rank - 1; d >= 0; --d) off = off * extent(d) + ix[d];
+    } else {
+      int d = 0;
+      ((off = off * extent(d++) + static_cast<std::size_t>(idx)), ...);
+    }
     return data_[off];
   }
   KOKKOS_FORCEINLINE_FUNCTION reference_type operator[](std::size_t i) const { return data_[i]; }
@@ -522,6 +537,10 @@ void deep_copy(const View<D1, P1...>& dst, const View<D2, P2...>& src) {
   using T1 = typename View<D1, P1...>::non_const_value_type;
   using T2 = typename View<D2, P2...>::non_const_value_type;
   static_assert(std::is_same_v<T1, T2>, "deep_copy: value types differ");
+  static_assert(std::is_same_v<typename View<D1, P1...>::array_layout,
+                               typename View<D2, P2...>::array_layout> ||
+                    View<D1, P1...>::rank <= 1,
+                "deep_copy: this Kokkos subset copies between views of one layout");
   if (dst.span() != src.span()) {
     std::fprintf(stderr, "Kokkos::deep_copy: extents differ (%zu vs %zu)\n", dst.span(),
                  src.span());
@@ -680,12 +699,14 @@ class TeamPolicy {
   TeamPolicy(int league, AUTO_t, int) : league_(league), team_(-1) {}
   TeamPolicy(const execution_space&, int league, int team) : league_(league), team_(team) {}
   TeamPolicy(const execution_space&, int league, AUTO_t) : league_(league), team_(-1) {}
-  TeamPolicy set_scratch_size(int level, PerTeamValue v) const {
-    TeamPolicy p = *this;
-    p.scratch_[level ? 1 : 0] = v.value;
-    return p;
+  // Sets the request in place and returns the policy, as Kokkos does: both
+  // `policy.set_scratch_size(0, PerTeam(b));` and a chained call on a
+  // temporary reach the launch.
+  TeamPolicy& set_scratch_size(int level, PerTeamValue v) {
+    scratch_[level ? 1 : 0] = v.value;
+    return *this;
   }
-  TeamPolicy set_scratch_size(int level, PerTeamValue v, PerThreadValue) const {
+  TeamPolicy& set_scratch_size(int level, PerTeamValue v, PerThreadValue) {
     return set_scratch_size(level, v);
   }
   int league_size() const { return league_; }

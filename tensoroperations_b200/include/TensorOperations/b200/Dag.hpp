@@ -510,7 +510,7 @@ struct DagLowering {
                             typename N::decl_seq, typename N::value_type, typename N::exec_space,
                             typename N::hook_type>;
     static type make(const N& n) {
-      return type{lower_op<K, 0>(n.node_a), lower_op<K, 1>(n.node_b), n.shape_};
+      return type{lower_op<K, 0>(n.node_a), lower_op<K, 1>(n.node_b), n.shape_, n.hook_op};
     }
   };
   template <std::size_t K, class N>

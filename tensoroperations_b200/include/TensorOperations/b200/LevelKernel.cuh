@@ -65,6 +65,11 @@ __device__ __forceinline__ auto& view_at(const View& v, const long long* g, std:
   return v(g[I]...);
 }
 
+template <class Op, class C, class V, std::size_t... I>
+__device__ __forceinline__ void call_hook(const Op& op, const C* g, V& v, std::index_sequence<I...>) {
+  op(static_cast<int>(g[I])..., v);
+}
+
 template <class V, class Lay, std::size_t S>
 __device__ __forceinline__ V* slot_ptr(unsigned char* smem) {
   constexpr std::size_t off = Lay::slot_offset(S);
@@ -90,7 +95,12 @@ __device__ __forceinline__ void stage_one(const tuple_element_t<M, tuple_element
     in = in && g[d] < static_cast<long long>(view.extent(d));
   });
   V* out = slot_ptr<V, Lay, S>(smem);
-  out[t] = in ? static_cast<V>(view_at(view, g, std::make_index_sequence<R>{})) : V(0);
+  V v = in ? static_cast<V>(view_at(view, g, std::make_index_sequence<R>{})) : V(0);
+  using Hook = decltype(node.operand_.hook_op);
+  if constexpr (!std::is_same_v<Hook, NoHook>) {
+    if (in) call_hook(node.operand_.hook_op, g, v, std::make_index_sequence<R>{});
+  }
+  out[t] = v;
 }
 
 template <class V, class Lay, class GS, class LT, class Levels, std::size_t L, std::size_t... M>
@@ -135,8 +145,10 @@ __device__ __forceinline__ int label_offset_extents_of(int idx) {
   return off;
 }
 
-template <class V, class Lay, class Levels, std::size_t L, std::size_t M>
-__device__ __forceinline__ void contract_one(unsigned char* smem, int a, int b, int t) {
+template <class V, class Lay, class GS, class LT, class Levels, std::size_t L, std::size_t M>
+__device__ __forceinline__ void contract_one(const tuple_element_t<M, tuple_element_t<L, Levels>>& node,
+                                             const int* tile_idx, unsigned char* smem, int a, int b,
+                                             int t) {
   using Node = tuple_element_t<M, tuple_element_t<L, Levels>>;
   using A = typename Node::node_a_type;
   using B = typename Node::node_b_type;
@@ -159,17 +171,37 @@ __device__ __forceinline__ void contract_one(unsigned char* smem, int a, int b, 
     for (int k = 0; k < SK; ++k)
       acc += pa[label_offset_extents_of<A, A, cont>(k)] * pb[label_offset_extents_of<A, B, cont>(k)];
   }
+  if constexpr (!std::is_same_v<typename Node::hook_type, NoHook>) {
+    // the element's global coordinates in the node's DECLARED order
+    constexpr int R = Node::Rank;
+    using STile = typename MT::tile;
+    constexpr auto decl = to_array<typename MT::decl_labels>();
+    constexpr auto perm = MT::decl_to_storage;
+    int c[R > 0 ? R : 1];
+    decode_tile<STile>(t, c);
+    long long g[R > 0 ? R : 1];
+    bool in = true;
+    const auto shape = node.shape();  // canonical
+    static_for<R>([&](auto dc) {
+      constexpr int d = decltype(dc)::value;
+      constexpr int32_t l = decl[d];
+      g[d] = label_origin<GS, LT, l>(tile_idx) + c[perm[d]];
+      in = in && g[d] < shape[perm[d]];
+    });
+    if (in) call_hook(node.hook_op, g, acc, std::make_index_sequence<R>{});
+  }
   slot_ptr<V, Lay, SC>(smem)[t] = acc;
 }
 
-template <class V, class Lay, class Levels, std::size_t L, std::size_t... M>
-__device__ void run_contraction_level(unsigned char* smem, std::index_sequence<M...>) {
+template <class V, class Lay, class GS, class LT, class Levels, std::size_t L, std::size_t... M>
+__device__ void run_contraction_level(const tuple_element_t<L, Levels>& lvl, const int* tile_idx,
+                                      unsigned char* smem, std::index_sequence<M...>) {
   using MT0 = member_traits<tuple_element_t<0, tuple_element_t<L, Levels>>>;
   constexpr int SA = MT0::sa, SB = MT0::sb;
   for (int t = threadIdx.x; t < SA * SB; t += blockDim.x) {
     const int a = t / SB;
     const int b = t - a * SB;
-    (contract_one<V, Lay, Levels, L, M>(smem, a, b, t), ...);
+    (contract_one<V, Lay, GS, LT, Levels, L, M>(lvl.template get<M>(), tile_idx, smem, a, b, t), ...);
   }
 }
 
@@ -259,7 +291,7 @@ __device__ __forceinline__ void run_level(const Levels& levels, const int* tile_
   if constexpr (kind == 0)
     run_stage_level<V, Lay, GS, LT, Levels, L>(levels.template get<L>(), tile_idx, smem, Ms{});
   else if constexpr (kind == 1)
-    run_contraction_level<V, Lay, Levels, L>(smem, Ms{});
+    run_contraction_level<V, Lay, GS, LT, Levels, L>(levels.template get<L>(), tile_idx, smem, Ms{});
   else
     run_combine_level<V, Lay, GS, LT, Levels, L>(levels.template get<L>(), tile_idx, smem, Ms{});
   __syncthreads();

@@ -182,6 +182,28 @@ struct exec_of<T, std::void_t<typename T::execution_space>> {
 };
 }  // namespace b200
 
+namespace b200 {
+// Hooks: op(i_0, ..., i_{Rank-1}, value&) applied in place to every element of
+// a node's tile at its global coordinates (reference NodeHandle.hpp:258-266,
+// Evaluator.hpp:59-77).
+template <int N, typename... Acc>
+struct ints_tuple {
+  using type = typename ints_tuple<N - 1, int, Acc...>::type;
+};
+template <typename... Acc>
+struct ints_tuple<0, Acc...> {
+  using type = std::tuple<Acc...>;
+};
+template <typename Op, typename V, typename Tup>
+struct hook_invocable;
+template <typename Op, typename V, typename... Is>
+struct hook_invocable<Op, V, std::tuple<Is...>> : std::is_invocable<const Op&, Is..., V&> {};
+template <typename Op, int Rank, typename V>
+constexpr bool hook_like() {
+  return hook_invocable<Op, V, typename ints_tuple<Rank>::type>::value;
+}
+}  // namespace b200
+
 // Input: a labelled tensor.
 template <typename T, typename ModesSeq, typename HookOp>
 struct NodeHandle<InputTag, T, ModesSeq, HookOp> {
@@ -203,6 +225,10 @@ struct NodeHandle<InputTag, T, ModesSeq, HookOp> {
 
 template <typename T, typename ModesSeq, typename HookOp = NoHook>
 auto make_input_node(TensorHandle<T, ModesSeq> h, HookOp hook = {}) {
+  static_assert(std::is_same_v<HookOp, NoHook> ||
+                    b200::hook_like<HookOp, static_cast<int>(ModesSeq::size()),
+                                    typename b200::value_of<T>::type>(),
+                "input hook must be callable as op(i_0, ..., i_{Rank-1}, value_type&)");
   return NodeHandle<InputTag, T, ModesSeq, HookOp>{h, hook};
 }
 
@@ -327,6 +353,7 @@ struct NodeHandle<ContractionTag, NodeA, NodeB, OutSeq, Scalar, ExecSpace, HookO
   NodeA node_a;
   NodeB node_b;
   Kokkos::Array<int, Rank> shape_;  // canonical order
+  HookOp hook_op;  // op(i_0.., i_{Rank-1}, value&) on every output element, declared order
 
   KOKKOS_INLINE_FUNCTION Kokkos::Array<int, Rank> shape() const { return shape_; }
 };
@@ -355,7 +382,7 @@ constexpr bool valid_contraction() {
 namespace Impl {
 template <typename Scalar, typename ExecSpace, int32_t... OutModes, typename NodeA, typename NodeB,
           typename HookOp>
-auto make_contraction_node_impl(NodeA a, NodeB b, HookOp) {
+auto make_contraction_node_impl(NodeA a, NodeB b, HookOp hook) {
   using AL = typename NodeA::modes_seq;
   using BL = typename NodeB::modes_seq;
   using OutSeq = Labels<OutModes...>;
@@ -363,10 +390,9 @@ auto make_contraction_node_impl(NodeA a, NodeB b, HookOp) {
                 "each output mode must appear in exactly one input tensor, output modes "
                 "must be pairwise distinct, and the output rank must equal the number "
                 "of free modes");
-  static_assert(std::is_same_v<HookOp, NoHook>,
-                "level graph: contraction hooks are not supported; apply the transform in "
-                "a combine member instead");
   using Node = NodeHandle<ContractionTag, NodeA, NodeB, OutSeq, Scalar, ExecSpace, HookOp>;
+  static_assert(std::is_same_v<HookOp, NoHook> || b200::hook_like<HookOp, Node::Rank, Scalar>(),
+                "contraction hook must be callable as op(i_0, ..., i_{Rank-1}, value_type&)");
   constexpr auto al = b200::to_array<AL>();
   constexpr auto bl = b200::to_array<BL>();
   const auto as = a.shape();
@@ -379,7 +405,7 @@ auto make_contraction_node_impl(NodeA a, NodeB b, HookOp) {
   Kokkos::Array<int, Node::Rank> shape{};
   for (int i = 0; i < Node::FreeA; ++i) shape[i] = as[b200::index_of(al, Node::freeA[i])];
   for (int i = 0; i < Node::FreeB; ++i) shape[Node::FreeA + i] = bs[b200::index_of(bl, Node::freeB[i])];
-  return Node{a, b, shape};
+  return Node{a, b, shape, hook};
 }
 }  // namespace Impl
 

@@ -102,7 +102,7 @@ struct TreeLowering {
       using B = std::decay_t<decltype(std::get<1>(rb))>;
       using C = NodeHandle<ContractionTag, A, B, typename Node::decl_seq, typename Node::value_type,
                            typename Node::exec_space, typename Node::hook_type>;
-      const C c{std::get<1>(ra), std::get<1>(rb), node.shape_};
+      const C c{std::get<1>(ra), std::get<1>(rb), node.shape_, node.hook_op};
       using TS = Tile<typename plain_tile<typename Spec::a_type>::type,
                       typename plain_tile<typename Spec::b_type>::type, typename Spec::c_type>;
       return finish(std::get<0>(rb), c, TS{});

@@ -9,8 +9,8 @@
 // gradient contractions on INPUT nodes -- declared in the consumer's order, so
 // the combine reads them through their storage permutation.  Case 2 is a
 // contraction chain R = (A . B) . C given as a flat pre-order list of
-// Tile<A,B,C> bundles (reference Graph.hpp:316-327).  Both with a partial last
-// tile.  Built and run by tests/test_frontend_cpu.py under ASan/UBSan.
+// Tile<A,B,C> bundles (reference Graph.hpp:316-327), with a contraction hook
+// and an input hook.  Both with a partial last tile.  Built and run by tests/test_frontend_cpu.py under ASan/UBSan.
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -171,11 +171,16 @@ int main(int argc, char** argv) {
     for (int n = 0; n < E * N * K; ++n) A.data()[n] = std::sin(0.05f * n + 1.f);
     for (int n = 0; n < K * N * N; ++n) B.data()[n] = std::cos(0.13f * n);
     for (int n = 0; n < N * N * N; ++n) C.data()[n] = 0.01f * (n % 17) - 0.05f;
-    // T(e, a, b, c) = sum_k A(e, a, k) B(k, b, c)
-    auto T = make_contraction_node<'e', 'a', 'b', 'c'>(make_input_node(make_handle<'e', 'a', 'k'>(A)),
-                                                       make_input_node(make_handle<'k', 'b', 'c'>(B)));
+    // T(e, a, b, c) = sum_k A(e, a, k) B(k, b, c), then the contraction hook
+    // T += 0.01 (a + 1) c at its global, declared-order coordinates; C passes
+    // through an input hook C *= 1 + 0.1 d when staged
+    auto T = make_contraction_node<'e', 'a', 'b', 'c'>(
+        make_input_node(make_handle<'e', 'a', 'k'>(A)), make_input_node(make_handle<'k', 'b', 'c'>(B)),
+        [](int, int a, int, int c, float& v) { v += 0.01f * static_cast<float>((a + 1) * c); });
     // R(e, a, d) = sum_{b,c} T(e,a,b,c) C(b,c,d)
-    auto Rn = make_contraction_node<'e', 'a', 'd'>(T, make_input_node(make_handle<'b', 'c', 'd'>(C)));
+    auto Rn = make_contraction_node<'e', 'a', 'd'>(
+        T, make_input_node(make_handle<'b', 'c', 'd'>(C),
+                           [](int, int, int d, float& v) { v *= 1.f + 0.1f * static_cast<float>(d); }));
     using BT = Tile<StaticTile<TE, N, K>, StaticTile<K, N, N>, StaticTile<TE, N, N, N>>;
     using BR = Tile<StaticTile<TE, N, N, N>, StaticTile<N, N, N>, StaticTile<TE, N, N>>;
     using Spec = typename b200::assembled_tile<0, decltype(Rn), std::tuple<BR, BT>>::type;
@@ -203,7 +208,8 @@ int main(int argc, char** argv) {
             for (int c = 0; c < N; ++c) {
               double t = 0;
               for (int k = 0; k < K; ++k) t += A(e, a, k) * B(k, b, c);
-              want += static_cast<float>(t) * C(b, c, d);
+              t += 0.01 * (a + 1) * c;
+              want += static_cast<float>(t) * (C(b, c, d) * (1.0 + 0.1 * d));
             }
           worst = std::fmax(worst, std::fabs(R(e, a, d) - want));
           scale = std::fmax(scale, std::fabs(want));

@@ -17,6 +17,8 @@
   AddressSanitizer/UBSan against a direct loop, with a partial last tile.
 * dag_guard_negative.cpp: each DagGraph diagnostic fires on the graph it
   forbids; the control graph compiles.
+* kokkos_subset_host_check.cpp: the Kokkos subset on the host -- scratch
+  requests set on a policy by statement, LayoutLeft views, MDRangePolicy.
 * tree_host_check.cpp: the tree route (make_graph().ops with nested Tile /
   CombineTile bundles, and a flat pre-order tile list of a contraction chain)
   lowered through the DAG onto the level plan and run the same way.
@@ -135,3 +137,12 @@ def test_tree_lowering_host_emulation_under_sanitizers(tree_host_exe, elements):
                          timeout=120)
     assert run.returncode == 0, run.stdout + run.stderr
     assert "tree max abs error" in run.stdout and "chain max abs error" in run.stdout
+
+
+def test_kokkos_subset_on_the_host(tmp_path):
+    exe = tmp_path / "kk_host"
+    r = _compile(["-O1", "-g", "-fsanitize=address,undefined", "-fno-sanitize-recover=all",
+                  str(CPP / "kokkos_subset_host_check.cpp"), "-o", str(exe)], timeout=600)
+    assert r.returncode == 0, r.stderr[-3000:]
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 0 and "kokkos subset host ok" in run.stdout, run.stdout + run.stderr
