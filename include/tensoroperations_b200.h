@@ -377,7 +377,8 @@ typedef struct to_level_plan_desc {
   int32_t num_levels;
   int32_t num_slots;
   int32_t num_pools;
-  const int32_t* level_kind;    /* [num_levels] 0 stage, 1 contraction, 2 combine */
+  const int32_t* level_kind;    /* [num_levels] 0 stage, 1 contraction, 2 combine,
+                                   3 contraction staging its own operand tiles */
   const int32_t* level_members; /* [num_levels]                                */
   const int64_t* level_space;   /* [num_levels] items of the level's one loop  */
   const int32_t* slot_def;      /* [num_slots] level that writes the slot      */

@@ -24,7 +24,7 @@ extern "C" int to_level_plan_lower(const to_level_plan_desc* d, int32_t query_de
   // levels
   int64_t widest = 1;
   for (int l = 0; l < d->num_levels; ++l) {
-    if (d->level_kind[l] < 0 || d->level_kind[l] > 2 || d->level_members[l] <= 0)
+    if (d->level_kind[l] < 0 || d->level_kind[l] > 3 || d->level_members[l] <= 0)
       return set_error(TO_ERR_INVALID_ARGUMENT, "level %d: bad kind or empty", l);
     if (d->level_space[l] <= 0)
       return set_error(TO_ERR_INVALID_ARGUMENT, "level %d: empty iteration space", l);

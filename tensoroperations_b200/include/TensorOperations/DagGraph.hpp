@@ -131,18 +131,47 @@ struct DagGraph {
     using ViewT = std::tuple_element_t<0, std::tuple<ViewTs...>>;
     static_assert((std::is_same_v<ViewT, ViewTs> && ...),
                   "DagGraph::execute: output views must share one type");
-    using Low = lowering;
     if (!index_consistent())
       throw LevelGraphError(
           TO_ERR_INVALID_ARGUMENT,
           "DagGraph: a node's mode is either tiled differently from the grid node's or is "
           "multi-tiled and absent from it, so its tile index cannot be gathered from the grid "
           "node's. Retile so every shared mode matches and every unshared mode has one tile.");
+    if (needs_contracted_tiles()) {
+      using Low = lowering_ktiled;
+      const typename Low::graph_t g{Low::make_levels(nodes)};
+      return g.template launch<ES, Low::level_slot(Roots)...>(team_size, views...);
+    }
+    using Low = lowering;
     const typename Low::graph_t g{Low::make_levels(nodes)};
     return g.template launch<ES, Low::level_slot(Roots)...>(team_size, views...);
   }
 
-  using lowering = b200::DagLowering<ValueType, ExecSpace, NodesT, TilesL>;
+  using lowering = b200::DagLowering<ValueType, ExecSpace, NodesT, TilesL, false>;
+  using lowering_ktiled = b200::DagLowering<ValueType, ExecSpace, NodesT, TilesL, true>;
+
+  // True when a contraction of two inputs has a contracted label longer than
+  // its tile: the launch then loops over the contracted tiles.
+  bool needs_contracted_tiles() const {
+    bool need = false;
+    for_each_node([&]<std::size_t K>(const auto& node) {
+      using Node = std::decay_t<decltype(node)>;
+      if constexpr (b200::dag_is_contraction_v<Node>) {
+        if constexpr (b200::dag_is_input_v<typename Node::node_a_type> &&
+                      b200::dag_is_input_v<typename Node::node_b_type>) {
+          using TS = typename b200::tl_at<K, TilesL>::type;
+          constexpr auto ta = b200::dag_operand_tile<Node, TS, 0>();
+          constexpr auto la = b200::to_array<typename Node::AL>();
+          const auto sh = node.node_a.shape();
+          for (std::size_t c = 0; c < Node::contracted.size(); ++c) {
+            const int d = b200::index_of(la, Node::contracted[c]);
+            if (sh[d] > ta[d]) need = true;
+          }
+        }
+      }
+    });
+    return need;
+  }
 
   // Slots of the flat DAG (one per node output).
   static constexpr std::size_t num_slots() {

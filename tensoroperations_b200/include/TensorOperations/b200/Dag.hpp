@@ -22,7 +22,10 @@
 // turns the DAG into a level plan at compile time and launches the same device
 // evaluator as the level-graph route (LevelKernel.cuh):
 //   1. every input operand of a node becomes a STAGE item (the tile the node's
-//      Tile<A,B,C> or CombineTile names, copied on chip);
+//      Tile<A,B,C> or CombineTile names, copied on chip) -- except, when a
+//      contracted label of a contraction of two inputs spans several tiles at
+//      run time, that contraction becomes one self-staging member, which copies
+//      its operand tiles once per contracted tile and accumulates;
 //   2. items get a depth -- stages 0, a node one more than the deepest item it
 //      reads -- and the items of one depth are grouped into levels by kind and
 //      iteration space (stages by tile, contractions by SA x SB, combines by
@@ -33,12 +36,13 @@
 //      launch are the level graph's.
 // For the reference's SEM 3D program (24 nodes) this gives six levels: stage
 // H and Hw, stage u, 9 gradients, 3 three-output integrands, 9 divergences,
-// 3 weighted sums.
+// 3 weighted sums (five, with the gradients self-staging, where a contracted
+// label spans several tiles).
 //
 // Restrictions, each a compile-time diagnostic: nodes are contractions or
 // combines; operands are input nodes or handles of this graph; tiles are
-// static; a contracted label fits in one tile; a label staged twice has one
-// tile extent.
+// static; a label staged twice has one tile extent.  A contracted label of a
+// contraction that reads a handle must fit in one tile (checked at launch).
 #pragma once
 
 #include <array>
@@ -258,7 +262,12 @@ constexpr bool arrays_equal(const Arr& a, const Arr& b, std::index_sequence<I...
 // ---------------------------------------------------------------------------
 // The lowering of one graph type.
 // ---------------------------------------------------------------------------
-template <class V, class ES, class NodesT, class TilesL>
+// SelfStage: contractions of two inputs become self-staging members (kind 3)
+// that loop over the tiles of their contracted labels; otherwise their
+// operands are stage items like any other input.  A launch takes the second
+// form whenever every contracted label fits its tile (the common case, and
+// the cheaper kernel) and the first only when one does not.
+template <class V, class ES, class NodesT, class TilesL, bool SelfStage = false>
 struct DagLowering {
   static constexpr std::size_t NK = tuple_size_v<NodesT>;
   static_assert(NK > 0, "DagGraph::execute: the graph has no nodes");
@@ -269,7 +278,7 @@ struct DagLowering {
 
   // ---- per-node facts --------------------------------------------------------
   struct NodeRow {
-    int kind = 0;  // 1 contraction, 2 combine
+    int kind = 0;  // 1 contraction, 2 combine, 3 contraction of two inputs (staged by itself)
     int arity = 1;
     int nops = 0;
     int rank = 0;
@@ -286,7 +295,11 @@ struct DagLowering {
                   "DagGraph: too many operands in one node for this build");
     static_assert(N::Rank <= kDagMaxRank, "DagGraph: node rank above this build's maximum (8)");
     NodeRow r{};
-    r.kind = dag_is_contraction_v<N> ? 1 : 2;
+    r.kind = dag_is_combine_v<N> ? 2 : 1;
+    if constexpr (SelfStage && dag_is_contraction_v<N>) {
+      if constexpr (dag_is_input_v<typename N::node_a_type> && dag_is_input_v<typename N::node_b_type>)
+        r.kind = 3;
+    }
     r.arity = output_arity<N>();
     r.nops = static_cast<int>(dag_num_ops<N>());
     r.rank = N::Rank;
@@ -348,11 +361,12 @@ struct DagLowering {
   struct StageRef {
     std::size_t node = 0, pos = 0;
   };
+  // (a contraction of two inputs stages its operands itself: no stage items)
   static constexpr std::size_t NS = [] {
     std::size_t n = 0;
     for (std::size_t k = 0; k < NK; ++k)
       for (int p = 0; p < rows[k].nops; ++p)
-        if (rows[k].input[p]) ++n;
+        if (rows[k].input[p] && rows[k].kind != 3) ++n;
     return n;
   }();
   static constexpr std::array<StageRef, NS> stages = [] {
@@ -360,7 +374,7 @@ struct DagLowering {
     std::size_t n = 0;
     for (std::size_t k = 0; k < NK; ++k)
       for (int p = 0; p < rows[k].nops; ++p)
-        if (rows[k].input[p]) s[n++] = StageRef{k, static_cast<std::size_t>(p)};
+        if (rows[k].input[p] && rows[k].kind != 3) s[n++] = StageRef{k, static_cast<std::size_t>(p)};
     return s;
   }();
   static constexpr std::size_t stage_of(std::size_t k, std::size_t p) {
@@ -414,7 +428,11 @@ struct DagLowering {
     return d;
   }();
   static constexpr int item_depth(std::size_t i) { return i < NS ? 0 : depth[i - NS]; }
-  static constexpr int item_arity(std::size_t i) { return i < NS ? 1 : rows[i - NS].arity; }
+  // slots of the lowered member: a self-staging contraction also holds its
+  // two operand tiles
+  static constexpr int item_arity(std::size_t i) {
+    return i < NS ? 1 : (rows[i - NS].kind == 3 ? 3 : rows[i - NS].arity);
+  }
   static constexpr Sig item_sig(std::size_t i) {
     Sig s{};
     if (i < NS) {
@@ -424,7 +442,7 @@ struct DagLowering {
     } else {
       const NodeRow& r = rows[i - NS];
       s[0] = r.kind;
-      if (r.kind == 1) {
+      if (r.kind == 1 || r.kind == 3) {
         s[1] = r.sa;
         s[2] = r.sb;
       } else {
@@ -541,13 +559,43 @@ struct DagLowering {
       return type{dag_op<N, ref.pos>::get(nodes.template get<ref.node>())};
     }
   };
-  template <std::size_t I>
-  struct member<I, false> {
+  // A contraction of two inputs: one member that stages both operand tiles
+  // into its own slots base+1 and base+2, once per contracted tile.
+  template <std::size_t K, class N = node_t<K>>
+  struct staged_node {
+    static constexpr std::size_t base = plan.slot_base[NS + K];
+    using InA = typename N::node_a_type;
+    using InB = typename N::node_b_type;
+    static constexpr auto ta = dag_operand_tile<N, spec_t<K>, 0>();
+    static constexpr auto tb = dag_operand_tile<N, spec_t<K>, 1>();
+    using SA = SlotNode<V, ES, base + 1, typename InA::modes_seq, array_tile_t<ta>,
+                        std::make_integer_sequence<int, InA::Rank>>;
+    using SB = SlotNode<V, ES, base + 2, typename InB::modes_seq, array_tile_t<tb>,
+                        std::make_integer_sequence<int, InB::Rank>>;
+    using Cs = NodeHandle<ContractionTag, SA, SB, typename N::decl_seq, typename N::value_type,
+                          typename N::exec_space, typename N::hook_type>;
+    using type = NodeHandle<StagedContractionTag, InA, InB, Cs>;
+    static type make(const N& n) {
+      return type{n.node_a, n.node_b, Cs{SA{n.node_a.shape()}, SB{n.node_b.shape()}, n.shape_, n.hook_op}};
+    }
+  };
+
+  template <std::size_t I, bool = (rows[I - NS].kind == 3)>
+  struct node_member {
     using type = typename lowered_node<I - NS>::type;
     static type make(const NodesT& nodes) {
       return lowered_node<I - NS>::make(nodes.template get<I - NS>());
     }
   };
+  template <std::size_t I>
+  struct node_member<I, true> {
+    using type = typename staged_node<I - NS>::type;
+    static type make(const NodesT& nodes) {
+      return staged_node<I - NS>::make(nodes.template get<I - NS>());
+    }
+  };
+  template <std::size_t I>
+  struct member<I, false> : node_member<I> {};
 
   template <std::size_t L, std::size_t... M>
   static auto level_type_of(std::index_sequence<M...>)
@@ -578,11 +626,54 @@ struct DagLowering {
   static constexpr int root_rank = GridNode::Rank;
   static constexpr auto root_tile = dag_storage_tile<GridNode, spec_t<NK - 1>>();
 
+  // Labels every staged tile carries: the stage items', and the FREE labels of
+  // the self-staging contractions' operands (their contracted labels are
+  // looped over, so they are in neither the grid nor the whole-label checks).
+  struct StagedLabels {
+    std::size_t n = 0;
+    std::array<int32_t, kDagMaxRank * 2 * (NS + NK) + 1> lab{};
+    std::array<int, kDagMaxRank * 2 * (NS + NK) + 1> tile{};
+  };
+  template <std::size_t K>
+  static constexpr void note_staged_node(StagedLabels& m) {
+    using N = node_t<K>;
+    if constexpr (SelfStage && dag_is_contraction_v<N>) {
+      if constexpr (dag_is_input_v<typename N::node_a_type> && dag_is_input_v<typename N::node_b_type>) {
+        constexpr auto ta = dag_operand_tile<N, spec_t<K>, 0>();
+        constexpr auto tb = dag_operand_tile<N, spec_t<K>, 1>();
+        constexpr auto la = to_array<typename N::AL>();
+        constexpr auto lb = to_array<typename N::BL>();
+        for (std::size_t d = 0; d < la.size(); ++d)
+          if (index_of(N::contracted, la[d]) < 0) {
+            m.lab[m.n] = la[d];
+            m.tile[m.n++] = ta[d];
+          }
+        for (std::size_t d = 0; d < lb.size(); ++d)
+          if (index_of(N::contracted, lb[d]) < 0) {
+            m.lab[m.n] = lb[d];
+            m.tile[m.n++] = tb[d];
+          }
+      }
+    }
+  }
+  static constexpr StagedLabels staged_labels = [] {
+    StagedLabels m{};
+    for (std::size_t s = 0; s < NS; ++s)
+      for (int d = 0; d < srows[s].rank; ++d) {
+        m.lab[m.n] = srows[s].lab[d];
+        m.tile[m.n++] = srows[s].tile[d];
+      }
+    [&]<std::size_t... K>(std::index_sequence<K...>) {
+      (note_staged_node<K>(m), ...);
+    }(std::make_index_sequence<NK>{});
+    return m;
+  }();
+
   struct LabelMap {
     std::size_t n = 0;
-    std::array<int32_t, kDagMaxRank * (NS + 1)> lab{};
-    std::array<int, kDagMaxRank * (NS + 1)> ext{};
-    std::array<bool, kDagMaxRank * (NS + 1)> grid{};
+    std::array<int32_t, kDagMaxRank * 2 * (NS + NK + 1)> lab{};
+    std::array<int, kDagMaxRank * 2 * (NS + NK + 1)> ext{};
+    std::array<bool, kDagMaxRank * 2 * (NS + NK + 1)> grid{};
     bool consistent = true;
   };
   static constexpr LabelMap label_map = [] {
@@ -593,20 +684,19 @@ struct DagLowering {
       m.grid[m.n] = true;
       ++m.n;
     }
-    for (std::size_t s = 0; s < NS; ++s)
-      for (int d = 0; d < srows[s].rank; ++d) {
-        const int32_t l = srows[s].lab[d];
-        std::size_t i = 0;
-        while (i < m.n && m.lab[i] != l) ++i;
-        if (i < m.n) {
-          if (m.ext[i] != srows[s].tile[d]) m.consistent = false;
-        } else {
-          m.lab[m.n] = l;
-          m.ext[m.n] = srows[s].tile[d];
-          m.grid[m.n] = false;
-          ++m.n;
-        }
+    for (std::size_t q = 0; q < staged_labels.n; ++q) {
+      const int32_t l = staged_labels.lab[q];
+      std::size_t i = 0;
+      while (i < m.n && m.lab[i] != l) ++i;
+      if (i < m.n) {
+        if (m.ext[i] != staged_labels.tile[q]) m.consistent = false;
+      } else {
+        m.lab[m.n] = l;
+        m.ext[m.n] = staged_labels.tile[q];
+        m.grid[m.n] = false;
+        ++m.n;
       }
+    }
     return m;
   }();
   static_assert(label_map.consistent,
@@ -636,9 +726,8 @@ struct DagLowering {
   static constexpr std::array<bool, root_rank> root_label_staged = [] {
     std::array<bool, root_rank> f{};
     for (int d = 0; d < root_rank; ++d)
-      for (std::size_t s = 0; s < NS; ++s)
-        for (int a = 0; a < srows[s].rank; ++a)
-          if (srows[s].lab[a] == root_labels[d]) f[d] = true;
+      for (std::size_t q = 0; q < staged_labels.n; ++q)
+        if (staged_labels.lab[q] == root_labels[d]) f[d] = true;
     return f;
   }();
 };

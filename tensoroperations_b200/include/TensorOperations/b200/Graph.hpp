@@ -146,24 +146,40 @@ struct LevelGraph {
     std::array<bool, GS::rank> seen{};
     std::vector<long long> wext;
     std::vector<int> wtile;
+    // one staged label: a grid extent, or a whole label that must fit its tile
+    auto note_label = [&](int32_t l, long long extent, int tile) {
+      const int g = GS::grid_slot(l);
+      if (g < 0) {
+        wext.push_back(extent);
+        wtile.push_back(tile);
+      } else {
+        if (seen[g] && gext[g] != extent)
+          throw LevelGraphError(TO_ERR_INVALID_ARGUMENT,
+                                "grid: two inputs disagree on a label's extent");
+        gext[g] = extent;
+        seen[g] = true;
+      }
+    };
     for_each_member([&](const auto& m) {
       using Node = std::decay_t<decltype(m)>;
       if constexpr (b200::member_traits<Node>::kind == 0) {
         constexpr auto lab = b200::to_array<typename Node::modes_seq>();
         const auto sh = m.shape();
-        for (int d = 0; d < Node::Rank; ++d) {
-          const int g = GS::grid_slot(lab[d]);
-          if (g < 0) {
-            wext.push_back(sh[d]);
-            wtile.push_back(LabelTilesT::tile(lab[d]));
-          } else {
-            if (seen[g] && gext[g] != sh[d])
-              throw LevelGraphError(TO_ERR_INVALID_ARGUMENT,
-                                    "grid: two inputs disagree on a label's extent");
-            gext[g] = sh[d];
-            seen[g] = true;
-          }
-        }
+        for (int d = 0; d < Node::Rank; ++d) note_label(lab[d], sh[d], LabelTilesT::tile(lab[d]));
+      } else if constexpr (b200::member_traits<Node>::kind == 3) {
+        // the free labels of both operands; contracted labels are looped over
+        using C = typename Node::contraction_type;
+        auto note_operand = [&](const auto& in, auto slot_tag) {
+          using In = std::decay_t<decltype(in)>;
+          using SlotOp = typename decltype(slot_tag)::type;
+          constexpr auto lab = b200::to_array<typename In::modes_seq>();
+          const auto sh = in.shape();
+          for (int d = 0; d < In::Rank; ++d)
+            if (b200::index_of(C::contracted, lab[d]) < 0)
+              note_label(lab[d], sh[d], SlotOp::storage_tile::extents[d]);
+        };
+        note_operand(m.in_a, std::type_identity<typename C::node_a_type>{});
+        note_operand(m.in_b, std::type_identity<typename C::node_b_type>{});
       }
     });
     std::array<int, GS::rank> gtile{};
@@ -285,7 +301,7 @@ struct LevelGraph {
            using MT = b200::member_traits<tuple_element_t<0, Lvl>>;
            kind[L] = MT::kind;
            mem[L] = static_cast<int32_t>(tuple_size_v<Lvl>);
-           if constexpr (MT::kind == 1)
+           if constexpr (MT::kind == 1 || MT::kind == 3)
              space[L] = static_cast<int64_t>(MT::sa) * MT::sb;
            else
              space[L] = MT::tile::num_elements;

@@ -32,6 +32,7 @@ struct ContractionTag {};
 struct CombineTag {};
 struct SlotTag {};
 struct StagedTag {};
+struct StagedContractionTag {};
 struct NoHook {};
 
 // ---------------------------------------------------------------------------
@@ -378,6 +379,33 @@ constexpr bool valid_contraction() {
   return true;
 }
 }  // namespace b200
+
+// A staged contraction: a contraction of two input operands as one level
+// member that stages the operand tiles itself (one pass per tile of the
+// contracted labels).  Built by the DAG lowering, never by user code.
+//   InA, InB      the input nodes
+//   Contraction   the contraction over slot operands naming the member's own
+//                 operand slots (output slot base+1: A's tile, base+2: B's)
+template <typename InA, typename InB, typename Contraction>
+struct NodeHandle<StagedContractionTag, InA, InB, Contraction> {
+  using node_tag = StagedContractionTag;
+  using input_a_type = InA;
+  using input_b_type = InB;
+  using contraction_type = Contraction;
+  using value_type = typename Contraction::value_type;
+  using exec_space = typename Contraction::exec_space;
+  using hook_type = typename Contraction::hook_type;
+  using modes_seq = typename Contraction::modes_seq;
+  using decl_seq = typename Contraction::decl_seq;
+  using canon_seq = typename Contraction::canon_seq;
+  static constexpr int Rank = Contraction::Rank;
+  static constexpr int NumOut = 1;
+  InA in_a;
+  InB in_b;
+  Contraction c;
+
+  KOKKOS_INLINE_FUNCTION Kokkos::Array<int, Rank> shape() const { return c.shape(); }
+};
 
 namespace Impl {
 template <typename Scalar, typename ExecSpace, int32_t... OutModes, typename NodeA, typename NodeB,

@@ -152,12 +152,58 @@ struct member_traits<Node, CombineTag> {
                 "combine node: operand tiles must match on every mode");
 };
 
+// A staged contraction (kind 3): a contraction of two INPUT operands whose
+// member stages both operand tiles itself, once per tile of the contracted
+// labels, and accumulates (reference Team.hpp Spec 4: the contracted modes may
+// be tiled).  Its three slots are the output and the two operand tiles; it
+// reads no slot of any other member.
+template <class Node>
+struct member_traits<Node, StagedContractionTag> {
+  using C = typename Node::contraction_type;
+  using CT = member_traits<C, ContractionTag>;
+  static constexpr int kind = 3;
+  static constexpr int num_out = 3;
+  static constexpr int rank = CT::rank;
+  using storage_labels = typename CT::storage_labels;
+  using decl_labels = typename CT::decl_labels;
+  using tile = typename CT::tile;
+  static constexpr auto decl_to_storage = CT::decl_to_storage;
+  static constexpr std::array<std::size_t, 0> reads{};
+  static constexpr int sa = CT::sa, sb = CT::sb, sk = CT::sk;
+  static constexpr std::size_t out_elems(std::size_t o) {
+    return o == 0 ? std::size_t(tile::num_elements)
+                  : (o == 1 ? std::size_t(C::node_a_type::storage_tile::num_elements)
+                            : std::size_t(C::node_b_type::storage_tile::num_elements));
+  }
+};
+
+// Elements of output o of a member (every output of other kinds has the
+// member's tile).
+template <class Node>
+constexpr std::size_t member_out_elems(std::size_t o) {
+  using MT = member_traits<Node>;
+  if constexpr (requires { MT::out_elems(o); })
+    return MT::out_elems(o);
+  else
+    return static_cast<std::size_t>(MT::tile::num_elements);
+}
+
 template <class Node>
 constexpr int output_arity() {
   if constexpr (requires { Node::NumOut; })
     return Node::NumOut;
   else
     return 1;
+}
+
+// Slots a member occupies in the level plan: its outputs, plus the two
+// operand tiles of a staged contraction.
+template <class Node>
+constexpr int member_slots() {
+  if constexpr (requires { typename Node::node_tag; }) {
+    if constexpr (std::is_same_v<typename Node::node_tag, StagedContractionTag>) return 3;
+  }
+  return output_arity<Node>();
 }
 
 // ---------------------------------------------------------------------------
@@ -181,7 +227,7 @@ struct Algebra {
 
   template <class Lvl, std::size_t... M>
   static constexpr std::array<std::size_t, sizeof...(M)> level_arities(std::index_sequence<M...>) {
-    return {static_cast<std::size_t>(output_arity<tuple_element_t<M, Lvl>>())...};
+    return {static_cast<std::size_t>(member_slots<tuple_element_t<M, Lvl>>())...};
   }
   template <std::size_t L>
   static constexpr auto arities_of() {
@@ -316,9 +362,8 @@ struct Pooling {
 // Bytes of one slot's tile, padded to 16.
 template <class V, class Levels, std::size_t S>
 constexpr std::size_t slot_tile_bytes() {
-  using Node = typename slot_member_node<Levels, S>::type;
-  using Tile = typename member_traits<Node>::tile;
-  const std::size_t b = static_cast<std::size_t>(Tile::num_elements) * sizeof(V);
+  using SN = slot_member_node<Levels, S>;
+  const std::size_t b = member_out_elems<typename SN::type>(SN::out) * sizeof(V);
   return (b + 15) & ~std::size_t(15);
 }
 
@@ -377,7 +422,7 @@ constexpr bool level_homogeneous() {
 template <class Lvl, std::size_t... M>
 constexpr bool level_space_agrees_impl(std::index_sequence<M...>) {
   using T0 = member_traits<tuple_element_t<0, Lvl>>;
-  if constexpr (T0::kind == 1) {
+  if constexpr (T0::kind == 1 || T0::kind == 3) {
     return ((member_traits<tuple_element_t<M, Lvl>>::sa == T0::sa &&
              member_traits<tuple_element_t<M, Lvl>>::sb == T0::sb) &&
             ...);
@@ -426,13 +471,22 @@ constexpr bool all_reads_earlier(std::index_sequence<L...>) {
 // Grid labels of a graph: the map's blocked labels that some stage member carries.
 template <class LT, class Levels>
 struct GridSpec {
+  template <class Node>
+  static constexpr bool member_carries(int32_t l) {
+    if constexpr (member_traits<Node>::kind == 0) {
+      return index_of(to_array<typename Node::modes_seq>(), l) >= 0;
+    } else if constexpr (member_traits<Node>::kind == 3) {
+      // the free labels of a staged contraction's operands (its contracted
+      // labels are looped over, not gridded)
+      using C = typename Node::contraction_type;
+      return index_of(C::freeA, l) >= 0 || index_of(C::freeB, l) >= 0;
+    } else {
+      return false;
+    }
+  }
   template <class Lvl, std::size_t... M>
   static constexpr bool level_carries(int32_t l, std::index_sequence<M...>) {
-    bool f = false;
-    ((f = f || (member_traits<tuple_element_t<M, Lvl>>::kind == 0 &&
-                index_of(to_array<typename tuple_element_t<M, Lvl>::modes_seq>(), l) >= 0)),
-     ...);
-    return f;
+    return (member_carries<tuple_element_t<M, Lvl>>(l) || ...);
   }
   template <std::size_t... L>
   static constexpr bool carried(int32_t l, std::index_sequence<L...>) {

@@ -11,7 +11,8 @@
 // weighted sums -- with functors of this test's own.  Checked:
 //   * the plan: 6 levels (stage 2-D operators | stage 4-D fields | gradients |
 //     combines | divergences | sums), 57 slots, the grid = the last node's
-//     blocked labels;
+//     blocked labels; and the self-staging form (5 levels);
+//   * values against a direct loop in BOTH forms;
 //   * values against a direct loop, with a partial last element tile;
 //   * index_consistent() and the scratch accounting on the host.
 // Built and run by tests/test_frontend_cpu.py under AddressSanitizer/UBSan.
@@ -168,6 +169,13 @@ static_assert(tuple_size_v<tuple_element_t<2, typename Low::levels_t>> == 9);
 static_assert(tuple_size_v<tuple_element_t<3, typename Low::levels_t>> == 3);
 static_assert(tuple_size_v<tuple_element_t<4, typename Low::levels_t>> == 9);
 static_assert(tuple_size_v<tuple_element_t<5, typename Low::levels_t>> == 3);
+// the form a launch takes when a contracted label spans several tiles: the
+// gradients (H x u) stage their own operands
+using LowK = typename Dag::lowering_ktiled;
+static_assert(LowK::NS == 9 && LowK::num_levels == 5);
+static_assert(b200::Algebra<typename LowK::levels_t>::num_slots == 57,
+              "30 node slots + 9 stages + 2 operand tiles per gradient");
+static_assert(b200::member_traits<tuple_element_t<0, tuple_element_t<1, typename LowK::levels_t>>>::kind == 3);
 using GS = b200::GridSpec<typename Low::label_tiles_t, typename Low::levels_t>;
 static_assert(GS::rank == 4 && GS::labels[0] == 'e', "the grid is the last node's labels");
 static_assert(Low::label_tiles_t::tile('e') == TE && !Low::label_tiles_t::is_gridded('q'));
@@ -197,20 +205,28 @@ int main(int argc, char** argv) {
               dag.scratch_bytes());
   if (outs.operand_bytes() != 0 || outs.scratch_bytes() > dag.scratch_bytes()) return 1;
 
-  constexpr std::size_t S0 = Low::level_slot(decltype(r0)::slot_index);
-  constexpr std::size_t S1 = Low::level_slot(decltype(r1)::slot_index);
-  constexpr std::size_t S2 = Low::level_slot(decltype(r2)::slot_index);
-  using GK = b200::GraphKernel<float, typename Low::label_tiles_t, typename Low::levels_t, S0, S1, S2>;
-  static_assert(GK::GR == 4);
-  b200::GridRuntime<GK::GR> grid{};
-  grid.ntiles[0] = (E + TE - 1) / TE;
-  grid.ntiles[1] = grid.ntiles[2] = grid.ntiles[3] = 1;
-  const auto levels = Low::make_levels(dag.nodes);
-  DeviceTuple<V4, V4, V4> views(f0, f1, f2);
-  for (unsigned bx = 0; bx < static_cast<unsigned>(grid.ntiles[0]); ++bx) {
-    blockIdx.x = bx;
-    GK::run(levels, grid, views);
-  }
+  if (dag.needs_contracted_tiles()) return 1;
+  auto emulate = [&]<class L>(L) {
+    constexpr std::size_t S0 = L::level_slot(decltype(r0)::slot_index);
+    constexpr std::size_t S1 = L::level_slot(decltype(r1)::slot_index);
+    constexpr std::size_t S2 = L::level_slot(decltype(r2)::slot_index);
+    using GK = b200::GraphKernel<float, typename L::label_tiles_t, typename L::levels_t, S0, S1, S2>;
+    static_assert(GK::GR == 4);
+    b200::GridRuntime<GK::GR> grid{};
+    grid.ntiles[0] = (E + TE - 1) / TE;
+    grid.ntiles[1] = grid.ntiles[2] = grid.ntiles[3] = 1;
+    const auto levels = L::make_levels(dag.nodes);
+    DeviceTuple<V4, V4, V4> views(f0, f1, f2);
+    for (unsigned bx = 0; bx < static_cast<unsigned>(grid.ntiles[0]); ++bx) {
+      blockIdx.x = bx;
+      GK::run(levels, grid, views);
+    }
+  };
+  const int form = argc > 2 ? std::atoi(argv[2]) : 0;
+  if (form == 0)
+    emulate(Low{});
+  else
+    emulate(LowK{});
 
   // direct loop
   V4* us[3] = {&u0, &u1, &u2};

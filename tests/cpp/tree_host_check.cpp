@@ -10,7 +10,9 @@
 // the combine reads them through their storage permutation.  Case 2 is a
 // contraction chain R = (A . B) . C given as a flat pre-order list of
 // Tile<A,B,C> bundles (reference Graph.hpp:316-327), with a contraction hook
-// and an input hook.  Both with a partial last tile.  Built and run by tests/test_frontend_cpu.py under ASan/UBSan.
+// and an input hook.  Case 3 contracts two labels that span several (ragged)
+// tiles, with a hook that must act once per element.  All with partial last
+// tiles.  Built and run by tests/test_frontend_cpu.py under ASan/UBSan.
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -215,6 +217,65 @@ int main(int argc, char** argv) {
           scale = std::fmax(scale, std::fabs(want));
         }
     std::printf("chain max abs error %.3e (scale %.3e)\n", worst, scale);
+    if (!(worst / scale < 1e-5)) bad = 1;
+  }
+  // ---- case 3: contracted labels spanning several tiles (ragged) -----------
+  {
+    constexpr int J = 6, K = 7, TI = 4, TL = 3, TJ = 4, TK = 3;
+    const int I = E + 2, L = 5;
+    using V3d = Kokkos::View<float***, Kokkos::LayoutRight>;
+    using V2d = Kokkos::View<float**, Kokkos::LayoutRight>;
+    V3d A("A", J, I, K), B("B", J, K, L);
+    V2d Cm("C", L, I);
+    for (int n = 0; n < J * I * K; ++n) A.data()[n] = std::sin(0.37f * n);
+    for (int n = 0; n < J * K * L; ++n) B.data()[n] = std::cos(0.23f * n + 0.5f);
+    // C[l, i] = sum_{j,k} A[j,i,k] B[j,k,l] + 1 (a hook applied once per element)
+    auto Cn = make_contraction_node<'l', 'i'>(make_input_node(make_handle<'j', 'i', 'k'>(A)),
+                                              make_input_node(make_handle<'j', 'k', 'l'>(B)),
+                                              [](int, int, float& v) { v += 1.f; });
+    using Spec = Tile<StaticTile<TJ, TI, TK>, StaticTile<TJ, TK, TL>, StaticTile<TL, TI>>;
+    auto [g1, h] = make_graph().ops(Cn);
+    (void)g1;
+    (void)h;
+    using TT = b200::tree_types<decltype(Cn), Spec>;
+    using Dag = typename TT::dag_t;
+    using Low = typename Dag::lowering_ktiled;
+    static_assert(Low::num_levels == 1 && Low::NS == 0, "one self-staging contraction");
+    const auto dag = b200::TreeLowering<float, ES>::dag_of<Spec>(Cn);
+    if (!dag.needs_contracted_tiles()) {
+      std::printf("ktiles: the contracted labels should span several tiles\n");
+      return 1;
+    }
+    if (!dag.index_consistent()) {
+      std::printf("ktiles: index_consistent false\n");
+      return 1;
+    }
+    using GK = b200::GraphKernel<float, typename Low::label_tiles_t, typename Low::levels_t,
+                                 Low::level_slot(Dag::num_slots() - 1)>;
+    // grid over (i, l): canonical storage (i, l) -- freeA ++ freeB
+    b200::GridRuntime<GK::GR> grid{};
+    static_assert(GK::GR == 2);
+    using GS = typename GK::GS;
+    const int ext[2] = {GS::labels[0] == 'i' ? I : L, GS::labels[1] == 'i' ? I : L};
+    const int til[2] = {GS::labels[0] == 'i' ? TI : TL, GS::labels[1] == 'i' ? TI : TL};
+    grid.ntiles[0] = (ext[0] + til[0] - 1) / til[0];
+    grid.ntiles[1] = (ext[1] + til[1] - 1) / til[1];
+    const auto levels = Low::make_levels(dag.nodes);
+    DeviceTuple<V2d> views(Cm);
+    for (unsigned bx = 0; bx < static_cast<unsigned>(grid.ntiles[0] * grid.ntiles[1]); ++bx) {
+      blockIdx.x = bx;
+      GK::run(levels, grid, views);
+    }
+    double worst = 0, scale = 1e-30;
+    for (int l = 0; l < L; ++l)
+      for (int i = 0; i < I; ++i) {
+        double want = 1.0;
+        for (int j = 0; j < J; ++j)
+          for (int k = 0; k < K; ++k) want += double(A(j, i, k)) * B(j, k, l);
+        worst = std::fmax(worst, std::fabs(Cm(l, i) - want));
+        scale = std::fmax(scale, std::fabs(want));
+      }
+    std::printf("ktiles max abs error %.3e (scale %.3e)\n", worst, scale);
     if (!(worst / scale < 1e-5)) bad = 1;
   }
   return bad;

@@ -114,10 +114,12 @@ def dag_host_exe(tmp_path_factory):
     return exe
 
 
+@pytest.mark.parametrize("form", [0, 1])
 @pytest.mark.parametrize("elements", [1, 5, 6])
-def test_dag_lowering_host_emulation_under_sanitizers(dag_host_exe, elements):
-    run = subprocess.run([str(dag_host_exe), str(elements)], capture_output=True, text=True,
-                         timeout=120)
+def test_dag_lowering_host_emulation_under_sanitizers(dag_host_exe, elements, form):
+    """form 0: operands staged by stage levels; 1: self-staging contractions."""
+    run = subprocess.run([str(dag_host_exe), str(elements), str(form)], capture_output=True,
+                         text=True, timeout=120)
     assert run.returncode == 0, run.stdout + run.stderr
     assert "max abs error" in run.stdout and "pools" in run.stdout
 
@@ -137,6 +139,7 @@ def test_tree_lowering_host_emulation_under_sanitizers(tree_host_exe, elements):
                          timeout=120)
     assert run.returncode == 0, run.stdout + run.stderr
     assert "tree max abs error" in run.stdout and "chain max abs error" in run.stdout
+    assert "ktiles max abs error" in run.stdout
 
 
 def test_kokkos_subset_on_the_host(tmp_path):
