@@ -25,6 +25,12 @@ are what the tests use on the GPU box, which has no reference tree.
                           the contraction benchmarks (tree route, nested and
                           flat tile bundles, hooks, LayoutLeft views), the
                           same way.
+  test_<name>             the reference's unit tests that use only the public
+                          API (tests/test_dag_graph.cpp, test_device_tuple.cpp,
+                          test_contraction_node.cpp, test_concept.cpp),
+                          unmodified, compiled for sm_100a against the frontend
+                          and tests/cpp/gtest_shim (a stand-in for the GoogleTest
+                          calls they make; GoogleTest is not installed).
   libref_sem2d.so         that 2D source compiled host-only through
                           oracle/ref_pin2d.cpp: its fill_field(),
                           fill_operators() and host_reference() behind a C
@@ -49,6 +55,11 @@ SEM3D_DAG = REF / "benchmarks" / "sem_stiffness_3d" / "bench_sem_stiffness_3d.cp
 SEM2D = REF / "benchmarks" / "sem_stiffness" / "bench_sem_stiffness.cpp"
 CONTRACTION_BENCHES = ("permuted_contraction", "multilevel_contraction", "permuted_combine",
                        "team_contraction")
+# reference unit tests that compile against the public API alone, with
+# whether the file defines its own main()
+UNIT_TESTS = {"test_dag_graph": True, "test_device_tuple": True, "test_contraction_node": True,
+              "test_concept": False}
+GTEST_SHIM = ROOT / "tests" / "cpp" / "gtest_shim"
 INC = [f"-I{ROOT / 'include'}", f"-I{ROOT / 'tensoroperations_b200' / 'include'}"]
 LIBDIR = ROOT / "tensoroperations_b200"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
@@ -99,13 +110,20 @@ def build(force: bool = False):
     for src, out in progs:
         if src.exists() and (force or _stale(out, deps + [src, LIBDIR / "libtensoroperations_b200.so"])):
             _nvcc_program(src, out)
+    shim = [GTEST_SHIM / "gtest" / "gtest.h", GTEST_SHIM / "gtest_main.cpp"]
+    for name, has_main in UNIT_TESTS.items():
+        src = REF / "tests" / f"{name}.cpp"
+        out = OUT / name
+        if src.exists() and (force or _stale(out, deps + shim + [src, LIBDIR / "libtensoroperations_b200.so"])):
+            extra = [] if has_main else [str(GTEST_SHIM / "gtest_main.cpp")]
+            _nvcc_program(src, out, [f"-I{GTEST_SHIM}"], extra)
     return PIN, DROPIN, DROPIN_DAG, DROPIN_2D, PIN2D
 
 
-def _nvcc_program(src: Path, out: Path):
+def _nvcc_program(src: Path, out: Path, inc=(), extra_sources=()):
     _run([NVCC, "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++20",
           "--extended-lambda", "--expt-relaxed-constexpr", "-diag-suppress", "186,20012",
-          *INC, "-x", "cu", str(src), f"-L{LIBDIR}", "-ltensoroperations_b200",
+          *INC, *inc, "-x", "cu", str(src), *extra_sources, f"-L{LIBDIR}", "-ltensoroperations_b200",
           "-Xlinker", "-rpath,$ORIGIN/../../tensoroperations_b200", "-o", str(out)])
 
 

@@ -71,8 +71,14 @@ struct DagGraph {
 
   // Un-pooled bounds, as the reference reports them: one storage tile per
   // node output, and one tile per staged input operand.
-  std::size_t slot_bytes() const { return slot_bytes_impl(std::make_index_sequence<N>{}); }
-  std::size_t operand_bytes() const {
+  std::size_t slot_bytes() const { return unpooled_slot_bytes(); }
+  std::size_t operand_bytes() const { return unpooled_operand_bytes(); }
+  std::size_t scratch_bytes() const { return slot_bytes() + operand_bytes(); }
+
+  static constexpr std::size_t unpooled_slot_bytes() {
+    return slot_bytes_impl(std::make_index_sequence<N>{});
+  }
+  static constexpr std::size_t unpooled_operand_bytes() {
     using Low = lowering;
     std::size_t b = 0;
     for (std::size_t s = 0; s < Low::NS; ++s) {
@@ -82,7 +88,6 @@ struct DagGraph {
     }
     return b;
   }
-  std::size_t scratch_bytes() const { return slot_bytes() + operand_bytes(); }
   // Staged operands live in the pooled store: there is no separate arena.
   std::size_t arena_bytes() const { return 0; }
   std::size_t arena_elems() const { return 0; }
@@ -198,7 +203,7 @@ struct DagGraph {
   }
 
   template <std::size_t... K>
-  std::size_t slot_bytes_impl(std::index_sequence<K...>) const {
+  static constexpr std::size_t slot_bytes_impl(std::index_sequence<K...>) {
     return (std::size_t{0} + ... +
             [&] {
               using Node = tuple_element_t<K, NodesT>;

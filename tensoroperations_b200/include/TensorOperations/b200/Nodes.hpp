@@ -102,6 +102,16 @@ struct DeviceTuple {
   }
 };
 
+// Free get<I>(tuple), as the reference's DeviceTuple offers.
+template <std::size_t I, class... T>
+KOKKOS_INLINE_FUNCTION constexpr const auto& get(const DeviceTuple<T...>& t) {
+  return t.template get<I>();
+}
+template <std::size_t I, class... T>
+KOKKOS_INLINE_FUNCTION constexpr auto& get(DeviceTuple<T...>& t) {
+  return t.template get<I>();
+}
+
 template <class Tup>
 struct tuple_size;
 template <class... T>
@@ -151,6 +161,10 @@ struct TensorHandle {
   using tensor_type = T;
   T tensor;
   KOKKOS_INLINE_FUNCTION std::size_t extent(int d) const { return tensor.extent(d); }
+  template <class... I>
+  KOKKOS_INLINE_FUNCTION decltype(auto) operator()(I... idx) const {
+    return tensor(idx...);
+  }
 };
 
 template <int32_t... Modes, TensorLike T>
@@ -201,7 +215,12 @@ template <typename Op, typename V, typename... Is>
 struct hook_invocable<Op, V, std::tuple<Is...>> : std::is_invocable<const Op&, Is..., V&> {};
 template <typename Op, int Rank, typename V>
 constexpr bool hook_like() {
-  return hook_invocable<Op, V, typename ints_tuple<Rank>::type>::value;
+  if constexpr (std::is_same_v<Op, NoHook>)
+    return true;
+  else if constexpr (std::is_void_v<V>)
+    return false;
+  else
+    return hook_invocable<Op, V, typename ints_tuple<Rank>::type>::value;
 }
 }  // namespace b200
 
@@ -226,9 +245,8 @@ struct NodeHandle<InputTag, T, ModesSeq, HookOp> {
 
 template <typename T, typename ModesSeq, typename HookOp = NoHook>
 auto make_input_node(TensorHandle<T, ModesSeq> h, HookOp hook = {}) {
-  static_assert(std::is_same_v<HookOp, NoHook> ||
-                    b200::hook_like<HookOp, static_cast<int>(ModesSeq::size()),
-                                    typename b200::value_of<T>::type>(),
+  static_assert(b200::hook_like<HookOp, static_cast<int>(ModesSeq::size()),
+                                typename b200::value_of<T>::type>(),
                 "input hook must be callable as op(i_0, ..., i_{Rank-1}, value_type&)");
   return NodeHandle<InputTag, T, ModesSeq, HookOp>{h, hook};
 }
@@ -419,7 +437,7 @@ auto make_contraction_node_impl(NodeA a, NodeB b, HookOp hook) {
                 "must be pairwise distinct, and the output rank must equal the number "
                 "of free modes");
   using Node = NodeHandle<ContractionTag, NodeA, NodeB, OutSeq, Scalar, ExecSpace, HookOp>;
-  static_assert(std::is_same_v<HookOp, NoHook> || b200::hook_like<HookOp, Node::Rank, Scalar>(),
+  static_assert(b200::hook_like<HookOp, Node::Rank, Scalar>(),
                 "contraction hook must be callable as op(i_0, ..., i_{Rank-1}, value_type&)");
   constexpr auto al = b200::to_array<AL>();
   constexpr auto bl = b200::to_array<BL>();

@@ -294,21 +294,28 @@ struct Graph {
 
 inline Graph<> make_graph() { return {}; }
 
-// Evaluator<TeamPolicyTag<ES>, Node, Spec>: the scratch one team of the tree
-// route requests for `Node` under bundle `Spec` (reference Evaluator.hpp:452,
-// scratch_size_per_team).  Everything is a compile-time constant of the plan.
+// Evaluator<TeamPolicyTag<ES>, Node, Spec>::scratch_size_per_team: the scratch
+// of `Node` under bundle `Spec` as the reference sizes a tree (reference
+// Evaluator.hpp:452): every node's output tile plus every staged operand tile,
+// nothing shared -- the same un-pooled sum DagGraph::scratch_bytes() gives the
+// tree's DAG spelling.  The launch itself requests the liveness-pooled store,
+// which is never larger (pooled_scratch_size_per_team).
 template <typename Policy, typename Node, typename Spec>
 struct Evaluator;
 template <typename ES, typename Node, typename Spec>
 struct Evaluator<TeamPolicyTag<ES>, Node, Spec> {
+  using dag_t = typename b200::tree_types<Node, Spec>::dag_t;
   using outputs_t = typename b200::tree_types<Node, Spec>::outputs_t;
   static std::size_t scratch_size_per_team(const Spec&) {
-    return scratch_of(static_cast<outputs_t*>(nullptr));
+    return dag_t::unpooled_slot_bytes() + dag_t::unpooled_operand_bytes();
+  }
+  static std::size_t pooled_scratch_size_per_team(const Spec&) {
+    return pooled_of(static_cast<outputs_t*>(nullptr));
   }
 
  private:
   template <typename Dag, std::size_t... R>
-  static std::size_t scratch_of(DagOutputs<Dag, R...>*) {
+  static std::size_t pooled_of(DagOutputs<Dag, R...>*) {
     using Low = typename Dag::lowering;
     return b200::Layout<typename Dag::value_type, typename Low::levels_t,
                         Low::level_slot(R)...>::scratch_bytes;

@@ -18,8 +18,12 @@ if str(ROOT) not in sys.path:
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200)")
-    from tensoroperations_b200 import _build
-    _build.build_library()
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("tensoroperations_b200_build",
+                                                  ROOT / "tensoroperations_b200" / "_build.py")
+    build_mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(build_mod)
+    build_mod.build_library()  # loaded by path: importing the package needs the library
     from oracle import build as oracle_build
     oracle_build.build()
     from oracle import build_ref

@@ -1,0 +1,39 @@
+"""The reference's own unit tests that use only the public API, unmodified, on B200 (GPU).
+
+oracle/_ref/test_<name> are the reference's tests/test_<name>.cpp compiled for
+sm_100a against this repository's frontend and Kokkos subset, with
+tests/cpp/gtest_shim standing in for the GoogleTest calls they make
+(oracle/build_ref.py):
+  test_dag_graph         a tree re-expressed as a DAG gives bit-identical
+                         results and the same un-pooled scratch; a diamond DAG
+                         (one node, two consumers) gives the tree's numbers at
+                         less scratch; multi-tiled grid labels gathered by label;
+  test_contraction_node  node construction, shapes, stored hooks;
+  test_device_tuple      DeviceTuple on host and in a kernel;
+  test_concept           TensorLike and the handle's element access.
+Each prints one line per test and exits non-zero if any failed.
+"""
+import os
+import subprocess
+from pathlib import Path
+
+import pytest
+
+REF = Path(__file__).resolve().parent.parent / "oracle" / "_ref"
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("name", ["test_dag_graph", "test_contraction_node", "test_device_tuple",
+                                  "test_concept"])
+def test_reference_unit_test_passes(name):
+    exe = REF / name
+    if not exe.exists():
+        pytest.skip("oracle/_ref not built")
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=600)
+    out_dir = Path(os.environ.get("GRAFT_REPO_ROOT", ".")) / "gpurun_out"
+    if out_dir.is_dir():
+        (out_dir / f"ref_unit_{name}.txt").write_text(r.stdout + r.stderr)
+    assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-2000:]
+    assert "[  FAILED  ]" not in r.stdout
+    assert "[       OK ]" in r.stdout
