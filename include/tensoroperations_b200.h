@@ -351,6 +351,22 @@ int to_chain_f32(int32_t E, const float* A, const float* B, const float* C, floa
 /* Useful flops of one chain: 2 E^6 + 2 E^4. */
 double to_chain_flops(int32_t E);
 
+/* One contraction as a dense GEMM on the tensor cores:
+ *   C[m][n] = sum_k A[m][k] * B[n][k]
+ * with both operands K-major and given split into TF32 parts, A = Ahi + Alo
+ * and B = Bhi + Blo elementwise (hi = the value rounded to TF32, lo = the
+ * exact remainder); the product is formed from three TF32 products (the lo*lo
+ * term, about 2^-22 relative, is dropped) accumulated in fp32.  This is the
+ * path the frontend lowers a large contraction of two inputs to (the
+ * reference's team contraction evaluator, include/TensorOperations/Evaluator/
+ * Team.hpp:318-927, with its permuted operands, Permute.hpp:127-228, packed
+ * by the frontend).  Mp, Np, Kp must be positive multiples of 128, 256 and
+ * 32 (pad with zeros); A* are [Mp][Kp], B* [Np][Kp], C [Mp][Np], row-major
+ * fp32 in device memory, 16-byte aligned.  C is overwritten.  Asynchronous on
+ * `stream`; allocates nothing. */
+int to_gemm_tf32x3(int64_t Mp, int64_t Np, int64_t Kp, const float* Ahi, const float* Alo,
+                   const float* Bhi, const float* Blo, float* C, void* stream);
+
 /* ---------------------------------------------------------------------- */
 /* Level-graph lowering                                                    */
 /* ---------------------------------------------------------------------- */

@@ -124,6 +124,7 @@ _sig("to_batched_small_gemm", C.c_int, [C.c_int32, C.c_int32, C.c_int32, C.c_int
                                         C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p])
 _sig("to_chain_workspace_bytes", C.c_size_t, [C.c_int32])
 _sig("to_chain_f32", C.c_int, [C.c_int32] + [C.c_void_p] * 6 + [C.c_size_t, C.c_void_p])
+_sig("to_gemm_tf32x3", C.c_int, [C.c_int64] * 3 + [C.c_void_p] * 6)
 _sig("to_chain_flops", C.c_double, [C.c_int32])
 _sig("to_synth_fill_device", C.c_int, [C.c_void_p, C.c_int32, C.c_int64, C.c_int64, C.c_uint64,
                                        C.c_int32, C.c_double, C.c_double, C.c_double, C.c_void_p])
@@ -284,6 +285,12 @@ def chain_f32(E: int, A, B, Cm, R, workspace, T=None, stream: int = 0):
     nbytes = workspace.numel() * workspace.element_size()
     check(lib.to_chain_f32(E, _ptr(A), _ptr(B), _ptr(Cm), _ptr(R), _ptr(T), _ptr(workspace), nbytes,
                            stream), "to_chain_f32")
+
+
+def gemm_tf32x3(Mp: int, Np: int, Kp: int, Ahi, Alo, Bhi, Blo, Cout, stream: int = 0):
+    """Cout[m][n] = sum_k (Ahi+Alo)[m][k] (Bhi+Blo)[n][k] on the tensor cores (K-major operands)."""
+    check(lib.to_gemm_tf32x3(Mp, Np, Kp, _ptr(Ahi), _ptr(Alo), _ptr(Bhi), _ptr(Blo), _ptr(Cout),
+                             stream), "to_gemm_tf32x3")
 
 
 def sm_count() -> int:

@@ -335,6 +335,174 @@ __global__ void __launch_bounds__(kThreads, 1)
                  "r"(uint32_t(2 * kTileN)) : "memory");
 }
 
+// ---- the general contraction as one GEMM: C[m][n] = sum_k A[m][k] B[n][k] ----
+// The same producer / MMA issuer / epilogue roles as the chain kernel, on
+// operands already grouped K-major and split into TF32 hi/lo (the caller -- the
+// frontend's contraction lowering -- packs them): A [Mp][Kp], B [Np][Kp], C
+// [Mp][Np] row-major, Mp a multiple of 128, Np of 256, Kp of 32.  K runs in
+// chunks of kChunkIters steps alternating between the two TMEM accumulators,
+// the last chunk possibly shorter; each finished chunk is added in IEEE fp32.
+struct GemmArgs {
+  float* C;
+  long long ldc;
+  int k_iters;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap mAhi, const __grid_constant__ CUtensorMap mAlo,
+                        const __grid_constant__ CUtensorMap mBhi, const __grid_constant__ CUtensorMap mBlo,
+                        const GemmArgs args) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* tiles = base;
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + kStages * kStageBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* acc_full = empty + kStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int k_iters = args.k_iters;
+  const int nchunks = (k_iters + kChunkIters - 1) / kChunkIters;
+  const int m_tile = blockIdx.y, n_tile = blockIdx.x;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int j = 0; j < 2; ++j) {
+      mbar_init(&acc_full[j], 1);
+      mbar_init(&acc_empty[j], kEpilogueWarps);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 ::"r"(smem_u32(tmem_slot)), "r"(uint32_t(2 * kTileN)) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---- producer ----
+    int issued = 0;
+    bool ok = true;
+    for (int it = 0; it < k_iters && ok; ++it) {
+      const int s = it % kStages, n = it / kStages;
+      if (n > 0 && !wait_bounded(&empty[s], (n - 1) & 1)) {
+        ok = false;
+        break;
+      }
+      if (*reinterpret_cast<volatile int*>(abort_flag)) break;
+      unsigned char* st = tiles + s * kStageBytes;
+      mbar_arrive_expect_tx(&full[s], kStageBytes);
+      tma_load_2d(st, &mAhi, it * kTileK, m_tile * kTileM, &full[s]);
+      tma_load_2d(st + kABytes, &mAlo, it * kTileK, m_tile * kTileM, &full[s]);
+      tma_load_2d(st + 2 * kABytes, &mBhi, it * kTileK, n_tile * kTileN, &full[s]);
+      tma_load_2d(st + 2 * kABytes + kBBytes, &mBlo, it * kTileK, n_tile * kTileN, &full[s]);
+      issued = it + 1;
+    }
+    if (!ok) {
+      atomicExch(&g_chain_status, int(TO_ERR_TIMEOUT));
+      atomicExch(abort_flag, 1);
+    }
+    for (int it = (issued > kStages ? issued - kStages : 0); it < issued; ++it)
+      wait_bounded(&full[it % kStages], (it / kStages) & 1);
+  } else if (warp == 1 && lane == 0) {
+    // ---- MMA issuer ----
+    bool ok = true;
+    for (int ch = 0; ch < nchunks && ok; ++ch) {
+      const int j = ch & 1;
+      if (ch >= 2 && !wait_bounded(&acc_empty[j], ((ch >> 1) - 1) & 1)) {
+        ok = false;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t dacc = tmem + uint32_t(j * kTileN);
+      const int iters = (k_iters - ch * kChunkIters) < kChunkIters ? (k_iters - ch * kChunkIters)
+                                                                    : kChunkIters;
+      for (int ci = 0; ci < iters; ++ci) {
+        const int it = ch * kChunkIters + ci;
+        const int s = it % kStages, n = it / kStages;
+        if (!wait_bounded(&full[s], n & 1) || *reinterpret_cast<volatile int*>(abort_flag)) {
+          ok = false;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t st = smem_u32(tiles + s * kStageBytes);
+        const uint32_t sAhi = st, sAlo = st + kABytes, sBhi = st + 2 * kABytes,
+                       sBlo = st + 2 * kABytes + kBBytes;
+#pragma unroll
+        for (int k = 0; k < kTileK / 8; ++k) {
+          const uint64_t dAhi = umma_desc(sAhi + 32 * k, 16, 1024);
+          const uint64_t dAlo = umma_desc(sAlo + 32 * k, 16, 1024);
+          const uint64_t dBhi = umma_desc(sBhi + 32 * k, 16, 1024);
+          const uint64_t dBlo = umma_desc(sBlo + 32 * k, 16, 1024);
+          umma_tf32(dacc, dAlo, dBhi, (ci > 0 || k > 0) ? 1u : 0u);
+          umma_tf32(dacc, dAhi, dBlo, 1u);
+          umma_tf32(dacc, dAhi, dBhi, 1u);
+        }
+        umma_commit(&empty[s]);
+      }
+      umma_commit(&acc_full[j]);
+    }
+    if (!ok) {
+      atomicExch(&g_chain_status, int(TO_ERR_TIMEOUT));
+      atomicExch(abort_flag, 1);
+    }
+  } else if (warp >= 2) {
+    // ---- epilogue: thread = tile row x 128 of the 256 columns ----
+    const int ew = warp - 2;
+    const int q = warp & 3;
+    const int h = ew >> 2;
+    const int row = q * 32 + lane;
+    float acc[kTileN / 2];
+#pragma unroll
+    for (int x = 0; x < kTileN / 2; ++x) acc[x] = 0.f;
+    bool live = true;
+    for (int ch = 0; ch < nchunks; ++ch) {
+      const int j = ch & 1;
+      const bool ok = live && wait_bounded(&acc_full[j], (ch >> 1) & 1);
+      if (!ok || *reinterpret_cast<volatile int*>(abort_flag)) {
+        if (live) atomicExch(&g_chain_status, int(TO_ERR_TIMEOUT));
+        live = false;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+      for (int part = 0; part < 4; ++part) {
+        uint32_t r[32];
+        TO_TMEM_LD_X32(tmem + (uint32_t(q * 32) << 16) + uint32_t(j * kTileN + h * 128 + part * 32), r);
+#pragma unroll
+        for (int x = 0; x < 32; ++x) acc[part * 32 + x] += __uint_as_float(r[x]);
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive_one(&acc_empty[j]);
+    }
+    if (live) {
+      float4* out = reinterpret_cast<float4*>(args.C + (size_t(m_tile) * kTileM + row) * args.ldc +
+                                              size_t(n_tile) * kTileN + h * 128);
+#pragma unroll
+      for (int x = 0; x < 32; ++x)
+        out[x] = make_float4(acc[4 * x], acc[4 * x + 1], acc[4 * x + 2], acc[4 * x + 3]);
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(uint32_t(2 * kTileN)) : "memory");
+}
+
 // hi = x rounded to TF32 (low 13 mantissa bits zero), lo = x - hi (exact).
 __global__ void tf32_split_kernel(const float* __restrict__ x, float* __restrict__ hi,
                                   float* __restrict__ lo, long long n) {
@@ -511,6 +679,48 @@ int to_chain_f32(int32_t E, const float* A, const float* B, const float* C, floa
 double to_chain_flops(int32_t E) {
   const double e = E;
   return 2.0 * e * e * e * e * e * e + 2.0 * e * e * e * e;
+}
+
+int to_gemm_tf32x3(int64_t Mp, int64_t Np, int64_t Kp, const float* Ahi, const float* Alo,
+                   const float* Bhi, const float* Blo, float* C, void* stream) {
+  if (Mp <= 0 || Np <= 0 || Kp <= 0 || Mp % kTileM || Np % kTileN || Kp % kTileK)
+    return set_error(TO_ERR_INVALID_ARGUMENT,
+                     "to_gemm_tf32x3: sizes %lld x %lld x %lld must be positive multiples of "
+                     "128 x 256 x 32", (long long)Mp, (long long)Np, (long long)Kp);
+  if (Mp / kTileM > 65535 || Kp / kTileK > (1ll << 30))
+    return set_error(TO_ERR_INVALID_ARGUMENT, "to_gemm_tf32x3: M or K too large");
+  const void* ptrs[] = {Ahi, Alo, Bhi, Blo, C};
+  for (const void* p : ptrs) {
+    if (!p) return set_error(TO_ERR_INVALID_ARGUMENT, "to_gemm_tf32x3: null pointer");
+    if (!aligned(p, 16)) return set_error(TO_ERR_ALIGNMENT, "to_gemm_tf32x3: operands must be 16-byte aligned");
+  }
+  int st = TO_OK;
+  EncodeTiled enc = encode_fn(&st);
+  if (!enc) return st;
+  const cuuint64_t fb = 4;
+  const cuuint64_t adims[2] = {cuuint64_t(Kp), cuuint64_t(Mp)};
+  const cuuint64_t astr[1] = {cuuint64_t(Kp) * fb};
+  const cuuint32_t abox[2] = {cuuint32_t(kTileK), cuuint32_t(kTileM)};
+  const cuuint64_t bdims[2] = {cuuint64_t(Kp), cuuint64_t(Np)};
+  const cuuint32_t bbox[2] = {cuuint32_t(kTileK), cuuint32_t(kTileN)};
+  CUtensorMap mAhi, mAlo, mBhi, mBlo;
+  if ((st = make_map(enc, &mAhi, Ahi, 2, adims, astr, abox))) return st;
+  if ((st = make_map(enc, &mAlo, Alo, 2, adims, astr, abox))) return st;
+  if ((st = make_map(enc, &mBhi, Bhi, 2, bdims, astr, bbox))) return st;
+  if ((st = make_map(enc, &mBlo, Blo, 2, bdims, astr, bbox))) return st;
+  static std::once_flag once;
+  static cudaError_t attr = cudaSuccess;
+  std::call_once(once, [] {
+    attr = cudaFuncSetAttribute(gemm_tcgen05_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(kSmemBytes));
+  });
+  TO_CUDA_TRY(attr);
+  GemmArgs args{C, (long long)Np, int(Kp / kTileK)};
+  const dim3 grid(unsigned(Np / kTileN), unsigned(Mp / kTileM));
+  gemm_tcgen05_kernel<<<grid, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(
+      mAhi, mAlo, mBhi, mBlo, args);
+  TO_CUDA_TRY(cudaGetLastError());
+  return ok();
 }
 
 }  // extern "C"

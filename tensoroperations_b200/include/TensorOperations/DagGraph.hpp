@@ -25,6 +25,7 @@
 #include <TensorOperations/LevelGraph.hpp>
 #include <TensorOperations/Tiling.hpp>
 #include <TensorOperations/b200/Dag.hpp>
+#include <TensorOperations/b200/TcContract.hpp>
 
 namespace TensorOperations {
 
@@ -142,6 +143,11 @@ struct DagGraph {
           "DagGraph: a node's mode is either tiled differently from the grid node's or is "
           "multi-tiled and absent from it, so its tile index cannot be gathered from the grid "
           "node's. Retile so every shared mode matches and every unshared mode has one tile.");
+    if constexpr (b200::tc_candidate<NodesT, ValueType>() && sizeof...(ViewTs) == 1) {
+      // one large fp32 contraction of two inputs: a GEMM on the tensor cores
+      const int league = b200::tc_try_contract(nodes.template get<0>(), views...);
+      if (league >= 0) return league;
+    }
     if (needs_contracted_tiles()) {
       using Low = lowering_ktiled;
       const typename Low::graph_t g{Low::make_levels(nodes)};

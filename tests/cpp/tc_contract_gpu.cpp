@@ -1,0 +1,100 @@
+// tc_contract_gpu.cpp -- TEST ONLY (GPU): a large fp32 contraction of two
+// inputs through the public API, which the frontend runs as a tensor-core GEMM
+// (b200/TcContract.hpp: pack -> to_gemm_tf32x3 -> unpack), against a float64
+// host loop.  Permuted operands and output, contracted labels spanning several
+// bundle tiles, an input hook and a contraction hook, ragged sizes:
+//   C[l, i] = h( sum_{j,k} A[j, i, k] * g(B[k, j, l]) )
+// through the tree route (make_graph().ops) and the DAG route (make_dag), plus
+// a small case (M < 128) that stays on the level evaluator.  Prints one line
+// per case with the relative error and the league execute() returned (the
+// GEMM's tile count on the tensor-core path; the grid on the level path).
+// Run by tests/test_frontend_gpu.py, with and without
+// TO_FRONTEND_TENSOR_CORES=0.
+#include <Kokkos_Core.hpp>
+#include <TensorOperations/DagGraph.hpp>
+#include <TensorOperations/Graph.hpp>
+#include <TensorOperations/Tiling.hpp>
+
+#include <cmath>
+#include <cstdio>
+
+using namespace TensorOperations;
+using ES = Kokkos::DefaultExecutionSpace;
+using V3 = Kokkos::View<float***, Kokkos::LayoutRight>;
+using V2 = Kokkos::View<float**, Kokkos::LayoutRight>;
+
+struct InHook {
+  KOKKOS_FUNCTION void operator()(int k, int, int l, float& v) const { v *= 1.f + 0.01f * ((k + l) % 5); }
+};
+struct OutHook {
+  KOKKOS_FUNCTION void operator()(int l, int i, float& v) const { v += 0.001f * l - 0.002f * i; }
+};
+
+using Bundle = Tile<StaticTile<4, 32, 4>, StaticTile<4, 4, 32>, StaticTile<32, 32>>;
+
+static double run_case(int I, int L, int J, int K, int route, int* league_out) {
+  V3 A("A", J, I, K), B("B", K, J, L);
+  V2 C("C", L, I);
+  auto hA = Kokkos::create_mirror_view(A);
+  auto hB = Kokkos::create_mirror_view(B);
+  for (int j = 0; j < J; ++j)
+    for (int i = 0; i < I; ++i)
+      for (int k = 0; k < K; ++k) hA(j, i, k) = std::sin(0.013f * i + 0.7f * j - 0.3f * k);
+  for (int k = 0; k < K; ++k)
+    for (int j = 0; j < J; ++j)
+      for (int l = 0; l < L; ++l) hB(k, j, l) = std::cos(0.021f * l - 0.4f * j + 0.9f * k);
+  Kokkos::deep_copy(A, hA);
+  Kokkos::deep_copy(B, hB);
+  auto node = make_contraction_node<'l', 'i'>(make_input_node(make_handle<'j', 'i', 'k'>(A)),
+                                              make_input_node(make_handle<'k', 'j', 'l'>(B), InHook{}),
+                                              OutHook{});
+  int league = 0;
+  if (route == 0) {
+    auto [g1, h] = make_graph().ops(node);
+    (void)h;
+    league = g1.execute(TeamPolicyTag<ES>{}, Bundle{}, C);
+  } else {
+    auto [g, h] = make_dag<float, ES>().add(node, Bundle{});
+    league = g.outputs(h).execute(TeamPolicyTag<ES>{}, C);
+  }
+  Kokkos::fence();
+  *league_out = league;
+  auto hC = Kokkos::create_mirror_view_and_copy(Kokkos::HostSpace{}, C);
+  double num = 0, den = 0;
+  for (int l = 0; l < L; ++l)
+    for (int i = 0; i < I; ++i) {
+      double s = 0;
+      for (int j = 0; j < J; ++j)
+        for (int k = 0; k < K; ++k) {
+          float b = hB(k, j, l);
+          InHook{}(k, j, l, b);
+          s += double(hA(j, i, k)) * double(b);
+        }
+      const double want = s + (0.001 * l - 0.002 * i);  // OutHook in float64
+      num += (hC(l, i) - want) * (hC(l, i) - want);
+      den += want * want;
+    }
+  return std::sqrt(num / den);
+}
+
+int main(int argc, char* argv[]) {
+  Kokkos::initialize(argc, argv);
+  int rc = 0;
+  {
+    struct Case {
+      const char* name;
+      int I, L, J, K, route;
+    } cases[] = {{"tree_large", 300, 260, 7, 9, 0},
+                 {"dag_large", 300, 260, 7, 9, 1},
+                 {"tree_square", 512, 512, 16, 16, 0},
+                 {"dag_small", 100, 90, 5, 6, 1}};
+    for (const Case& c : cases) {
+      int league = 0;
+      const double err = run_case(c.I, c.L, c.J, c.K, c.route, &league);
+      std::printf("case %s err %.3e league %d\n", c.name, err, league);
+      if (!(err <= 1e-5)) rc = 1;
+    }
+  }
+  Kokkos::finalize();
+  return rc;
+}

@@ -7,7 +7,14 @@ conftest when stale) and only run on the GPU box:
 * level_graph_runtime_gpu: graphs of every member kind (stage, contraction
   with permuted/relabelled operands, combine with coordinates, several roots,
   ragged last tile) executed at two team sizes against host loops.
+* tc_contract_gpu: one large fp32 contraction of two inputs (permuted
+  operands and output, hooks, ragged sizes) through the tree and DAG routes,
+  which the frontend runs as a tensor-core GEMM -- and, with
+  TO_FRONTEND_TENSOR_CORES=0, on the level evaluator -- against float64 host
+  loops (relative L2 <= 1e-5); the league execute() returns shows which path
+  ran (the GEMM's 128 x 256 tile count on the tensor cores).
 """
+import os
 import subprocess
 from pathlib import Path
 
@@ -24,3 +31,25 @@ def test_program(program):
     r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
     print(r.stdout[-4000:])
     assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-2000:]
+
+
+# league per case: the GEMM tile count (tensor cores) / the level grid
+TC_LEAGUES = {"tree_large": 6, "dag_large": 6, "tree_square": 8}
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("tensor_cores", [True, False])
+def test_tensor_core_contraction(tensor_cores):
+    exe = BIN / "tc_contract_gpu"
+    assert exe.exists(), f"{exe} not built (tests/cpp/build.py)"
+    env = dict(os.environ)
+    if not tensor_cores:
+        env["TO_FRONTEND_TENSOR_CORES"] = "0"
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300, env=env)
+    print(r.stdout[-4000:])
+    assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-2000:]
+    leagues = {ln.split()[1]: int(ln.split()[-1]) for ln in r.stdout.splitlines()
+               if ln.startswith("case ")}
+    assert set(leagues) == {"tree_large", "dag_large", "tree_square", "dag_small"}
+    for name, tiles in TC_LEAGUES.items():
+        assert (leagues[name] == tiles) == tensor_cores, (name, leagues[name])
