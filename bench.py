@@ -255,6 +255,78 @@ def run_reference(args):
     return 0
 
 
+def run_gemm(args):
+    """The general contraction's tensor-core GEMM (to_gemm_tf32x3), printed with
+    --workload gemm.  A step = one call, C = A B^T with K-major fp32 operands
+    already split into TF32 hi/lo (the frontend's pack step is not timed here);
+    M = N = K = --gemm-size.  Useful flops 2 M N K; the tensor cores run three
+    TF32 products."""
+    import torch
+    from tensoroperations_b200 import abi
+    n = args.gemm_size
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(5)
+    A = torch.randn((n, n), generator=g, device=dev)
+    B = torch.randn((n, n), generator=g, device=dev)
+
+    def split(x):
+        b = x.view(torch.int32)
+        hb = (b + 0x1000) & ~0x1FFF
+        hi = hb.view(torch.float32)
+        return hi.contiguous(), (x - hi).contiguous()
+    Ahi, Alo = split(A)
+    Bhi, Blo = split(B)
+    C = torch.empty((n, n), device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    s = stream.cuda_stream
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            abi.gemm_tf32x3(n, n, n, Ahi, Alo, Bhi, Blo, C, stream=s)
+    torch.cuda.synchronize()
+    steps = args.steps
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    with ClockSampler(gpu_id_for(dev)) as clocks:
+        ev[0].record(stream)
+        for _ in range(steps):
+            abi.gemm_tf32x3(n, n, n, Ahi, Alo, Bhi, Blo, C, stream=s)
+        ev[1].record(stream)
+        torch.cuda.synchronize()
+    ms = ev[0].elapsed_time(ev[1]) / steps
+    abi.check(abi.lib.to_device_status(1), "device status")
+    useful = 2.0 * n ** 3
+    torch.backends.cuda.matmul.allow_tf32 = False
+    ref = A.double() @ B.double().T
+    rel = float((C.double() - ref).norm() / ref.norm())
+    for _ in range(2):
+        A @ B.T
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(5):
+        A @ B.T
+    e1.record()
+    torch.cuda.synchronize()
+    torch_ms = e0.elapsed_time(e1) / 5
+    mp_path = ROOT / "MEASURED_PEAKS.json"
+    mp = json.loads(mp_path.read_text()) if mp_path.exists() else {}
+    peak = float(mp.get("bf16_tflops", 1590.0)) / 2
+    achieved = 3 * useful / (ms * 1e-3) / 1e12
+    line = {"metric": "general contraction GEMM on tcgen05 (fp32 via 3xTF32), useful TFLOP/s",
+            "value": useful / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "n_gpus": 1, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32 (3xTF32 on tcgen05)",
+            "data": "synthetic N(0,1), seeded",
+            "config": {"workload": f"C = A B^T, M = N = K = {n}, K-major split operands",
+                       "l2": f"operands 4 x {4 * n * n / 2**20:.0f} MB"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": None,
+                         "peak_source": "measured bf16_tflops / 2 (TF32 rate is half the bf16 rate)"},
+            "library_fp32": {"torch_fp32_ms": torch_ms, "speedup": torch_ms / ms},
+            "rel_l2_vs_float64": rel, "gpu_launches": steps, "clocks": clocks.summary()}
+    print(json.dumps(line))
+
+
 def run_chain(args):
     """Config 4: the permuted multilevel contraction chain (E = 64) on the tensor cores.
 
@@ -706,13 +778,15 @@ def main():
                          "2 streaming, 3 point-pair 4x4, 4 point-pair 16x1, 5 line-owner 8x3, 6 line-owner 4x5")
     ap.add_argument("--workload", default="sem3d",
                     choices=["sem3d", "chain", "batched-gemm", "large", "sem2d", "acoustic2d",
-                             "local"],
-                    help="sem3d: the headline SEM operator (default); chain: config 4 "
+                             "local", "gemm"],
+                    help="sem3d: the headline SEM operator (default); gemm: the general "
+                         "contraction's tensor-core GEMM; chain: config 4 "
                          "contraction; batched-gemm: config 2; large: config 5; sem2d: the "
                          "reference's 2D elastic operator; acoustic2d: config 1; local: "
                          "element-local at the reference's published sizes")
     ap.add_argument("--sem2d-elements", type=int, default=2621440)
     ap.add_argument("--large-mesh", type=int, default=128, help="hexes per side for --workload large")
+    ap.add_argument("--gemm-size", type=int, default=4096, help="M = N = K for --workload gemm")
     ap.add_argument("--chain-extent", type=int, default=64)
     ap.add_argument("--layout", default="components", choices=["components", "interleaved"],
                     help="assembled u / f: one array per component, or interleaved per node "
@@ -731,6 +805,8 @@ def main():
         return run_batched_gemm(args)
     if args.workload == "large":
         return run_large(args)
+    if args.workload == "gemm":
+        return run_gemm(args)
     if args.workload == "sem2d":
         return run_sem2d(args)
     if args.workload == "acoustic2d":

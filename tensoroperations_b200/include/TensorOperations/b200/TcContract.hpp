@@ -141,27 +141,60 @@ __global__ void tc_pack_kernel(const typename tc_side<Node, Side>::In in, float*
   }
 }
 
+// One thread per output element, in the output view's storage order (so the
+// writes are coalesced whatever the declared order); it reads its value from
+// the packed C.
 template <class Node, class View>
 __global__ void tc_unpack_kernel(const Node node, const View out, const float* __restrict__ C,
-                                 long long M, long long Nn, long long ldc) {
+                                 long long ldc) {
   using A = typename Node::node_a_type;
   using B = typename Node::node_b_type;
   constexpr int R = Node::Rank;
   constexpr auto perm = label_positions<typename Node::decl_seq, typename Node::canon_seq>();
-  const long long total = M * Nn;
+  constexpr bool left = std::is_same_v<typename View::array_layout, Kokkos::LayoutLeft>;
+  // canonical extents (freeA ++ freeB) from the operands, and the declared ones
+  long long cext[R > 0 ? R : 1];
+  {
+    constexpr auto la = to_array<typename A::modes_seq>();
+    constexpr auto lb = to_array<typename B::modes_seq>();
+    constexpr auto fa = Node::freeA;
+    constexpr auto fb = Node::freeB;
+    static_for<Node::FreeA>([&](auto dc) {
+      constexpr int d = decltype(dc)::value;
+      cext[d] = static_cast<long long>(node.node_a.handle.tensor.extent(index_of(la, fa[d])));
+    });
+    static_for<Node::FreeB>([&](auto dc) {
+      constexpr int d = decltype(dc)::value;
+      cext[Node::FreeA + d] = static_cast<long long>(node.node_b.handle.tensor.extent(index_of(lb, fb[d])));
+    });
+  }
+  long long dext[R > 0 ? R : 1];
+  long long total = 1;
+  for (int d = 0; d < R; ++d) {
+    const long long e = static_cast<long long>(out.extent(d));
+    dext[d] = cext[perm[d]] < e ? cext[perm[d]] : e;  // write what fits
+    total *= dext[d];
+  }
   for (long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x; t < total;
        t += (long long)gridDim.x * blockDim.x) {
-    const long long m = t / Nn, n = t - m * Nn;
-    long long cc[R > 0 ? R : 1];  // canonical: freeA ++ freeB
-    tc_decode<A, array_seq_t<Node::freeA>>(node.node_a, m, cc);
-    tc_decode<B, array_seq_t<Node::freeB>>(node.node_b, n, cc + Node::FreeA);
     long long g[R > 0 ? R : 1];
-    bool in = true;
-    for (int d = 0; d < R; ++d) {
-      g[d] = cc[perm[d]];
-      in = in && g[d] < static_cast<long long>(out.extent(d));
+    long long x = t;
+    if constexpr (left) {
+      for (int d = 0; d < R; ++d) {
+        g[d] = x % dext[d];
+        x /= dext[d];
+      }
+    } else {
+      for (int d = R - 1; d >= 0; --d) {
+        g[d] = x % dext[d];
+        x /= dext[d];
+      }
     }
-    if (!in) continue;  // an output view smaller than the node: write what fits
+    long long cc[R > 0 ? R : 1];
+    for (int d = 0; d < R; ++d) cc[perm[d]] = g[d];
+    long long m = 0, n = 0;
+    for (int d = 0; d < Node::FreeA; ++d) m = m * cext[d] + cc[d];
+    for (int d = Node::FreeA; d < R; ++d) n = n * cext[d] + cc[d];
     float v = C[m * ldc + n];
     if constexpr (!std::is_same_v<typename Node::hook_type, NoHook>)
       call_hook(node.hook_op, g, v, std::make_index_sequence<R>{});
@@ -213,7 +246,7 @@ int tc_try_contract(const Node& node, const View& out) {
     throw LevelGraphError(TO_ERR_CUDA, std::string("tensor-core contraction: pack: ") + cudaGetErrorString(e));
   if (int st = to_gemm_tf32x3(Mp, Np, Kp, Ahi, Alo, Bhi, Blo, C, nullptr))
     throw LevelGraphError(st, to_last_error());
-  tc_unpack_kernel<Node, View><<<blocks, 256>>>(node, out, C, M, Nn, Np);
+  tc_unpack_kernel<Node, View><<<blocks, 256>>>(node, out, C, Np);
   e = cudaGetLastError();
   if (e != cudaSuccess)
     throw LevelGraphError(TO_ERR_CUDA, std::string("tensor-core contraction: unpack: ") + cudaGetErrorString(e));
