@@ -66,6 +66,44 @@ long long tc_extent_product(const In& in, const std::array<int32_t, NL>& labs) {
   return p;
 }
 
+// The same over any node's shape (an input's or a nested node's storage order).
+template <class Nd, std::size_t NL>
+long long tc_shape_product(const Nd& nd, const std::array<int32_t, NL>& labs) {
+  constexpr auto lab = to_array<typename Nd::modes_seq>();
+  const auto sh = nd.shape();
+  long long p = 1;
+  for (std::size_t i = 0; i < NL; ++i) p *= static_cast<long long>(sh[index_of(lab, labs[i])]);
+  return p;
+}
+
+// True when fp32 contraction `node` is large enough for the tensor-core GEMM
+// (M, N >= 128, K >= 32).  A tree whose root qualifies evaluates its nested
+// operands first, so that the root can take that path.
+template <class Node>
+bool tc_sized(const Node& node) {
+  if constexpr (!std::is_same_v<typename Node::value_type, float> || Node::NumContracted == 0 ||
+                Node::FreeA == 0 || Node::FreeB == 0) {
+    return false;
+  } else {
+    return tc_enabled() && tc_shape_product(node.node_a, Node::freeA) >= 128 &&
+           tc_shape_product(node.node_b, Node::freeB) >= 128 &&
+           tc_shape_product(node.node_a, Node::contracted) >= 32;
+  }
+}
+
+// True when a fusible tree should still run in steps so that its root takes
+// the tensor-core GEMM: the root is tc_sized and has at least 2^27 multiply-
+// adds.  Measured on the reference's multilevel chain (root M = N = n, K = 32):
+// at n = 1024 the fused launch is faster (2.8 vs 1.8 TFLOP/s; three small
+// launches), at 2048 and 4096 the steps are (5.5 vs 4.7, 8.9 vs 5.7).
+template <class Node>
+bool tc_steps_pay(const Node& node) {
+  if (!tc_sized(node)) return false;
+  return tc_shape_product(node.node_a, Node::freeA) * tc_shape_product(node.node_b, Node::freeB) *
+             tc_shape_product(node.node_a, Node::contracted) >=
+         (1LL << 27);
+}
+
 #if defined(__CUDACC__)
 
 // Decode `idx` row-major over labels `labs` (last fastest), extents read from

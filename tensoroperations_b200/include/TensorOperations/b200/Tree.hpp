@@ -20,9 +20,12 @@
 // reference; sharing is what the DagGraph route is for.
 #pragma once
 
+#include <mutex>
 #include <tuple>
+#include <vector>
 
 #include <TensorOperations/b200/Dag.hpp>
+#include <TensorOperations/b200/TcContract.hpp>
 
 namespace TensorOperations {
 
@@ -147,6 +150,98 @@ struct TreeLowering {
     return DagGraph<V, ES, DeviceTuple<>, TypeList<>>{DeviceTuple<>{}};
   }
 };
+
+// ---- materialised intermediates --------------------------------------------
+// A tree whose nested contraction is read by a parent that contracts one of
+// its labels over several tiles cannot run as one fused launch: the level plan
+// would have to recompute the child once per contracted tile (reference
+// Evaluator.hpp re-evaluates the sub-tree per tile).  Such a tree runs in
+// steps instead: each non-input operand of the root is evaluated on its own,
+// with its own bundle, into a device buffer in its declared label order, and
+// the root then runs as a contraction of two inputs -- the self-staging member
+// or the tensor-core GEMM.  Results are the same sums in another order.  A
+// fusible tree also runs in steps when its root alone is a large tensor-core
+// GEMM (tc_steps_pay): the fused launch would do the root's contraction on
+// the CUDA cores.
+
+// Device buffers for those intermediates: kept and reused across launches and
+// never handed back to the driver (a cudaFree would synchronise the device on
+// every execute).  Reuse is stream-ordered: the frontend launches every
+// evaluation on the default stream.
+class IntermediateLease {
+ public:
+  IntermediateLease() = default;
+  IntermediateLease(const IntermediateLease&) = delete;
+  IntermediateLease& operator=(const IntermediateLease&) = delete;
+  ~IntermediateLease() {
+    if (idx_ == kNone) return;
+    std::lock_guard<std::mutex> lk(mu());
+    pool()[idx_].busy = false;
+  }
+
+  // The smallest idle buffer of at least `bytes` in that memory, else a new one.
+  void* acquire(std::size_t bytes, bool device) {
+    std::lock_guard<std::mutex> lk(mu());
+    auto& p = pool();
+    std::size_t best = kNone;
+    for (std::size_t i = 0; i < p.size(); ++i)
+      if (!p[i].busy && p[i].device == device && p[i].bytes >= bytes &&
+          (best == kNone || p[i].bytes < p[best].bytes))
+        best = i;
+    if (best == kNone) {
+      p.push_back({Kokkos::Impl::alloc_bytes(bytes, device, "TensorOperations intermediate"), bytes,
+                   device, false});
+      best = p.size() - 1;
+    }
+    p[best].busy = true;
+    idx_ = best;
+    return p[best].ptr;
+  }
+
+ private:
+  struct Buf {
+    void* ptr;
+    std::size_t bytes;
+    bool device;
+    bool busy;
+  };
+  static constexpr std::size_t kNone = ~std::size_t(0);
+  static std::vector<Buf>& pool() {
+    static auto* v = new std::vector<Buf>;  // intentionally never destroyed
+    return *v;
+  }
+  static std::mutex& mu() {
+    static auto* m = new std::mutex;
+    return *m;
+  }
+  std::size_t idx_ = kNone;
+};
+
+template <class V, int R>
+struct ptr_rank {
+  using type = typename ptr_rank<V, R - 1>::type*;
+};
+template <class V>
+struct ptr_rank<V, 0> {
+  using type = V;
+};
+template <class V, int R>
+using intermediate_view_t =
+    Kokkos::View<typename ptr_rank<V, R>::type, Kokkos::LayoutRight, Kokkos::MemoryUnmanaged>;
+
+template <class Node>
+constexpr bool has_nested_operand() {
+  if constexpr (dag_is_contraction_v<Node>)
+    return !dag_is_input_v<typename Node::node_a_type> || !dag_is_input_v<typename Node::node_b_type>;
+  else
+    return false;
+}
+
+// Evaluate operand `node` (bundle Spec) into a leased buffer and return an
+// input node over it under the node's declared labels; an input node is
+// returned as it is.
+template <class Spec, class Node>
+auto materialize(const Node& node, IntermediateLease& lease);
 
 // Roots of the lowered tree: the root node's slots, the last ones of the DAG.
 template <class Dag, class Seq>
@@ -277,6 +372,9 @@ struct Graph {
     return o;
   }
 
+  template <typename Spec, typename Node, typename Out>
+  static int run_in_steps(const Node& node, const Out& out);
+
   template <std::size_t I, typename Spec, typename Views>
   int run_output(const Views& views) const {
     using Node = std::tuple_element_t<I, OutputTuple>;
@@ -286,6 +384,12 @@ struct Graph {
     const auto dag = b200::TreeLowering<V, ES>::template dag_of<Spec>(std::get<I>(outputs));
     const typename TT::outputs_t outs{dag};
     constexpr int off = view_offset<I>();
+    if constexpr (b200::has_nested_operand<Node>()) {
+      // run in steps when a nested contraction is read over several contracted
+      // tiles, or when the root alone is a large tensor-core GEMM
+      if (!dag.index_consistent() || b200::tc_steps_pay(std::get<I>(outputs)))
+        return run_in_steps<Spec>(std::get<I>(outputs), std::get<off>(views));
+    }
     return [&]<std::size_t... K>(std::index_sequence<K...>) {
       return outs.execute(TeamPolicyTag<ES>{}, std::get<off + K>(views)...);
     }(std::make_index_sequence<static_cast<std::size_t>(b200::output_arity<Node>())>{});
@@ -293,6 +397,63 @@ struct Graph {
 };
 
 inline Graph<> make_graph() { return {}; }
+
+namespace b200 {
+template <class Spec, class Node>
+auto materialize(const Node& node, IntermediateLease& lease) {
+  if constexpr (dag_is_input_v<Node>) {
+    (void)lease;
+    return node;
+  } else {
+    using V = typename Node::value_type;
+    using ES = typename Node::exec_space;
+    constexpr int R = Node::Rank;
+    using DeclSeq = std::conditional_t<dag_is_contraction_v<Node>, typename Node::decl_seq,
+                                       typename Node::modes_seq>;
+    static_assert(output_arity<Node>() == 1,
+                  "Graph: a multi-output combine cannot be an operand of another node on the "
+                  "tree route (name its outputs through DagGraph instead)");
+    const auto sh = node.shape();
+    std::array<std::size_t, R> ext{};
+    for (int d = 0; d < R; ++d) {
+      if constexpr (dag_is_contraction_v<Node>) {
+        constexpr auto perm = label_positions<typename Node::decl_seq, typename Node::canon_seq>();
+        ext[d] = static_cast<std::size_t>(sh[perm[d]]);
+      } else {
+        ext[d] = static_cast<std::size_t>(sh[d]);
+      }
+    }
+    std::size_t elems = 1;
+    for (int d = 0; d < R; ++d) elems *= ext[d];
+    using TV = intermediate_view_t<V, R>;
+    constexpr bool dev = !std::is_same_v<typename TV::memory_space, Kokkos::HostSpace>;
+    V* p = static_cast<V*>(lease.acquire(elems * sizeof(V), dev));
+    const TV t = [&]<std::size_t... D>(std::index_sequence<D...>) {
+      return TV(p, ext[D]...);
+    }(std::make_index_sequence<R>{});
+    const auto step = std::get<0>(make_graph().ops(node));
+    step.execute(TeamPolicyTag<ES>{}, Spec{}, t);
+    return make_input_node(TensorHandle<TV, DeclSeq>{t});
+  }
+}
+}  // namespace b200
+
+template <typename OutputTuple>
+template <typename Spec, typename Node, typename Out>
+int Graph<OutputTuple>::run_in_steps(const Node& node, const Out& out) {
+  using V = typename Node::value_type;
+  using ES = typename Node::exec_space;
+  b200::IntermediateLease la, lb;
+  const auto a = b200::materialize<typename Spec::a_type>(node.node_a, la);
+  const auto b = b200::materialize<typename Spec::b_type>(node.node_b, lb);
+  using A = std::decay_t<decltype(a)>;
+  using B = std::decay_t<decltype(b)>;
+  using C = NodeHandle<ContractionTag, A, B, typename Node::decl_seq, V, ES, typename Node::hook_type>;
+  const C root{a, b, node.shape_, node.hook_op};
+  using TS = Tile<typename b200::plain_tile<typename Spec::a_type>::type,
+                  typename b200::plain_tile<typename Spec::b_type>::type, typename Spec::c_type>;
+  return std::get<0>(make_graph().ops(root)).execute(TeamPolicyTag<ES>{}, TS{}, out);
+}
 
 // Evaluator<TeamPolicyTag<ES>, Node, Spec>::scratch_size_per_team: the scratch
 // of `Node` under bundle `Spec` as the reference sizes a tree (reference

@@ -5,7 +5,11 @@
 // bundle tiles, an input hook and a contraction hook, ragged sizes:
 //   C[l, i] = h( sum_{j,k} A[j, i, k] * g(B[k, j, l]) )
 // through the tree route (make_graph().ops) and the DAG route (make_dag), plus
-// a small case (M < 128) that stays on the level evaluator.  Prints one line
+// a small case (M < 128) that stays on the level evaluator; and chains whose
+// intermediate is contracted over one (fused), three (run in steps, the root a
+// self-staging contraction) and four (in steps, the root on the tensor cores)
+// tiles; and a fusible chain whose root is large enough for the tensor cores
+// (in steps with them, fused without).  Prints one line
 // per case with the relative error and the league execute() returned (the
 // GEMM's tile count on the tensor-core path; the grid on the level path).
 // Run by tests/test_frontend_gpu.py, with and without
@@ -17,6 +21,7 @@
 
 #include <cmath>
 #include <cstdio>
+#include <vector>
 
 using namespace TensorOperations;
 using ES = Kokkos::DefaultExecutionSpace;
@@ -77,6 +82,55 @@ static double run_case(int I, int L, int J, int K, int route, int* league_out) {
   return std::sqrt(num / den);
 }
 
+// A chain whose intermediate is contracted over several tiles, run in steps
+// (the intermediate evaluated into a buffer, then the root):
+//   M[j, i] = m( sum_k A[i, k] B[k, j] ),  E[l, i] = sum_j M[j, i] D[j, l]
+struct MidHook {
+  KOKKOS_FUNCTION void operator()(int j, int i, float& v) const { v = v * 0.5f + 0.001f * (j - i); }
+};
+using TopBundle = Tile<StaticTile<32, 32>, StaticTile<32, 32>, StaticTile<32, 32>>;
+using MidBundle = Tile<StaticTile<32, 16>, StaticTile<16, 32>, StaticTile<32, 32>>;
+
+static double run_chain(int I, int L, int J, int K, int* league_out) {
+  V2 A("A", I, K), B("B", K, J), D("D", J, L), E("E", L, I);
+  auto hA = Kokkos::create_mirror_view(A);
+  auto hB = Kokkos::create_mirror_view(B);
+  auto hD = Kokkos::create_mirror_view(D);
+  for (int i = 0; i < I; ++i)
+    for (int k = 0; k < K; ++k) hA(i, k) = std::sin(0.017f * i - 0.5f * k);
+  for (int k = 0; k < K; ++k)
+    for (int j = 0; j < J; ++j) hB(k, j) = std::cos(0.3f * k + 0.023f * j);
+  for (int j = 0; j < J; ++j)
+    for (int l = 0; l < L; ++l) hD(j, l) = std::sin(0.011f * l + 0.031f * j + 0.2f);
+  Kokkos::deep_copy(A, hA);
+  Kokkos::deep_copy(B, hB);
+  Kokkos::deep_copy(D, hD);
+  auto M = make_contraction_node<'j', 'i'>(make_input_node(make_handle<'i', 'k'>(A)),
+                                           make_input_node(make_handle<'k', 'j'>(B)), MidHook{});
+  auto root = make_contraction_node<'l', 'i'>(M, make_input_node(make_handle<'j', 'l'>(D)));
+  auto [g, h] = make_graph().ops(root);
+  (void)h;
+  *league_out = g.execute(TeamPolicyTag<ES>{}, std::make_tuple(TopBundle{}, MidBundle{}), E);
+  Kokkos::fence();
+  auto hE = Kokkos::create_mirror_view_and_copy(Kokkos::HostSpace{}, E);
+  std::vector<double> mid(static_cast<std::size_t>(J) * I);
+  for (int j = 0; j < J; ++j)
+    for (int i = 0; i < I; ++i) {
+      double s = 0;
+      for (int k = 0; k < K; ++k) s += double(hA(i, k)) * double(hB(k, j));
+      mid[static_cast<std::size_t>(j) * I + i] = s * 0.5 + 0.001 * (j - i);
+    }
+  double num = 0, den = 0;
+  for (int l = 0; l < L; ++l)
+    for (int i = 0; i < I; ++i) {
+      double s = 0;
+      for (int j = 0; j < J; ++j) s += mid[static_cast<std::size_t>(j) * I + i] * double(hD(j, l));
+      num += (hE(l, i) - s) * (hE(l, i) - s);
+      den += s * s;
+    }
+  return std::sqrt(num / den);
+}
+
 int main(int argc, char* argv[]) {
   Kokkos::initialize(argc, argv);
   int rc = 0;
@@ -91,6 +145,19 @@ int main(int argc, char* argv[]) {
     for (const Case& c : cases) {
       int league = 0;
       const double err = run_case(c.I, c.L, c.J, c.K, c.route, &league);
+      std::printf("case %s err %.3e league %d\n", c.name, err, league);
+      if (!(err <= 1e-5)) rc = 1;
+    }
+    struct Chain {
+      const char* name;
+      int I, L, J, K;
+    } chains[] = {{"chain_one_tile", 96, 64, 32, 16},
+                  {"chain_three_tiles", 96, 64, 96, 16},
+                  {"chain_large", 384, 320, 128, 16},
+                  {"chain_large_one_tile", 2048, 2048, 32, 16}};
+    for (const Chain& c : chains) {
+      int league = 0;
+      const double err = run_chain(c.I, c.L, c.J, c.K, &league);
       std::printf("case %s err %.3e league %d\n", c.name, err, league);
       if (!(err <= 1e-5)) rc = 1;
     }

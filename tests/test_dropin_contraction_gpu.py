@@ -12,7 +12,11 @@ oracle/build_ref.py:
                         hand-tiled Kokkos team kernels, LayoutRight and
                         LayoutLeft inputs;
   permuted_combine      a contraction with a hook feeding a combine, the operand
-                        in four staging paths; every path must give one result.
+                        in four staging paths; every path must give one result;
+  multilevel_contraction E = (A B) D against its naive and hand-tiled chains,
+                        the intermediate's contracted label in one tile (one
+                        fused launch) and in four (run in steps: intermediate
+                        into a buffer, then the root).
 Each program prints PASS per row when its result matches (max relative
 difference < 1e-2); these tests require every row to pass (they do not hold
 the programs' timing ratios).
@@ -43,7 +47,8 @@ def _result_rows(stdout):
     return [ln for ln in stdout.splitlines() if "PASS(" in ln or "FAIL(" in ln]
 
 
-@pytest.mark.parametrize("name", ["permuted_contraction", "team_contraction", "permuted_combine"])
+@pytest.mark.parametrize("name", ["permuted_contraction", "team_contraction", "permuted_combine",
+                                  "multilevel_contraction"])
 def test_contraction_benchmark_results_match(name):
     r = _run(name)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]

@@ -12,7 +12,10 @@ conftest when stale) and only run on the GPU box:
   which the frontend runs as a tensor-core GEMM -- and, with
   TO_FRONTEND_TENSOR_CORES=0, on the level evaluator -- against float64 host
   loops (relative L2 <= 1e-5); the league execute() returns shows which path
-  ran (the GEMM's 128 x 256 tile count on the tensor cores).
+  ran (the GEMM's 128 x 256 tile count on the tensor cores).  The same
+  program runs contraction chains whose intermediate is contracted over
+  several tiles: the tree then runs in steps (intermediate into a buffer,
+  then the root), the root of the largest on the tensor cores.
 """
 import os
 import subprocess
@@ -34,7 +37,8 @@ def test_program(program):
 
 
 # league per case: the GEMM tile count (tensor cores) / the level grid
-TC_LEAGUES = {"tree_large": 6, "dag_large": 6, "tree_square": 8}
+TC_LEAGUES = {"tree_large": 6, "dag_large": 6, "tree_square": 8, "chain_large": 6,
+              "chain_large_one_tile": 128}
 
 
 @pytest.mark.gpu
@@ -50,6 +54,8 @@ def test_tensor_core_contraction(tensor_cores):
     assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-2000:]
     leagues = {ln.split()[1]: int(ln.split()[-1]) for ln in r.stdout.splitlines()
                if ln.startswith("case ")}
-    assert set(leagues) == {"tree_large", "dag_large", "tree_square", "dag_small"}
+    assert set(leagues) == {"tree_large", "dag_large", "tree_square", "dag_small",
+                            "chain_one_tile", "chain_three_tiles", "chain_large",
+                            "chain_large_one_tile"}
     for name, tiles in TC_LEAGUES.items():
         assert (leagues[name] == tiles) == tensor_cores, (name, leagues[name])
