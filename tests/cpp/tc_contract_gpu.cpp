@@ -9,7 +9,8 @@
 // intermediate is contracted over one (fused), three (run in steps, the root a
 // self-staging contraction) and four (in steps, the root on the tensor cores)
 // tiles; and a fusible chain whose root is large enough for the tensor cores
-// (in steps with them, fused without).  Prints one line
+// (in steps with them, fused without); and the permuted rank-4 chain of the
+// chain benchmark (config 4) at extent 32.  Prints one line
 // per case with the relative error and the league execute() returned (the
 // GEMM's tile count on the tensor-core path; the grid on the level path).
 // Run by tests/test_frontend_gpu.py, with and without
@@ -131,6 +132,68 @@ static double run_chain(int I, int L, int J, int K, int* league_out) {
   return std::sqrt(num / den);
 }
 
+// The permuted multilevel chain of the chain benchmark, through the public
+// tree API with rank-4 permuted operands:
+//   T[a, b, c, d] = sum_{e,f} A[a, e, c, f] B[f, b, e, d],
+//   R[a, d]       = sum_{b,c} T[a, b, c, d] C[c, b]
+// T's contracted labels b, c span four tiles, so the tree runs in steps: T on
+// the tensor cores (M = (a, c), N = (b, d), K = (e, f)), then R as a
+// self-staging contraction.
+using V4 = Kokkos::View<float****, Kokkos::LayoutRight>;
+using TBundle = Tile<StaticTile<4, 8, 8, 8>, StaticTile<8, 8, 8, 4>, StaticTile<4, 8, 8, 4>>;
+using RBundle = Tile<StaticTile<4, 8, 8, 4>, StaticTile<8, 8>, StaticTile<4, 4>>;
+
+static double run_config4(int n, int* league_out) {
+  V4 A("A", n, n, n, n), B("B", n, n, n, n);
+  V2 C("C", n, n), R("R", n, n);
+  auto hA = Kokkos::create_mirror_view(A);
+  auto hB = Kokkos::create_mirror_view(B);
+  auto hC = Kokkos::create_mirror_view(C);
+  for (int a = 0; a < n; ++a)
+    for (int e = 0; e < n; ++e)
+      for (int c = 0; c < n; ++c)
+        for (int f = 0; f < n; ++f) hA(a, e, c, f) = std::sin(0.37f * a + 0.11f * e - 0.23f * c + 0.05f * f);
+  for (int f = 0; f < n; ++f)
+    for (int b = 0; b < n; ++b)
+      for (int e = 0; e < n; ++e)
+        for (int d = 0; d < n; ++d) hB(f, b, e, d) = std::cos(0.13f * f - 0.29f * b + 0.07f * e + 0.41f * d);
+  for (int c = 0; c < n; ++c)
+    for (int b = 0; b < n; ++b) hC(c, b) = std::sin(0.19f * c - 0.31f * b + 0.5f);
+  Kokkos::deep_copy(A, hA);
+  Kokkos::deep_copy(B, hB);
+  Kokkos::deep_copy(C, hC);
+  auto T = make_contraction_node<'a', 'b', 'c', 'd'>(make_input_node(make_handle<'a', 'e', 'c', 'f'>(A)),
+                                                     make_input_node(make_handle<'f', 'b', 'e', 'd'>(B)));
+  auto root = make_contraction_node<'a', 'd'>(T, make_input_node(make_handle<'c', 'b'>(C)));
+  auto [g, h] = make_graph().ops(root);
+  (void)h;
+  *league_out = g.execute(TeamPolicyTag<ES>{}, std::make_tuple(RBundle{}, TBundle{}), R);
+  Kokkos::fence();
+  auto hR = Kokkos::create_mirror_view_and_copy(Kokkos::HostSpace{}, R);
+  // float64: W[a, c, b, d] = sum_{e,f} A B, then R = sum_{b,c} W C
+  std::vector<double> W(static_cast<std::size_t>(n) * n * n * n, 0.0);
+  for (int a = 0; a < n; ++a)
+    for (int c = 0; c < n; ++c)
+      for (int e = 0; e < n; ++e)
+        for (int f = 0; f < n; ++f) {
+          const double x = hA(a, e, c, f);
+          for (int b = 0; b < n; ++b)
+            for (int d = 0; d < n; ++d)
+              W[((static_cast<std::size_t>(a) * n + c) * n + b) * n + d] += x * double(hB(f, b, e, d));
+        }
+  double num = 0, den = 0;
+  for (int a = 0; a < n; ++a)
+    for (int d = 0; d < n; ++d) {
+      double s = 0;
+      for (int b = 0; b < n; ++b)
+        for (int c = 0; c < n; ++c)
+          s += W[((static_cast<std::size_t>(a) * n + c) * n + b) * n + d] * double(hC(c, b));
+      num += (hR(a, d) - s) * (hR(a, d) - s);
+      den += s * s;
+    }
+  return std::sqrt(num / den);
+}
+
 int main(int argc, char* argv[]) {
   Kokkos::initialize(argc, argv);
   int rc = 0;
@@ -159,6 +222,12 @@ int main(int argc, char* argv[]) {
       int league = 0;
       const double err = run_chain(c.I, c.L, c.J, c.K, &league);
       std::printf("case %s err %.3e league %d\n", c.name, err, league);
+      if (!(err <= 1e-5)) rc = 1;
+    }
+    {
+      int league = 0;
+      const double err = run_config4(32, &league);
+      std::printf("case config4_n32 err %.3e league %d\n", err, league);
       if (!(err <= 1e-5)) rc = 1;
     }
   }

@@ -15,7 +15,8 @@ conftest when stale) and only run on the GPU box:
   ran (the GEMM's 128 x 256 tile count on the tensor cores).  The same
   program runs contraction chains whose intermediate is contracted over
   several tiles: the tree then runs in steps (intermediate into a buffer,
-  then the root), the root of the largest on the tensor cores.
+  then the root), the root of the largest on the tensor cores; and the
+  permuted rank-4 chain (config 4) through the same API.
 """
 import os
 import subprocess
@@ -56,6 +57,6 @@ def test_tensor_core_contraction(tensor_cores):
                if ln.startswith("case ")}
     assert set(leagues) == {"tree_large", "dag_large", "tree_square", "dag_small",
                             "chain_one_tile", "chain_three_tiles", "chain_large",
-                            "chain_large_one_tile"}
+                            "chain_large_one_tile", "config4_n32"}
     for name, tiles in TC_LEAGUES.items():
         assert (leagues[name] == tiles) == tensor_cores, (name, leagues[name])
