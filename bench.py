@@ -766,6 +766,9 @@ def config_dict(prob, world):
 
 def main():
     global MESH_PER_GPU
+    # NCCL writes its log (at NCCL_DEBUG=WARN, the version line too) to stdout
+    # by default; stdout carries only the result line
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=1000)
