@@ -362,8 +362,10 @@ double to_chain_flops(int32_t E);
  * Team.hpp:318-927, with its permuted operands, Permute.hpp:127-228, packed
  * by the frontend).  Mp, Np, Kp must be positive multiples of 128, 256 and
  * 32 (pad with zeros); A* are [Mp][Kp], B* [Np][Kp], C [Mp][Np], row-major
- * fp32 in device memory, 16-byte aligned.  C is overwritten.  Asynchronous on
- * `stream`; allocates nothing. */
+ * fp32 in device memory, 16-byte aligned.  C is overwritten (when the tiles
+ * leave the last wave of SMs less than half full, those tiles are split in K
+ * between two CTAs that add into rows of C zeroed first on `stream`).
+ * Asynchronous on `stream`; allocates nothing. */
 int to_gemm_tf32x3(int64_t Mp, int64_t Np, int64_t Kp, const float* Ahi, const float* Alo,
                    const float* Bhi, const float* Blo, float* C, void* stream);
 

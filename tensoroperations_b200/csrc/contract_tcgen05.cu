@@ -342,10 +342,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 // [Mp][Np] row-major, Mp a multiple of 128, Np of 256, Kp of 32.  K runs in
 // chunks of kChunkIters steps alternating between the two TMEM accumulators,
 // the last chunk possibly shorter; each finished chunk is added in IEEE fp32.
+// One CTA per work unit (one CTA fits an SM).  Units [0, full_tiles) are whole
+// 128 x 256 tiles, stored; when the tiles do not fill the last wave of SMs,
+// each remaining tile is split in K between `split` (= 2) CTAs that add their
+// halves into C, zeroed by the host beforehand -- the last wave then takes
+// half as long.  Two contributions to a zero keep the sum independent of
+// their order.
 struct GemmArgs {
   float* C;
   long long ldc;
-  int k_iters;
+  int k_iters;     // K-iterations (of 32) of a whole tile
+  int tiles_n;     // tiles along N
+  int full_tiles;  // units that are whole tiles
+  int split;       // K-parts of each remaining tile (1 or 2)
 };
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -364,9 +373,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int k_iters = args.k_iters;
+  int tile = static_cast<int>(blockIdx.x), k_begin = 0, k_end = args.k_iters;
+  bool partial = false;
+  if (tile >= args.full_tiles) {
+    const int r = tile - args.full_tiles, part = r % args.split;
+    tile = args.full_tiles + r / args.split;
+    k_begin = static_cast<int>(static_cast<long long>(args.k_iters) * part / args.split);
+    k_end = static_cast<int>(static_cast<long long>(args.k_iters) * (part + 1) / args.split);
+    partial = args.split > 1;
+  }
+  const int k_iters = k_end - k_begin;
   const int nchunks = (k_iters + kChunkIters - 1) / kChunkIters;
-  const int m_tile = blockIdx.y, n_tile = blockIdx.x;
+  const int m_tile = tile / args.tiles_n, n_tile = tile % args.tiles_n;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -403,10 +421,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (*reinterpret_cast<volatile int*>(abort_flag)) break;
       unsigned char* st = tiles + s * kStageBytes;
       mbar_arrive_expect_tx(&full[s], kStageBytes);
-      tma_load_2d(st, &mAhi, it * kTileK, m_tile * kTileM, &full[s]);
-      tma_load_2d(st + kABytes, &mAlo, it * kTileK, m_tile * kTileM, &full[s]);
-      tma_load_2d(st + 2 * kABytes, &mBhi, it * kTileK, n_tile * kTileN, &full[s]);
-      tma_load_2d(st + 2 * kABytes + kBBytes, &mBlo, it * kTileK, n_tile * kTileN, &full[s]);
+      const int kx = (k_begin + it) * kTileK;
+      tma_load_2d(st, &mAhi, kx, m_tile * kTileM, &full[s]);
+      tma_load_2d(st + kABytes, &mAlo, kx, m_tile * kTileM, &full[s]);
+      tma_load_2d(st + 2 * kABytes, &mBhi, kx, n_tile * kTileN, &full[s]);
+      tma_load_2d(st + 2 * kABytes + kBBytes, &mBlo, kx, n_tile * kTileN, &full[s]);
       issued = it + 1;
     }
     if (!ok) {
@@ -490,9 +509,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (live) {
       float4* out = reinterpret_cast<float4*>(args.C + (size_t(m_tile) * kTileM + row) * args.ldc +
                                               size_t(n_tile) * kTileN + h * 128);
+      if (partial) {
 #pragma unroll
-      for (int x = 0; x < 32; ++x)
-        out[x] = make_float4(acc[4 * x], acc[4 * x + 1], acc[4 * x + 2], acc[4 * x + 3]);
+        for (int x = 0; x < 32; ++x)
+          atomicAdd(out + x, make_float4(acc[4 * x], acc[4 * x + 1], acc[4 * x + 2], acc[4 * x + 3]));
+      } else {
+#pragma unroll
+        for (int x = 0; x < 32; ++x)
+          out[x] = make_float4(acc[4 * x], acc[4 * x + 1], acc[4 * x + 2], acc[4 * x + 3]);
+      }
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -687,8 +712,8 @@ int to_gemm_tf32x3(int64_t Mp, int64_t Np, int64_t Kp, const float* Ahi, const f
     return set_error(TO_ERR_INVALID_ARGUMENT,
                      "to_gemm_tf32x3: sizes %lld x %lld x %lld must be positive multiples of "
                      "128 x 256 x 32", (long long)Mp, (long long)Np, (long long)Kp);
-  if (Mp / kTileM > 65535 || Kp / kTileK > (1ll << 30))
-    return set_error(TO_ERR_INVALID_ARGUMENT, "to_gemm_tf32x3: M or K too large");
+  if ((Mp / kTileM) * (Np / kTileN) > (1ll << 30) || Kp / kTileK > (1ll << 30))
+    return set_error(TO_ERR_INVALID_ARGUMENT, "to_gemm_tf32x3: M x N or K too large");
   const void* ptrs[] = {Ahi, Alo, Bhi, Blo, C};
   for (const void* p : ptrs) {
     if (!p) return set_error(TO_ERR_INVALID_ARGUMENT, "to_gemm_tf32x3: null pointer");
@@ -715,10 +740,22 @@ int to_gemm_tf32x3(int64_t Mp, int64_t Np, int64_t Kp, const float* Ahi, const f
                                 int(kSmemBytes));
   });
   TO_CUDA_TRY(attr);
-  GemmArgs args{C, (long long)Np, int(Kp / kTileK)};
-  const dim3 grid(unsigned(Np / kTileN), unsigned(Mp / kTileM));
-  gemm_tcgen05_kernel<<<grid, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(
-      mAhi, mAlo, mBhi, mBlo, args);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const long long tiles_n = Np / kTileN, tiles = (Mp / kTileM) * tiles_n;
+  const int k_iters = static_cast<int>(Kp / kTileK);
+  int dev = 0;
+  const int sms = device_sm_count(&dev);
+  const long long tail = sms > 0 ? tiles % sms : 0;
+  GemmArgs args{C, (long long)Np, k_iters, static_cast<int>(tiles_n), static_cast<int>(tiles), 1};
+  if (tail > 0 && 2 * tail <= sms && k_iters >= 2) {
+    // split the partial last wave in K; zero the rows of tiles it adds into
+    args.split = 2;
+    args.full_tiles = static_cast<int>(tiles - tail);
+    const long long row0 = (args.full_tiles / tiles_n) * kTileM;
+    TO_CUDA_TRY(cudaMemsetAsync(C + row0 * Np, 0, size_t((Mp - row0) * Np) * sizeof(float), s));
+  }
+  const long long units = args.full_tiles + (tiles - args.full_tiles) * args.split;
+  gemm_tcgen05_kernel<<<unsigned(units), kThreads, kSmemBytes, s>>>(mAhi, mAlo, mBhi, mBlo, args);
   TO_CUDA_TRY(cudaGetLastError());
   return ok();
 }

@@ -5,7 +5,10 @@ hi/lo splits (three TF32 products, fp32 accumulation in TMEM drained in IEEE
 fp32).  Against a float64 product of the same fp32 inputs: relative L2 error
 <= 1e-5 (the dropped lo*lo term is about 2^-22), for K within one
 accumulation chunk, across several chunks and with a ragged last chunk, and
-with zero-padded rows / columns.  Argument errors are reported, not faulted.
+with zero-padded rows / columns.  Grids smaller than the 148 SMs, and the
+tiles of a partial last wave, are split in K between two CTAs adding into a
+zeroed C; a last wave fuller than half the SMs is not.  Argument errors are
+reported, not faulted.
 """
 import numpy as np
 import pytest
@@ -47,6 +50,8 @@ def run(M, N, K, Mp, Np, Kp, seed):
     (300, 500, 200, 384, 512, 224),      # ragged, zero-padded, one chunk
     (256, 256, 1504, 256, 256, 1504),    # 47 K steps: two full chunks and a ragged one
     (1024, 768, 4096, 1024, 768, 4096),  # 128 K steps, 8 chunks
+    (1600, 3000, 90, 1664, 3072, 96),    # 156 tiles: one full wave, the last 8 split in K
+    (1536, 5120, 64, 1536, 5120, 64),    # 240 tiles: a last wave of 92, not split
 ])
 def test_gemm_matches_float64(M, N, K, Mp, Np, Kp):
     err, got, ref = run(M, N, K, Mp, Np, Kp, seed=M + N + K)
