@@ -48,6 +48,8 @@ struct resolve_member {
 };
 template <class LT, class M>
 struct resolve_member<LT, M, StagedTag> {
+  static_assert(std::is_same_v<typename M::operand_type::node_tag, InputTag>,
+                "level graph: a stage member copies an input node into scratch");
   using type = NodeHandle<StagedTag, typename M::operand_type, typename M::modes_seq,
                           tile_from_labels_t<LT, typename M::modes_seq>>;
   static type get(const M& m) { return type{m.operand_}; }
@@ -348,3 +350,5 @@ auto make_level_graph(LabelTilesT) {
 }
 
 }  // namespace TensorOperations
+
+#include <TensorOperations/b200/ImplNames.hpp>

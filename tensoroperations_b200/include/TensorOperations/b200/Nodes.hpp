@@ -277,8 +277,9 @@ struct NodeHandle<StagedTag, Operand, ModesSeq, Tile> {
 
 template <typename Operand>
 auto make_stage_node(Operand op) {
-  static_assert(std::is_same_v<typename Operand::node_tag, InputTag>,
-                "make_stage_node: the operand must be an input node");
+  static_assert(std::is_same_v<typename Operand::node_tag, InputTag> ||
+                    std::is_same_v<typename Operand::node_tag, SlotTag>,
+                "make_stage_node: the operand must be an input node (or, in a DAG, a slot)");
   return NodeHandle<StagedTag, Operand, typename Operand::modes_seq, void>{op};
 }
 

@@ -1,4 +1,4 @@
-"""The reference's own unit tests that use only the public API, unmodified, on B200 (GPU).
+"""The reference's own unit tests, unmodified, on B200 (GPU).
 
 oracle/_ref/test_<name> are the reference's tests/test_<name>.cpp compiled for
 sm_100a against this repository's frontend and Kokkos subset, with
@@ -10,8 +10,21 @@ tests/cpp/gtest_shim standing in for the GoogleTest calls they make
                          less scratch; multi-tiled grid labels gathered by label;
   test_contraction_node  node construction, shapes, stored hooks;
   test_device_tuple      DeviceTuple on host and in a kernel;
-  test_concept           TensorLike and the handle's element access.
-Each prints one line per test and exits non-zero if any failed.
+  test_concept           TensorLike and the handle's element access;
+  test_level_graph       the LevelGraph slot algebra, tile derivation and level
+                         guards (static), and graphs executed against host
+                         references: one contraction, a three-direction
+                         gradient level, combine over contraction, multi-output
+                         combine, declared-order roots, combines and
+                         contractions over declared slots, the combine's
+                         global coordinate;
+  test_level_liveness    level liveness and left-edge pooling (static), and the
+                         pooled chain ((A B) E) F against a host reference;
+  test_label_tiles       every SEM3D tile from the label map (static).
+The level-graph tests also name the reference's internal plan names, which
+b200/ImplNames.hpp spells over this build's plan code.  Their static asserts
+are checked when oracle/build_ref.py compiles them.  Each program prints one
+line per test and exits non-zero if any failed.
 """
 import os
 import subprocess
@@ -25,7 +38,8 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("name", ["test_dag_graph", "test_contraction_node", "test_device_tuple",
-                                  "test_concept"])
+                                  "test_concept", "test_level_graph", "test_level_liveness",
+                                  "test_label_tiles"])
 def test_reference_unit_test_passes(name):
     exe = REF / name
     if not exe.exists():
