@@ -13,12 +13,16 @@
 // Where the reference asserts (index_consistent) or traps, this build throws
 // TensorOperations::LevelGraphError with a one-line reason.
 //
-// Scratch accounting.  The reference stages each node's input operands in a
-// per-node arena next to the slot store.  Here a staged input is a slot of the
-// lowered plan, pooled by liveness with everything else, so
-// DagOutputs::slot_bytes() is the whole request and operand_bytes() is 0;
-// DagGraph::slot_bytes() / operand_bytes() keep the reference's un-pooled
-// bounds (one tile per node output / per staged operand).
+// Scratch accounting.  The numbers are the reference's account of the DAG
+// (reference DagGraph.hpp: DagGraph::slot_bytes / operand_bytes /
+// pooled_slot_bytes / arena_bytes, DagOutputs::slot_bytes / operand_bytes /
+// num_pools): DagGraph::slot_bytes() / operand_bytes() are the un-pooled bounds
+// (one tile per node output / per staged operand); DagOutputs::slot_bytes() and
+// num_pools pool the node outputs by live range on the node timeline (a root
+// lives past the last node), and DagOutputs::operand_bytes() is the largest
+// single node's operand staging.  What a launch here requests is the lowered
+// level plan's store, where staged inputs are slots pooled with everything
+// else: DagOutputs::launch_scratch_bytes().
 #pragma once
 
 #include <TensorOperations/LabelTiles.hpp>
@@ -89,13 +93,50 @@ struct DagGraph {
     }
     return b;
   }
-  // Staged operands live in the pooled store: there is no separate arena.
-  std::size_t arena_bytes() const { return 0; }
-  std::size_t arena_elems() const { return 0; }
+  // The largest single node's operand staging (no two nodes' staged operands
+  // are live together).
+  std::size_t arena_bytes() const { return max_node_operand_bytes(); }
+  std::size_t arena_elems() const { return (arena_bytes() + sizeof(ValueType) - 1) / sizeof(ValueType); }
 
-  // The store of the lowered plan, pooled by liveness for these roots.
+  static constexpr std::size_t max_node_operand_bytes() {
+    using Low = lowering;
+    std::array<std::size_t, N + 1> per{};
+    for (std::size_t s = 0; s < Low::NS; ++s) {
+      std::size_t e = 1;
+      for (int d = 0; d < Low::srows[s].rank; ++d) e *= static_cast<std::size_t>(Low::srows[s].tile[d]);
+      per[Low::stages[s].node] += round16(e * sizeof(ValueType));
+    }
+    std::size_t m = 0;
+    for (std::size_t b : per)
+      if (b > m) m = b;
+    return m;
+  }
+
+  // The node-output slots pooled by live range for these roots: the sum of the
+  // pools' largest slots.
   template <std::size_t... Roots>
   std::size_t pooled_slot_bytes() const {
+    return node_pooled_slot_bytes<Roots...>();
+  }
+  template <std::size_t... Roots>
+  static constexpr std::size_t node_pooled_slot_bytes() {
+    constexpr std::size_t NSL = num_slots();
+    constexpr auto pool = Impl::dag_pool_of_slot<NodesT, Roots...>();
+    constexpr auto sz = slot_sizes(std::make_index_sequence<N>{});
+    std::array<std::size_t, NSL + 1> pmax{};
+    for (std::size_t s = 0; s < NSL; ++s) {
+      const auto q = static_cast<std::size_t>(pool[s]);
+      if (sz[s] > pmax[q]) pmax[q] = sz[s];
+    }
+    std::size_t b = 0;
+    for (std::size_t x : pmax) b += x;
+    return b;
+  }
+
+  // The store the launch requests: the lowered level plan's, pooled by
+  // liveness for these roots (staged inputs included).
+  template <std::size_t... Roots>
+  std::size_t launch_scratch_bytes() const {
     using Low = lowering;
     return b200::Layout<ValueType, typename Low::levels_t, Low::level_slot(Roots)...>::scratch_bytes;
   }
@@ -208,6 +249,24 @@ struct DagGraph {
                            b200::DagSlotHandle<Base + Ms, ValueType, ExecSpace, SL, ST>{shape}...);
   }
 
+  // Bytes of each node-output slot, in slot order.
+  template <std::size_t... K>
+  static constexpr auto slot_sizes(std::index_sequence<K...>) {
+    std::array<std::size_t, num_slots() + 1> out{};
+    std::size_t s = 0;
+    ((
+         [&] {
+           using Node = tuple_element_t<K, NodesT>;
+           constexpr auto st =
+               b200::dag_storage_tile<Node, typename b200::tl_at<K, TilesL>::type>();
+           std::size_t e = 1;
+           for (int d = 0; d < Node::Rank; ++d) e *= static_cast<std::size_t>(st[d]);
+           for (int o = 0; o < b200::output_arity<Node>(); ++o) out[s++] = round16(e * sizeof(ValueType));
+         }()),
+     ...);
+    return out;
+  }
+
   template <std::size_t... K>
   static constexpr std::size_t slot_bytes_impl(std::index_sequence<K...>) {
     return (std::size_t{0} + ... +
@@ -240,9 +299,11 @@ struct DagOutputs {
   std::size_t slot_bytes() const { return dag.template pooled_slot_bytes<Roots...>(); }
   std::size_t operand_bytes() const { return dag.arena_bytes(); }
   std::size_t scratch_bytes() const { return slot_bytes() + operand_bytes(); }
+  // What a launch requests (the lowered level plan's pooled store).
+  std::size_t launch_scratch_bytes() const { return dag.template launch_scratch_bytes<Roots...>(); }
 
   static constexpr std::size_t num_pools =
-      b200::Pooling<typename Dag::lowering::levels_t, Dag::lowering::level_slot(Roots)...>::num_pools;
+      Impl::dag_pool_count<typename Dag::nodes_type, Roots...>();
 
   template <typename ES, TensorLike... Ts>
   int execute(const TeamPolicyTag<ES>&, const Ts&... ts) const {

@@ -22,6 +22,9 @@
 //   Impl::lg_resolve_member(_t)         resolve_member (a stage's tile from the map)
 //   Impl::canonC_modes_seq_t<R, A, B>   freeA in A's order ++ freeB in B's order
 //   Impl::label_tile_v / label_tiles_distinct_v   LabelTiles::tile / distinct
+//   Impl::permA_seq_t / permB_seq_t / permC_seq_t / inverse_perm_seq_t /
+//     is_identity_seq / operand_stageable_v   the contraction's operand
+//                                       permutations (test_graph.cpp)
 //   Impl::dag_num_slots / dag_operand_slot / dag_pool_of_slot / dag_pool_count
 //                                       slot liveness on a flat node list (below)
 #pragma once
@@ -32,6 +35,7 @@
 
 #include <TensorOperations/LabelTiles.hpp>
 #include <TensorOperations/b200/Plan.hpp>
+#include <TensorOperations/b200/TileSpec.hpp>
 
 namespace TensorOperations {
 
@@ -120,6 +124,86 @@ using canonC_modes_seq_t =
     typename b200::concat_seq<b200::array_seq_t<b200::minus_labels<A, B>::values()>,
                               b200::array_seq_t<b200::minus_labels<B, A>::values()>>::type;
 
+// Operand permutations of a contraction, gather convention (perm[c] = the
+// user axis that becomes canonical axis c): canonical A = freeA ++ contracted
+// (both in A's order), canonical B = contracted (A's order) ++ freeB, canonical
+// C = freeA ++ freeB.  This build reads operands through these permutations
+// instead of permuting them in scratch; the names serve the reference's plan
+// checks (reference Permute.hpp).
+namespace perm_detail {
+template <class Seq, class Labs>
+struct positions;
+template <class Seq, int32_t... L>
+struct positions<Seq, std::integer_sequence<int32_t, L...>> {
+  using type = std::integer_sequence<int, b200::index_of(b200::to_array<Seq>(), L)...>;
+};
+template <class A, class B>
+using canon_a_t =
+    typename b200::concat_seq<b200::array_seq_t<b200::minus_labels<A, B>::values()>,
+                              b200::array_seq_t<b200::common_labels<A, B>::values()>>::type;
+template <class A, class B>
+using canon_b_t =
+    typename b200::concat_seq<b200::array_seq_t<b200::common_labels<A, B>::values()>,
+                              b200::array_seq_t<b200::minus_labels<B, A>::values()>>::type;
+template <class Perm>
+struct inverse_of;
+template <int... P>
+struct inverse_of<std::integer_sequence<int, P...>> {
+  static constexpr std::size_t n = sizeof...(P);
+  static constexpr std::array<int, n> inv = [] {
+    std::array<int, n> r{};
+    const int p[] = {P..., 0};
+    for (std::size_t j = 0; j < n; ++j) r[static_cast<std::size_t>(p[j])] = static_cast<int>(j);
+    return r;
+  }();
+  template <std::size_t... I>
+  static auto make(std::index_sequence<I...>) -> std::integer_sequence<int, inv[I]...>;
+  using type = decltype(make(std::make_index_sequence<n>{}));
+};
+template <class S>
+struct out_tile {
+  using type = S;
+};
+template <class A, class B, class C>
+struct out_tile<Tile<A, B, C>> {
+  using type = C;
+};
+}  // namespace perm_detail
+
+template <typename A, typename B>
+using permA_seq_t = typename perm_detail::positions<A, perm_detail::canon_a_t<A, B>>::type;
+template <typename A, typename B>
+using permB_seq_t = typename perm_detail::positions<B, perm_detail::canon_b_t<A, B>>::type;
+template <int Rank, typename A, typename B, typename Out>
+using permC_seq_t = typename perm_detail::positions<Out, canonC_modes_seq_t<Rank, A, B>>::type;
+template <typename Perm>
+using inverse_perm_seq_t = typename perm_detail::inverse_of<Perm>::type;
+
+template <int... P>
+constexpr bool is_identity_seq(std::integer_sequence<int, P...>) {
+  int i = 0;
+  return ((P == i++) && ...);
+}
+
+// The reference evaluator's staging rule for a permuted operand: a fused
+// (node) operand is reordered inside its own output tile, so the permutation
+// must map that tile's extents onto themselves; an input is copied into a
+// fresh buffer and always qualifies.  (This build reads a fused operand
+// through its storage permutation and has no such restriction; the predicate
+// is kept for the reference's plan checks.)
+template <typename Operand, typename TileSpec, typename Perm>
+inline constexpr bool operand_stageable_v = [] {
+  if constexpr (std::is_same_v<typename Operand::node_tag, InputTag>) {
+    return true;
+  } else {
+    using T = typename perm_detail::out_tile<TileSpec>::type;
+    constexpr auto p = b200::to_array_int<Perm>();
+    for (std::size_t i = 0; i < p.size(); ++i)
+      if (T::extents[static_cast<std::size_t>(p[i])] != T::extents[i]) return false;
+    return true;
+  }
+}();
+
 template <typename LT, int32_t L>
 inline constexpr int label_tile_v = LT::tile(L);
 template <typename LT>
@@ -140,6 +224,8 @@ template <typename Op>
 constexpr std::size_t slot_of() {
   if constexpr (requires { Op::SlotIdx; })
     return Op::SlotIdx;
+  else if constexpr (requires { Op::slot_index; })
+    return Op::slot_index;
   else
     return kNone;
 }

@@ -251,6 +251,21 @@ auto make_input_node(TensorHandle<T, ModesSeq> h, HookOp hook = {}) {
   return NodeHandle<InputTag, T, ModesSeq, HookOp>{h, hook};
 }
 
+// Intermediate: a view the evaluator owns, named as a node (reference
+// NodeHandle.hpp IntermTag, make_interm_node).  This build's evaluators keep
+// intermediates in slots, so the node only carries its storage and tag.
+template <typename Storage>
+struct NodeHandle<IntermTag, Storage> {
+  using node_tag = IntermTag;
+  using storage_type = Storage;
+  Storage storage;
+};
+
+template <typename Storage>
+auto make_interm_node(Storage s) {
+  return NodeHandle<IntermTag, Storage>{s};
+}
+
 // Stage: a tile of an input copied on chip.  Tile is void until the graph
 // resolves it from its label map (LevelGraph::add).
 template <typename Operand, typename ModesSeq, typename Tile>

@@ -203,7 +203,9 @@ int main(int argc, char** argv) {
   const auto outs = dag.outputs(r0, r1, r2);
   std::printf("pools %zu scratch %zu unpooled %zu\n", decltype(outs)::num_pools, outs.scratch_bytes(),
               dag.scratch_bytes());
-  if (outs.operand_bytes() != 0 || outs.scratch_bytes() > dag.scratch_bytes()) return 1;
+  if (outs.slot_bytes() > dag.slot_bytes() || outs.operand_bytes() > dag.operand_bytes() ||
+      outs.launch_scratch_bytes() == 0)
+    return 1;
 
   if (dag.needs_contracted_tiles()) return 1;
   auto emulate = [&]<class L>(L) {

@@ -20,7 +20,15 @@ tests/cpp/gtest_shim standing in for the GoogleTest calls they make
                          global coordinate;
   test_level_liveness    level liveness and left-edge pooling (static), and the
                          pooled chain ((A B) E) F against a host reference;
-  test_label_tiles       every SEM3D tile from the label map (static).
+  test_label_tiles       every SEM3D tile from the label map (static);
+  test_graph             the tree route: einsum permutation plans (static), one
+                         and several tiles per label, non-square and
+                         non-symmetric tiles, permuted inputs / outputs /
+                         contracted order, input and contraction hooks at
+                         global indices across tiles, fused two-level chains,
+                         permuted fused operands -- each against a host loop;
+  test_nodehandle        node tags, input nodes over a user TensorLike type;
+  test_slot_liveness     DAG slot liveness and pooling.
 The level-graph tests also name the reference's internal plan names, which
 b200/ImplNames.hpp spells over this build's plan code.  Their static asserts
 are checked when oracle/build_ref.py compiles them.  Each program prints one
@@ -39,7 +47,8 @@ pytestmark = pytest.mark.gpu
 
 @pytest.mark.parametrize("name", ["test_dag_graph", "test_contraction_node", "test_device_tuple",
                                   "test_concept", "test_level_graph", "test_level_liveness",
-                                  "test_label_tiles"])
+                                  "test_label_tiles", "test_graph", "test_nodehandle",
+                                  "test_slot_liveness"])
 def test_reference_unit_test_passes(name):
     exe = REF / name
     if not exe.exists():
