@@ -766,9 +766,14 @@ def config_dict(prob, world):
 
 def main():
     global MESH_PER_GPU
-    # NCCL writes its log (at NCCL_DEBUG=WARN, the version line too) to stdout
-    # by default; stdout carries only the result line
-    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+    # Native libraries write to file descriptor 1 directly (NCCL prints its
+    # version line there at communicator set-up): point it at stderr and keep
+    # Python's stdout on a duplicate of the original, so stdout carries only
+    # the result line
+    sys.stdout.flush()
+    result_fd = os.dup(1)
+    os.dup2(2, 1)
+    sys.stdout = os.fdopen(result_fd, "w", buffering=1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=1000)
