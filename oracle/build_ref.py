@@ -60,7 +60,7 @@ CONTRACTION_BENCHES = ("permuted_contraction", "multilevel_contraction", "permut
 UNIT_TESTS = {"test_dag_graph": True, "test_device_tuple": True, "test_contraction_node": True,
               "test_concept": False, "test_level_graph": True, "test_level_liveness": True,
               "test_label_tiles": True, "test_graph": True, "test_nodehandle": True,
-              "test_slot_liveness": True}
+              "test_slot_liveness": True, "test_combine_node": True}
 GTEST_SHIM = ROOT / "tests" / "cpp" / "gtest_shim"
 INC = [f"-I{ROOT / 'include'}", f"-I{ROOT / 'tensoroperations_b200' / 'include'}"]
 LIBDIR = ROOT / "tensoroperations_b200"

@@ -25,6 +25,9 @@
 //   Impl::permA_seq_t / permB_seq_t / permC_seq_t / inverse_perm_seq_t /
 //     is_identity_seq / operand_stageable_v   the contraction's operand
 //                                       permutations (test_graph.cpp)
+//   Impl::label_perm_seq_t / same_label_set / produces_own_scratch_v /
+//     fusable_operand_v / operand_relabelable_v   the combine's operand rules
+//                                       (test_combine_node.cpp)
 //   Impl::dag_num_slots / dag_operand_slot / dag_pool_of_slot / dag_pool_count
 //                                       slot liveness on a flat node list (below)
 #pragma once
@@ -168,7 +171,38 @@ template <class A, class B, class C>
 struct out_tile<Tile<A, B, C>> {
   using type = C;
 };
+template <class O, class... Ops>
+struct out_tile<CombineTile<O, Ops...>> {
+  using type = O;
+};
+template <class Op>
+constexpr bool hooked() {
+  if constexpr (requires { typename Op::hook_type; })
+    return !std::is_same_v<typename Op::hook_type, NoHook>;
+  else
+    return false;
+}
 }  // namespace perm_detail
+
+// A combine gathers each operand into its output order: perm[o] = the operand
+// axis carrying output label o (reference Permute.hpp label_perm).
+template <typename OutSeq, typename OpSeq>
+using label_perm_seq_t = typename perm_detail::positions<OpSeq, OutSeq>::type;
+
+template <typename A, typename B>
+constexpr bool same_label_set() {
+  return b200::same_label_set<A, B>();
+}
+
+// A contraction or combine hands its output back in scratch it owns; an input
+// is the user's tensor.  Both kinds are legal operands.
+template <typename Op>
+inline constexpr bool produces_own_scratch_v =
+    std::is_same_v<typename Op::node_tag, ContractionTag> ||
+    std::is_same_v<typename Op::node_tag, CombineTag>;
+template <typename Op>
+inline constexpr bool fusable_operand_v =
+    std::is_same_v<typename Op::node_tag, InputTag> || produces_own_scratch_v<Op>;
 
 template <typename A, typename B>
 using permA_seq_t = typename perm_detail::positions<A, perm_detail::canon_a_t<A, B>>::type;
@@ -203,6 +237,16 @@ inline constexpr bool operand_stageable_v = [] {
     return true;
   }
 }();
+
+// The reference combine evaluator's relabel rule: a permuted operand that
+// produces its own scratch and carries no hook is read through a relabel
+// instead of being reordered (an input is never relabelled, an unpermuted
+// operand is passed through).  This build reads every operand through its
+// permutation; the predicate is kept for the reference's plan checks.
+template <typename Operand, typename Perm>
+inline constexpr bool operand_relabelable_v =
+    produces_own_scratch_v<Operand> && !perm_detail::hooked<Operand>() &&
+    !is_identity_seq(Perm{});
 
 template <typename LT, int32_t L>
 inline constexpr int label_tile_v = LT::tile(L);

@@ -243,6 +243,12 @@ constexpr bool has_nested_operand() {
 template <class Spec, class Node>
 auto materialize(const Node& node, IntermediateLease& lease);
 
+// The handle of output M of a multi-output root (its index among the outputs).
+template <std::size_t M>
+struct OutputHandle : std::integral_constant<std::size_t, M> {
+  static constexpr std::size_t OutputIndex = M;
+};
+
 // Roots of the lowered tree: the root node's slots, the last ones of the DAG.
 template <class Dag, class Seq>
 struct tree_outputs;
@@ -355,7 +361,7 @@ struct Graph {
       return std::make_tuple(n);
     else
       return [&]<std::size_t... Ms>(std::index_sequence<Ms...>) {
-        return std::make_tuple(std::integral_constant<std::size_t, Ms>{}...);
+        return std::make_tuple(b200::OutputHandle<Ms>{}...);
       }(std::make_index_sequence<static_cast<std::size_t>(M)>{});
   }
 

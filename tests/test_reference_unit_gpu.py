@@ -28,7 +28,11 @@ tests/cpp/gtest_shim standing in for the GoogleTest calls they make
                          global indices across tiles, fused two-level chains,
                          permuted fused operands -- each against a host loop;
   test_nodehandle        node tags, input nodes over a user TensorLike type;
-  test_slot_liveness     DAG slot liveness and pooling.
+  test_slot_liveness     DAG slot liveness and pooling;
+  test_combine_node      combines: label gathers, multi-output combines,
+                         combines over permuted and hooked contractions and
+                         over other combines, coordinates -- against host
+                         loops.
 The level-graph tests also name the reference's internal plan names, which
 b200/ImplNames.hpp spells over this build's plan code.  Their static asserts
 are checked when oracle/build_ref.py compiles them.  Each program prints one
@@ -48,7 +52,7 @@ pytestmark = pytest.mark.gpu
 @pytest.mark.parametrize("name", ["test_dag_graph", "test_contraction_node", "test_device_tuple",
                                   "test_concept", "test_level_graph", "test_level_liveness",
                                   "test_label_tiles", "test_graph", "test_nodehandle",
-                                  "test_slot_liveness"])
+                                  "test_slot_liveness", "test_combine_node"])
 def test_reference_unit_test_passes(name):
     exe = REF / name
     if not exe.exists():
