@@ -48,11 +48,13 @@ METRIC = ("SEM stiffness Melem/s and HBM GB/s (% of ~8 TB/s) at 1/2/4/8 B200 vs 
 MESH_PER_GPU = (64, 64, 64)
 NGLL = 5
 FALLBACK_HBM_GBS = 6650.0
-# DRAM bytes (read + write) per launch of the kernel, from one ncu capture of the
-# 32^3 case scaled by elements to the 64^3 launch
-# (profiles/sem3d_elastic_v3_32cube_full.md, sem3d_elastic_v5_32cube_full.md);
-# None where not captured.
-NCU_TRAFFIC_PER_LAUNCH = {"0": 276.76e6 * 8, "5": 275.32e6 * 8}
+# DRAM bytes (read + write) per launch of the kernel at 64^3: variant 5 from one
+# ncu capture of a single 64^3 launch (profiles/sem3d_elastic_v5_64cube_mix.md),
+# variant 0 from the 32^3 capture scaled by elements
+# (profiles/sem3d_elastic_v3_32cube_full.md); None where not captured.
+NCU_TRAFFIC_PER_LAUNCH = {"0": 276.76e6 * 8, "5": 2225873664.0 + 214804736.0}
+NCU_TRAFFIC_SOURCE = {"0": "ncu dram__bytes_read+write of the 32^3 case x8",
+                      "5": "ncu dram__bytes_read+write of one 64^3 launch"}
 DEFAULT_VARIANT = "5"
 KERNEL_NAMES = {"0": "sem3d_elastic_v3_kernel<5,8,2,true>",
                 "1": "sem3d_elastic_tma_kernel<float,5,8,2,true>",
@@ -167,6 +169,7 @@ def gpu_id_for(dev) -> str:
 def cpu_baseline(prob, seconds: float = 12.0, max_reps: int = 50):
     """OpenMP restatement of the reference host loop on all host threads."""
     from oracle import sem as osem
+    osem.set_num_threads(osem.host_cores())  # torchrun exports OMP_NUM_THREADS=1
     cpu = osem.AssembledCPU(prob.nelem, prob.ngll, prob.nglob, prob.ibool, prob.arrays,
                             prob.H, prob.Hw, prob.w, prob.dtype)
     f = [np.empty(prob.nglob, dtype=prob.dtype) for _ in range(3)]
@@ -186,14 +189,63 @@ def cpu_baseline(prob, seconds: float = 12.0, max_reps: int = 50):
                        "bench_sem3d_levelgraph.cpp:600-663 (Kokkos absent)")}
 
 
-def make_problem(rank: int, world: int):
-    """This rank's z-slab of the nex x ney x (world*nez) mesh: element layers
-    [rank*nez, (rank+1)*nez), generated as the exact slice of the whole
-    synthetic problem."""
+def make_problem(rank: int, world: int, strong: bool = False):
+    """This rank's z-slab, generated as the exact slice of the whole synthetic
+    problem: weak scaling cuts the nex x ney x (world*nez) mesh (nez layers per
+    rank), strong scaling the fixed nex x ney x nez mesh."""
     from tensoroperations_b200.slab import SlabPartition, slab_problem
     nex, ney, nez = MESH_PER_GPU
-    part = SlabPartition(nex, ney, nez * world, NGLL, world, rank)
+    part = SlabPartition(nex, ney, nez if strong else nez * world, NGLL, world, rank)
     return part, slab_problem(part, np.float32)
+
+
+def check_against_one_gpu(part, u, f, arrays, dev, stream):
+    """Relative L2 error of this rank's assembled f against the same operator
+    applied on ONE GPU (to_sem3d_apply, no partition, no exchange) to the
+    rank's element layers plus the neighbouring layer on each side -- the
+    layers that contribute to the rank's nodes.  The middle of the extended
+    inputs is the rank's own device data; the extra layers come from the same
+    seeded generator."""
+    import torch
+    from tensoroperations_b200 import abi
+    from tensoroperations_b200.slab import layer_problem
+    N, P, L, plane = part.ngll, part.ngll ** 3, part.layer, part.plane
+    lo = 1 if part.rank > 0 else 0
+    hi = 1 if part.rank < part.world - 1 else 0
+    za, zb = part.z0 - lo, part.z1 + hi
+    nel = (zb - za) * L
+    nglob = plane * ((zb - za) * (N - 1) + 1)
+    below = layer_problem(part.nex, part.ney, za, za + 1, N, np.float32) if lo else None
+    above = layer_problem(part.nex, part.ney, zb - 1, zb, N, np.float32) if hi else None
+    ext = {}
+    for name in abi.POINT_ARRAYS:
+        t = torch.empty(nel * P, dtype=torch.float32, device=dev)
+        t[lo * L * P:lo * L * P + part.nelem * P].copy_(arrays[name])
+        if lo:
+            t[:L * P].copy_(torch.from_numpy(below.arrays[name]))
+        if hi:
+            t[-L * P:].copy_(torch.from_numpy(above.arrays[name]))
+        ext[name] = t
+    off = lo * (N - 1) * plane  # the rank's first node inside the extended numbering
+    ue = []
+    for c in range(3):
+        t = torch.empty(nglob, dtype=torch.float32, device=dev)
+        t[off:off + part.nglob].copy_(u[c])
+        if lo:
+            t[:off].copy_(torch.from_numpy(below.u[c][:off]))
+        if hi:
+            t[off + part.nglob:].copy_(torch.from_numpy(above.u[c][plane:]))
+        ue.append(t)
+    ib = torch.from_numpy(abi.structured_ibool(part.nex, part.ney, zb - za, N).reshape(-1)).to(dev)
+    fe = [torch.empty(nglob, dtype=torch.float32, device=dev) for _ in range(3)]
+    _, w, H, Hw = abi.gll_operators(N)
+    plan = abi.Sem3dPlan(np.float32, N, nel, H, Hw, w, nglob=nglob, assembled=True)
+    plan.apply(plan.fields(ue, fe, ext, ib), stream=stream.cuda_stream)
+    torch.cuda.synchronize()
+    num = sum(float(torch.sum((f[c].double() - fe[c][off:off + part.nglob].double()) ** 2))
+              for c in range(3))
+    den = sum(float(torch.sum(fe[c][off:off + part.nglob].double() ** 2)) for c in range(3))
+    return (num / max(den, 1e-300)) ** 0.5
 
 
 def run_reference(args):
@@ -207,6 +259,7 @@ def run_reference(args):
         return 0
     from oracle import sem as osem
     from tensoroperations_b200.sem3d import structured_problem
+    osem.set_num_threads(osem.host_cores())  # torchrun exports OMP_NUM_THREADS=1
     nex, ney, nez = MESH_PER_GPU
     probe = structured_problem(nex, ney, max(1, nez // 16), ngll=NGLL, dtype=np.float32,
                                assembled=True)
@@ -552,6 +605,7 @@ def run_large(args):
                              "peak_source": peak_src, "algorithmic_bytes_per_step_all_ranks": alg_total},
                 "clocks": clocks.summary()}
         print(json.dumps(line), flush=True)
+    op.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -755,13 +809,13 @@ def run_local(args):
     return 0
 
 
-def config_dict(prob, world):
-    nex, ney, nez = prob.mesh
+def config_dict(prob, world, part):
     return {"workload": ("3D SEM isotropic elastic stiffness, NGLL=5, f32, structured "
-                         f"{nex}x{ney}x{nez * world} hexes, assembled through ibool"),
+                         f"{part.nex}x{part.ney}x{part.nez} hexes, assembled through ibool"),
             "nelem_per_gpu": prob.nelem, "nglob_per_gpu": prob.nglob, "ngll": prob.ngll,
             "mode": "assembled", "parallelism": f"z-slabs x{world}" if world > 1 else "single GPU",
-            "l2": "inputs larger than L2 (2.1 GB streamed per step per GPU), no flush"}
+            "l2": (f"inputs larger than L2 ({prob.plan().algorithmic_bytes() / 1e9:.2f} GB "
+                   "streamed per step per GPU vs 126 MB of L2), no flush")}
 
 
 def main():
@@ -801,6 +855,11 @@ def main():
                          "(x, y, z, unused; 1 GPU)")
     ap.add_argument("--mesh", type=int, nargs=3, default=[64, 64, 64],
                     metavar=("NEX", "NEY", "NEZ"), help="hexes per GPU (profiling runs)")
+    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
+                    help="weak: --mesh per GPU (nex x ney x N*nez hexes in all); strong: the "
+                         "--mesh hexes in all, split over the N GPUs")
+    ap.add_argument("--no-check", action="store_true",
+                    help="skip the post-run comparison of f with the one-GPU operator")
     args = ap.parse_args()
     MESH_PER_GPU = tuple(args.mesh)
     if args.variant is not None:
@@ -837,7 +896,8 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
     from tensoroperations_b200.slab import SlabOperator
-    part, prob = make_problem(rank, world)
+    strong = args.scaling == "strong"
+    part, prob = make_problem(rank, world, strong)
     u, f, arrays, ibool = to_device(prob, dev)
     stream = torch.cuda.Stream(device=dev)
     if args.layout == "interleaved":
@@ -889,7 +949,21 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     total_ms, kern_ms = float(t[0]), float(t[1])
     ms_per_step = total_ms / args.steps
-    value = prob.nelem * world / (ms_per_step * 1e-3) / 1e6
+    nelem_total = part.nex * part.ney * part.nez
+    value = nelem_total / (ms_per_step * 1e-3) / 1e6
+
+    # ---- correctness of the timed path: f of the last step against the one-GPU
+    # operator on the rank's layers plus their neighbours (max over ranks) ----
+    check = None
+    if not args.no_check and args.layout == "components":
+        rel = check_against_one_gpu(part, u, f, arrays, dev, stream)
+        t = torch.tensor([rel], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        check = {"rel_l2_max": float(t[0]), "tol": 1e-5,
+                 "reference": "the same operator on one GPU (to_sem3d_apply) over each rank's "
+                              "element layers plus one neighbouring layer per side; f of the "
+                              "last timed step, relative L2 over the rank's nodes, max over ranks"}
 
     # ---- end to end through the C ABI with pinned host buffers ----
     # Every step copies its u host -> device, applies the operator and copies
@@ -907,7 +981,7 @@ def main():
         u_set = [[torch.empty_like(x) for x in u] for _ in range(2)]
         f_set = [f, [torch.empty_like(x) for x in f]]
         ops = [SlabOperator(part, plan, plan.fields(u_set[k], f_set[k], arrays, ibool), f_set[k],
-                            dev) for k in range(2)]
+                            dev, comm=op.comm) for k in range(2)]
         s_in = torch.cuda.Stream(device=dev)
         s_out = torch.cuda.Stream(device=dev)
         ev_in = [torch.cuda.Event() for _ in range(2)]
@@ -960,34 +1034,44 @@ def main():
     peak, peak_src = measured_peak_hbm()
     achieved = alg / (kern_ms * 1e-3) / 1e9
     if rank == 0:
-        cpu = None if args.no_cpu_baseline or world > 1 else cpu_baseline(prob)
+        cpu = None if args.no_cpu_baseline else cpu_baseline(prob)
         line = {
             "metric": METRIC, "value": value, "unit": "Melem/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded splitmix64 fields on a structured mesh, GLL operators)",
-            "config": config_dict(prob, world),
+            "config": config_dict(prob, world, part),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
                          "traffic": (NCU_TRAFFIC_PER_LAUNCH.get(os.environ.get("TO_SEM3D_VARIANT", DEFAULT_VARIANT))
                                      if tuple(MESH_PER_GPU) == (64, 64, 64) else None),
-                         "traffic_source": "ncu dram__bytes_read+write of the 32^3 case x8",
+                         "traffic_source": NCU_TRAFFIC_SOURCE.get(
+                             os.environ.get("TO_SEM3D_VARIANT", DEFAULT_VARIANT)),
                          "peak_source": peak_src,
                          "algorithmic_bytes_per_launch": alg, "kernel_ms": kern_ms,
                          "kernel": KERNEL_NAMES.get(os.environ.get("TO_SEM3D_VARIANT", DEFAULT_VARIANT))},
             "cpu_baseline": cpu,
             "e2e": None if not e2e_steps else
-                   {"value": prob.nelem * world / (e2e_ms * 1e-3) / 1e6, "unit": "Melem/s",
+                   {"value": nelem_total / (e2e_ms * 1e-3) / 1e6, "unit": "Melem/s",
                     "h2d_bytes_per_step": bytes_uf, "d2h_bytes_per_step": bytes_uf,
                     "steps": e2e_steps},
+            "check": check,
             "gpu_launches": args.steps * op.kernel_launches(),
             "clocks": clocks.summary(),
             "gflops": plan.flops() / (kern_ms * 1e-3) / 1e9,
         }
         print(json.dumps(line), flush=True)
+    if e2e_steps:
+        for o in ops:
+            o.close()
+    op.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    if check is not None and not check["rel_l2_max"] <= check["tol"]:
+        print(f"bench: f differs from the one-GPU operator: rel L2 {check['rel_l2_max']:.3e}",
+              file=sys.stderr)
+        return 1
     return 0
 
 

@@ -215,6 +215,74 @@ int to_sem3d_halo_accumulate(int32_t dtype, void* const f[3], int64_t offset, in
                              const void* buf, void* stream);
 
 /* ---------------------------------------------------------------------- */
+/* Z-slab operator over NCCL (one rank per GPU)                            */
+/* ---------------------------------------------------------------------- */
+/*
+ * NCCL's communicator handle: the same typedef as nccl.h's, so a caller that
+ * includes nccl.h passes its own ncclComm_t unchanged.
+ */
+typedef struct ncclComm* ncclComm_t;
+
+#define TO_NCCL_UNIQUE_ID_BYTES 128
+
+/*
+ * One rank's z-slab of a structured mesh split in element layers across the
+ * ranks of `comm`.  The rank's plan covers its elements (whole layers of
+ * layer_elems elements, ordered layer by layer) and the nodes they touch;
+ * its first node plane is shared with rank `prev` and its last with rank
+ * `next` (-1: no neighbour on that side).  With the structured numbering each
+ * plane is one contiguous range of plane_nodes nodes per component: nodes
+ * [0, plane_nodes) and [nglob - plane_nodes, nglob).
+ */
+typedef struct to_slab {
+  int32_t prev;          /* rank below in `comm`, or -1                      */
+  int32_t next;          /* rank above in `comm`, or -1                      */
+  int64_t layer_elems;   /* elements per element layer (nex * ney)           */
+  int64_t plane_nodes;   /* nodes per node plane                             */
+  void* recv[2];         /* device buffers of 3 * plane_nodes values: the
+                            partial sums received from prev ([0]) / next ([1]) */
+  void* sync;            /* device buffer of to_slab_sync_bytes() bytes,
+                            16-byte aligned (batch tickets of the launches)  */
+  int32_t f_is_zero;     /* 0: the call zeroes f first (on compute_stream);
+                            1: the caller has already zeroed f in stream order
+                            (lets a caller time the operator without the fill) */
+} to_slab;
+
+/*
+ * f = K u on this rank's slab, with the shared planes summed across the
+ * neighbours, so every copy of a shared node holds the full sum and f equals
+ * the slice of the single-mesh result for this rank's nodes.
+ * The reference evaluates the whole mesh in one Kokkos launch on one device
+ * (include/TensorOperations/LevelGraph.hpp:576-628, bench_sem3d_levelgraph.cpp
+ * :247-351); this is the same operator partitioned over ranks.
+ *   compute_stream: zero f (unless slab->f_is_zero); the element layers next
+ *     to a neighbour (one launch); the interior layers (one launch, batches
+ *     handed out by a ticket counter); then it waits for the exchange.
+ *   comm_stream: after the boundary layers, one NCCL group sends this rank's
+ *     shared planes (read in place from f) and receives the neighbours' into
+ *     `recv`, then adds them into f's shared planes -- overlapped with the
+ *     interior, which touches no shared plane.  Give comm_stream a higher
+ *     priority than compute_stream (cudaStreamCreateWithPriority) so its
+ *     kernels are dispatched ahead of the interior's batches.
+ * Every rank must make the same sequence of calls.  Asynchronous; returns
+ * TO_ERR_COMM if NCCL cannot be loaded or a call fails.  Nothing is allocated.
+ */
+size_t to_slab_sync_bytes(void);
+int to_sem3d_elastic_mgpu(const to_sem3d_plan* plan, const to_sem3d_fields* fields,
+                          const to_slab* slab, ncclComm_t comm, void* compute_stream,
+                          void* comm_stream);
+
+/* NCCL set-up for callers without their own: rank 0 makes an id (bytes
+ * TO_NCCL_UNIQUE_ID_BYTES), every rank receives it by its own means and
+ * creates its communicator (the current device is the rank's GPU).  These and
+ * to_nccl_allreduce_sum_f64 (in-place sum of n doubles across the ranks, on
+ * `stream`) call the process's libnccl.so.2. */
+int to_nccl_unique_id(void* id);
+int to_nccl_comm_init(int32_t nranks, int32_t rank, const void* id, ncclComm_t* comm);
+int to_nccl_comm_destroy(ncclComm_t comm);
+int to_nccl_allreduce_sum_f64(double* x, int64_t n, ncclComm_t comm, void* stream);
+
+/* ---------------------------------------------------------------------- */
 /* Field reductions (repeated applications u <- K u / ||K u||)             */
 /* ---------------------------------------------------------------------- */
 /*
@@ -243,6 +311,10 @@ int to_sumsq3(int32_t dtype, const void* const x[3], int64_t first, int64_t n, d
  *     per GPU, kept until the process exits); nothing is allocated per call.
  *   - The first call on a device looks up that array's device address (with
  *     the device current); make that first call before any stream capture.
+ *     The address is remembered per device and CUDA context: a call in
+ *     another context (the caller's own, or a new primary context after
+ *     cudaDeviceReset) looks it up again, so it too should come before any
+ *     capture in that context.
  *   - n per component is limited to to_sumsq3_noalloc_max_n()
  *     (1,431,655,765); a larger n is rejected with TO_ERR_INVALID_ARGUMENT
  *     before anything is launched.

@@ -49,7 +49,9 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent
 OUT = HERE / "_ref"
-REF = Path(os.environ.get("TO_REFERENCE_ROOT", "/root/reference"))
+# The reference tree: TO_REFERENCE_ROOT, else a `reference` directory beside
+# this repository's checkout.  Nothing here runs where neither exists.
+REF = Path(os.environ.get("TO_REFERENCE_ROOT", str(ROOT.parent / "reference")))
 SEM3D = REF / "benchmarks" / "sem_stiffness_3d" / "bench_sem3d_levelgraph.cpp"
 SEM3D_DAG = REF / "benchmarks" / "sem_stiffness_3d" / "bench_sem_stiffness_3d.cpp"
 SEM2D = REF / "benchmarks" / "sem_stiffness" / "bench_sem_stiffness.cpp"

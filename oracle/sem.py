@@ -147,6 +147,23 @@ def num_threads() -> int:
     return fn()
 
 
+def host_cores() -> int:
+    """Cores this process may run on (its CPU affinity set)."""
+    import os
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def set_num_threads(n: int) -> int:
+    """Threads of the OpenMP CPU port (ignores OMP_NUM_THREADS); returns the count now in use."""
+    fn = _fast.oracle_set_num_threads
+    fn.restype = None
+    fn(C.c_int(int(n)))
+    return num_threads()
+
+
 def rel_l2(a, b) -> float:
     """Relative L2 error of a against reference b over all components."""
     a = np.concatenate([np.asarray(x, dtype=np.float64).ravel() for x in a])

@@ -295,6 +295,17 @@ int oracle_num_threads(void) {
 #endif
 }
 
+// Thread count of the OpenMP CPU port, set explicitly: launchers such as
+// torch.distributed.run export OMP_NUM_THREADS=1 to every rank, which would
+// otherwise time the port on one core.
+void oracle_set_num_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+#else
+  (void)n;
+#endif
+}
+
 void oracle_sem3d_local_f32(int64_t E, int N, const float* const* u, const float* const* m,
                             const float* H, const float* Hw, const float* w, float* const* f) {
   sem3d_local<float>(E, N, u, m, H, Hw, w, f);

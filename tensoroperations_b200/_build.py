@@ -70,7 +70,7 @@ def build_library(force: bool = False, verbose: bool = False) -> Path:
         objs.append(obj)
     tmp = LIB.with_suffix(".so.tmp")
     _run([NVCC] + ARCH + ["-shared", "-Xcompiler", "-fopenmp", "-o", str(tmp)] +
-         [str(o) for o in objs] + ["-lcudart"])
+         [str(o) for o in objs] + ["-lcudart", "-ldl"])
     os.replace(tmp, LIB)
     return LIB
 

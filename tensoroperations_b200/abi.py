@@ -85,6 +85,16 @@ class Acoustic2dFields(C.Structure):
         [(n, C.c_void_p) for n in ("xix", "xiz", "gamx", "gamz", "jac", "rho")]
 
 
+class Slab(C.Structure):
+    """to_slab: one rank's z-slab of a structured mesh (see to_sem3d_elastic_mgpu)."""
+    _fields_ = [("prev", C.c_int32), ("next", C.c_int32), ("layer_elems", C.c_int64),
+                ("plane_nodes", C.c_int64), ("recv", C.c_void_p * 2), ("sync", C.c_void_p),
+                ("f_is_zero", C.c_int32)]
+
+
+NCCL_UNIQUE_ID_BYTES = 128
+
+
 def _sig(name, restype, argtypes):
     fn = getattr(lib, name)
     fn.restype = restype
@@ -135,6 +145,13 @@ _sig("to_sem3d_plan_destroy", C.c_int, [C.c_void_p])
 _sig("to_sem3d_apply", C.c_int, [C.c_void_p, C.POINTER(Sem3dFields), C.c_int32, C.c_void_p])
 _sig("to_sem3d_algorithmic_bytes", C.c_double, [C.c_void_p])
 _sig("to_sem3d_flops", C.c_double, [C.c_void_p])
+_sig("to_slab_sync_bytes", C.c_size_t, [])
+_sig("to_sem3d_elastic_mgpu", C.c_int, [C.c_void_p, C.POINTER(Sem3dFields), C.POINTER(Slab),
+                                        C.c_void_p, C.c_void_p, C.c_void_p])
+_sig("to_nccl_unique_id", C.c_int, [C.c_void_p])
+_sig("to_nccl_comm_init", C.c_int, [C.c_int32, C.c_int32, C.c_void_p, C.POINTER(C.c_void_p)])
+_sig("to_nccl_comm_destroy", C.c_int, [C.c_void_p])
+_sig("to_nccl_allreduce_sum_f64", C.c_int, [C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p])
 
 
 def status_name(status: int) -> str:
@@ -291,6 +308,41 @@ def gemm_tf32x3(Mp: int, Np: int, Kp: int, Ahi, Alo, Bhi, Blo, Cout, stream: int
     """Cout[m][n] = sum_k (Ahi+Alo)[m][k] (Bhi+Blo)[n][k] on the tensor cores (K-major operands)."""
     check(lib.to_gemm_tf32x3(Mp, Np, Kp, _ptr(Ahi), _ptr(Alo), _ptr(Bhi), _ptr(Blo), _ptr(Cout),
                              stream), "to_gemm_tf32x3")
+
+
+def nccl_unique_id() -> bytes:
+    """A new NCCL unique id (rank 0 makes it; every rank passes it to nccl_comm_init)."""
+    buf = C.create_string_buffer(NCCL_UNIQUE_ID_BYTES)
+    check(lib.to_nccl_unique_id(buf), "to_nccl_unique_id")
+    return buf.raw
+
+
+def nccl_comm_init(nranks: int, rank: int, uid: bytes) -> int:
+    """This rank's NCCL communicator (the current CUDA device is its GPU), as an int handle."""
+    if len(uid) != NCCL_UNIQUE_ID_BYTES:
+        raise ValueError(f"NCCL unique id of {len(uid)} bytes")
+    h = C.c_void_p()
+    check(lib.to_nccl_comm_init(nranks, rank, C.c_char_p(uid), C.byref(h)), "to_nccl_comm_init")
+    return h.value
+
+
+def nccl_comm_destroy(comm: int):
+    check(lib.to_nccl_comm_destroy(comm), "to_nccl_comm_destroy")
+
+
+def nccl_allreduce_sum_f64(x, n: int, comm: int, stream: int = 0):
+    """x[:n] (device doubles) <- their sum over the communicator's ranks, in place."""
+    check(lib.to_nccl_allreduce_sum_f64(_ptr(x), n, comm, stream), "to_nccl_allreduce_sum_f64")
+
+
+def slab_sync_bytes() -> int:
+    return lib.to_slab_sync_bytes()
+
+
+def sem3d_elastic_mgpu(plan, fields, slab: Slab, comm: int, compute_stream: int, comm_stream: int):
+    """f = K u on a z-slab rank, shared planes summed across its neighbours (NCCL)."""
+    check(lib.to_sem3d_elastic_mgpu(plan._h, C.byref(fields), C.byref(slab), comm or None,
+                                    compute_stream, comm_stream), "to_sem3d_elastic_mgpu")
 
 
 def sm_count() -> int:

@@ -214,6 +214,42 @@ int launch_v5(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t
   return ok();
 }
 
+// The line-owner kernel over up to two element ranges with ticketed batches
+// (f32 NGLL 5, assembled; the z-slab operator's launches).
+int launch_v5_ranges(const to_sem3d_plan* plan, const to_sem3d_fields* fl, const int64_t first[2],
+                     const int64_t count[2], unsigned long long* ticket, cudaStream_t stream,
+                     int dev, int sms) {
+  constexpr int EB = 8, NT = EB * 25;
+  constexpr int OPT = kV5Packed | kV5Ranges;
+  const size_t smem = Sem3dV5Layout<EB, true>::kTotal;
+  auto kernel = sem3d_elastic_v5_kernel<EB, 3, true, false, OPT>;
+  static KernelSlot slot;
+  int nb = 0;
+  if (int st = configure(slot, kernel, dev, NT, smem, &nb)) return st;
+  Sem3dV5Args a{};
+  a.a = make_args<float, 5>(plan, fl);
+  a.a.prefetch = 1;
+  for (int i = 0; i < 5; ++i)
+    for (int p = 0; p < 5; ++p) {
+      a.H2[i][p] = make_float2(a.a.ops.H[i][p], a.a.ops.H[i][p]);
+      a.Hw2[i][p] = make_float2(a.a.ops.Hw[i][p], a.a.ops.Hw[i][p]);
+    }
+  long long total = 0;
+  for (int r = 0; r < 2; ++r) {
+    a.rg.first[r] = first[r];
+    a.rg.count[r] = count[r];
+    a.rg.nb[r] = (count[r] + EB - 1) / EB;
+    total += a.rg.nb[r];
+  }
+  a.rg.ticket = ticket;
+  if (total == 0) return ok();
+  const long long cap = static_cast<long long>(sms) * nb;
+  const int grid = static_cast<int>(total < cap ? total : cap);
+  kernel<<<grid, NT, smem, stream>>>(a);
+  TO_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
 // The line-owner kernel with geometry from global memory (NGLL 8).
 template <typename T, int N, int EB, int MINB, bool ASM>
 int launch_lo(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t stream,
@@ -357,6 +393,45 @@ int apply_dispatch(const to_sem3d_plan* plan, const to_sem3d_fields* fl, int acc
 }
 
 }  // namespace
+
+// Element ranges [first[r], first[r] + count[r]) of the plan's elements (r = 0, 1;
+// a zero count skips a range), scattered into f without zeroing it.  f32 NGLL 5
+// assembled plans with 16-byte aligned per-point arrays run as ONE launch of the
+// line-owner kernel with ticketed batches (`ticket` must be zero on `stream`
+// when the launch starts); other plans run to_sem3d_apply_elements per range.
+const to_sem3d_desc* sem3d_plan_desc(const to_sem3d_plan* plan) { return &plan->desc; }
+
+int sem3d_apply_ranges(const to_sem3d_plan* plan, const to_sem3d_fields* fl,
+                       const int64_t first[2], const int64_t count[2],
+                       unsigned long long* ticket, cudaStream_t stream) {
+  const to_sem3d_desc& d = plan->desc;
+  for (int r = 0; r < 2; ++r)
+    if (first[r] < 0 || count[r] < 0 || first[r] > d.nelem || count[r] > d.nelem - first[r])
+      return set_error(TO_ERR_INVALID_ARGUMENT, "sem3d ranges: range %d outside the plan", r);
+  // bulk copies need every batch's per-point rows 16-byte aligned: element
+  // e starts at e * 500 bytes, so each range must start at a multiple of 4
+  bool starts4 = true;
+  for (int r = 0; r < 2; ++r)
+    if (count[r] && first[r] % 4 != 0) starts4 = false;
+  const bool fast = d.dtype == TO_F32 && d.ngll == 5 && d.assembled && d.node_layout == 0 &&
+                    ticket != nullptr && sem3d_f32_variant() == 5 && starts4 &&
+                    staged_arrays_aligned(fl, true) && aligned(ticket, 8);
+  if (fast) {
+    int dev = 0;
+    const int sms = device_sm_count(&dev);
+    if (sms <= 0) return -sms;
+    for (int q = 0; q < 6; ++q)
+      if (!(q < 3 ? fl->u[q] : fl->f[q - 3]))
+        return set_error(TO_ERR_INVALID_ARGUMENT, "sem3d ranges: null u / f");
+    if (!fl->ibool) return set_error(TO_ERR_INVALID_ARGUMENT, "sem3d ranges: null ibool");
+    return launch_v5_ranges(plan, fl, first, count, ticket, stream, dev, sms);
+  }
+  for (int r = 0; r < 2; ++r)
+    if (count[r])
+      if (int st = to_sem3d_apply_elements(plan, fl, first[r], count[r], stream)) return st;
+  return ok();
+}
+
 }  // namespace to_b200
 
 using namespace to_b200;

@@ -66,6 +66,20 @@ struct Sem3dV5Layout {
   static constexpr size_t kTotal = kHeader + kStageBytes + kXBytes + kEBytes;
 };
 
+// Up to two element ranges processed in order, batch by batch, with the
+// batches handed out by a device-wide ticket counter instead of the static
+// grid stride (option kV5Ranges).  Batches never straddle a range: the last
+// batch of a range may hold fewer than EB elements.  The z-slab operator uses
+// it to scatter the two element layers next to its neighbours in one launch
+// and to run the interior so that CTAs which start late (their SM was busy
+// with the exchange) simply take fewer batches.
+struct Sem3dV5Ranges {
+  long long first[2];            // first element of each range
+  long long count[2];            // elements of each range (count[1] = 0: one range)
+  long long nb[2];               // batches of each range
+  unsigned long long* ticket;    // zeroed before the launch; one ticket per batch fetch
+};
+
 // The kernel's parameters: the common arguments plus the operators splatted
 // into f32 pairs, so a packed FMA takes both lanes' coefficient from one
 // 64-bit constant.
@@ -73,6 +87,7 @@ struct Sem3dV5Args {
   Sem3dArgs<float, 5> a;
   float2 H2[5][5];   // (H(i,p), H(i,p))
   float2 Hw2[5][5];  // (Hw(q,i), Hw(q,i))
+  Sem3dV5Ranges rg;  // used with kV5Ranges only
 };
 
 // Options of the line-owner kernel (OPT bit mask):
@@ -83,7 +98,8 @@ struct Sem3dV5Args {
 // (Waiting for the staged geometry just before B2 instead of before A, so the
 // bulk copies also overlap A and B1, measured 0.597 vs 0.592 ms and was
 // removed.)
-enum : int { kV5Packed = 2 };
+//   kV5Ranges    the element ranges of Sem3dV5Args::rg with ticketed batches.
+enum : int { kV5Packed = 2, kV5Ranges = 4 };
 
 // IL: assembled u and f interleaved per node (x, y, z, unused) -- one 128-bit
 // gather and one 128-bit atomicAdd per point instead of three of each.
@@ -92,6 +108,7 @@ __global__ void __launch_bounds__(EB * 25, MINB)
     sem3d_elastic_v5_kernel(const __grid_constant__ Sem3dV5Args args) {
   const Sem3dArgs<float, 5>& a = args.a;
   constexpr bool kPk = (OPT & kV5Packed) != 0;
+  constexpr bool kRg = (OPT & kV5Ranges) != 0;
   using LY = Sem3dV5Layout<EB, ASM>;
   constexpr int N = 5, NN = 25, P = 125, NT = LY::NT, EP = LY::EP;
   constexpr int SKX = LY::SKX, SKE = LY::SKE;
@@ -114,17 +131,32 @@ __global__ void __launch_bounds__(EB * 25, MINB)
   const int ly = ra * SKE + le * NN + rb;      // eta-line (k=a, i=b): + 5 j
   const int spt = le * P + ab;                  // staged point (k=0, j=a, i=b): + k*NN
 
-  const long long nbatch = (a.nelem + EB - 1) / EB;
+  const long long nbatch = kRg ? args.rg.nb[0] + args.rg.nb[1] : (a.nelem + EB - 1) / EB;
   const long long G = gridDim.x;
   const uint64_t pol_stream = l2_policy_evict_first();
 
-  auto batch_words = [&](long long bb) {
-    const long long e0 = bb * EB;
-    const long long ne = (a.nelem - e0 < EB) ? (a.nelem - e0) : EB;
-    return ne * P;
+  // batch bb -> its first element and element count
+  auto batch_first = [&](long long bb) -> long long {
+    if constexpr (kRg) {
+      return bb < args.rg.nb[0] ? args.rg.first[0] + bb * EB
+                                : args.rg.first[1] + (bb - args.rg.nb[0]) * EB;
+    } else {
+      return bb * EB;
+    }
   };
+  auto batch_elems = [&](long long bb) -> long long {
+    long long end;
+    if constexpr (kRg)
+      end = bb < args.rg.nb[0] ? args.rg.first[0] + args.rg.count[0]
+                               : args.rg.first[1] + args.rg.count[1];
+    else
+      end = a.nelem;
+    const long long e0 = batch_first(bb);
+    return (end - e0 < EB) ? (end - e0) : EB;
+  };
+  auto batch_words = [&](long long bb) { return batch_elems(bb) * P; };
   auto issue_stage = [&](long long bb) {
-    const long long e0 = bb * EB;
+    const long long e0 = batch_first(bb);
     const uint32_t bytes = static_cast<uint32_t>(batch_words(bb) * 4) & ~15u;
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     mbar_arrive_expect_tx(bar, kStaged * bytes);
@@ -139,8 +171,8 @@ __global__ void __launch_bounds__(EB * 25, MINB)
     }
   };
   auto prefetch_batch = [&](long long bb) {
-    if (bb >= nbatch) return;
-    const long long e0 = bb * EB;
+    if (kRg || bb >= nbatch) return;  // ticketed batches are not known ahead
+    const long long e0 = batch_first(bb);
     const uint32_t bytes = static_cast<uint32_t>(batch_words(bb) * 4);
 #pragma unroll
     for (int q = 0; q < kNumPointArrays; ++q) l2_prefetch_bulk(a.m[q] + e0 * P, bytes);
@@ -151,12 +183,15 @@ __global__ void __launch_bounds__(EB * 25, MINB)
       for (int c = 0; c < 3; ++c) l2_prefetch_bulk(a.u[c] + e0 * P, bytes);
   };
 
-  const long long b0 = blockIdx.x;
+  // ticketed batches: thread 0 draws the next ticket and leaves it here
+  long long* next_ticket = reinterpret_cast<long long*>(smem_raw + 64);
   if (tid == 0) {
     mbar_init(bar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    if (kRg) *next_ticket = static_cast<long long>(atomicAdd(args.rg.ticket, 1ull));
   }
   __syncthreads();
+  const long long b0 = kRg ? *next_ticket : static_cast<long long>(blockIdx.x);
   if (tid == 0 && b0 < nbatch) {
     issue_stage(b0);
     prefetch_batch(b0 + G);
@@ -171,8 +206,8 @@ __global__ void __launch_bounds__(EB * 25, MINB)
   int node_n[N];
   float uc_n[3][N];
   auto gather = [&](long long bb) {
-    const long long e = bb * EB + le;
-    const bool v = (bb < nbatch) && (e < a.nelem);
+    const bool v = (bb < nbatch) && (le < batch_elems(bb));
+    const long long e = v ? batch_first(bb) + le : 0;
     const long long base = e * P + ab;
 #pragma unroll
     for (int k = 0; k < N; ++k) node_n[k] = v ? __ldg(a.ibool + base + k * NN) : 0;
@@ -194,11 +229,11 @@ __global__ void __launch_bounds__(EB * 25, MINB)
   };
   if (ASM) gather(b0);
 
-  for (long long b = b0; b < nbatch; b += G) {
+  for (long long b = b0, bnext = 0; b < nbatch; b = bnext) {
     if (tid == 0) prefetch_batch(b + 2 * G);
-    const long long e0 = b * EB;
+    const long long e0 = batch_first(b);
     const long long e = e0 + le;
-    const bool valid = e < a.nelem;
+    const bool valid = le < batch_elems(b);
 
     int node[N];
 #pragma unroll
@@ -366,10 +401,12 @@ __global__ void __launch_bounds__(EB * 25, MINB)
         }
       }
     }
+    if (kRg && tid == 0) *next_ticket = static_cast<long long>(atomicAdd(args.rg.ticket, 1ull));
     __syncthreads();  // stage reads and flux writes of this batch are done
 
-    if (tid == 0 && b + G < nbatch) issue_stage(b + G);
-    if (ASM) gather(b + G);  // lands while the divergences run
+    bnext = kRg ? *next_ticket : b + G;
+    if (tid == 0 && bnext < nbatch) issue_stage(bnext);
+    if (ASM) gather(bnext);  // lands while the divergences run
 
     // ---- C1: line owners -> xi- and eta-divergences of their rows ----
 #pragma unroll

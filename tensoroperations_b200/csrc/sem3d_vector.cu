@@ -119,12 +119,33 @@ constexpr long long kNoAllocMaxPartials = 32768;
 constexpr long long kNoAllocMaxN = kNoAllocMaxPartials * kSumChunk / 3;
 static __device__ __align__(256) double g_noalloc_partials[kNoAllocMaxPartials];
 
-// Device address of g_noalloc_partials, looked up once per device.  In host
-// code the array's name only stands in for the symbol, so the address comes
-// from cudaGetSymbolAddress with that device current.
+// Device address of g_noalloc_partials, looked up once per device and CUDA
+// context.  In host code the array's name only stands in for the symbol, so
+// the address comes from cudaGetSymbolAddress with that device current.  The
+// cache remembers the context it was filled in (through the driver's
+// cuCtxGetCurrent, reached without linking the driver library): a caller that
+// makes its own context current, or a cudaDeviceReset that replaced the
+// primary context, gets a fresh lookup instead of a stale address.
+using CtxGetCurrentFn = int (*)(void**);
+
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      cudaGetLastError();
+      f = nullptr;
+    }
+    return reinterpret_cast<CtxGetCurrentFn>(f);
+  }();
+  return fn;
+}
+
 double* noalloc_partials(int* status) {
   static std::mutex mu;
   static double* ptr[64] = {};
+  static void* ctx_of[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) {
@@ -135,8 +156,15 @@ double* noalloc_partials(int* status) {
     *status = set_error(TO_ERR_UNSUPPORTED, "to_sumsq3_noalloc: device id %d >= 64", dev);
     return nullptr;
   }
+  auto current_ctx = [] {
+    void* c = nullptr;
+    if (CtxGetCurrentFn f = ctx_get_current())
+      if (f(&c) != 0) c = nullptr;
+    return c;
+  };
+  void* ctx = current_ctx();  // null until the runtime has made a context current
   std::lock_guard<std::mutex> lock(mu);
-  if (!ptr[dev]) {
+  if (!ptr[dev] || ctx == nullptr || ctx_of[dev] != ctx) {
     double* p = nullptr;
     e = cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_noalloc_partials);
     if (e != cudaSuccess) {
@@ -144,6 +172,7 @@ double* noalloc_partials(int* status) {
       return nullptr;
     }
     ptr[dev] = p;
+    ctx_of[dev] = ctx ? ctx : current_ctx();  // the lookup made the primary context current
   }
   *status = TO_OK;
   return ptr[dev];

@@ -92,7 +92,7 @@ struct Cuda {
   using scratch_memory_space = ScratchMemorySpace<Cuda>;
   using size_type = std::size_t;
   static constexpr const char* name() { return "Cuda"; }
-  void fence(const char* = nullptr) const { cudaDeviceSynchronize(); }
+  void fence(const char* = nullptr) const;
   static int concurrency() { return 148 * 2048; }
 };
 using DefaultExecutionSpace = Cuda;
@@ -140,6 +140,54 @@ inline bool& initialized_flag() {
 }
 }  // namespace Impl
 
+namespace Impl {
+// Status word of team scratch overflows: set by a team whose scratch requests
+// go past the size set on its policy (that team stops before it uses any of
+// the memory), read and cleared by fence() / finalize(), which then abort as
+// Kokkos::abort would.  CUDA builds keep it in mapped pinned host memory, so
+// a kernel writes it and the host reads it after synchronising; without
+// mapped memory the word is null and only the device message remains.
+inline int* scratch_status() {
+#ifdef KOKKOS_ENABLE_CUDA
+  static int* word = [] {
+    void* h = nullptr;
+    if (cudaHostAlloc(&h, sizeof(int), cudaHostAllocMapped) != cudaSuccess) {
+      cudaGetLastError();
+      return static_cast<int*>(nullptr);
+    }
+    *static_cast<volatile int*>(h) = 0;
+    return static_cast<int*>(h);
+  }();
+  return word;
+#else
+  static int word = 0;
+  return &word;
+#endif
+}
+
+// Returns and clears the status word (1 after an overflow, else 0).
+inline int take_scratch_status() {
+  int* w = scratch_status();
+  if (!w) return 0;
+  const int v = *static_cast<volatile int*>(w);
+  *static_cast<volatile int*>(w) = 0;
+  return v;
+}
+
+inline void check_scratch_status(const char* where) {
+  if (take_scratch_status()) {
+    std::fprintf(stderr,
+                 "Kokkos::%s: a team scratch request exceeded the size set on its policy; "
+                 "the team stopped before using the memory, so results are incomplete\n",
+                 where);
+    std::abort();
+  }
+}
+
+// Thrown on the host to stop a team whose scratch request overflowed.
+struct ScratchOverflow {};
+}  // namespace Impl
+
 inline void initialize() {
 #ifdef KOKKOS_ENABLE_CUDA
   cudaFree(nullptr);  // create the primary context
@@ -159,14 +207,23 @@ inline void finalize() {
   cudaDeviceSynchronize();
 #endif
   Impl::initialized_flag() = false;
+  Impl::check_scratch_status("finalize");
 }
 inline bool is_initialized() { return Impl::initialized_flag(); }
+
 
 inline void fence(const char* = nullptr) {
 #ifdef KOKKOS_ENABLE_CUDA
   cudaDeviceSynchronize();
 #endif
+  Impl::check_scratch_status("fence");
 }
+#ifdef KOKKOS_ENABLE_CUDA
+inline void Cuda::fence(const char*) const {
+  cudaDeviceSynchronize();
+  Impl::check_scratch_status("Cuda::fence");
+}
+#endif
 
 KOKKOS_INLINE_FUNCTION void abort(const char* msg) {
 #if defined(TO_KOKKOS_DEVICE_PASS)
@@ -200,20 +257,36 @@ struct ScratchMemorySpace {
   char* base_ = nullptr;
   std::size_t size_ = 0;
   mutable std::size_t used_ = 0;
+  int* status_ = nullptr;  // Impl::scratch_status(), or null
 
   ScratchMemorySpace() = default;
-  KOKKOS_INLINE_FUNCTION ScratchMemorySpace(void* base, std::size_t size)
-      : base_(static_cast<char*>(base)), size_(size), used_(0) {}
-  // A request past the size set on the policy is reported and answered with
-  // the start of the team's region when the request alone fits there (the
-  // results are then wrong, and the message says why), so that an
-  // under-sized policy never sends the kernel outside its shared memory; a
-  // request larger than the whole region gets a null pointer.
+  KOKKOS_INLINE_FUNCTION ScratchMemorySpace(void* base, std::size_t size, int* status = nullptr)
+      : base_(static_cast<char*>(base)), size_(size), used_(0), status_(status) {}
+  // A request past the size set on the policy never gets a pointer: the
+  // status word is set and the team stops right there -- on the device every
+  // thread of the team exits (they all make the same requests in the same
+  // order), on the host the team's functor is unwound -- so no view of an
+  // under-sized policy reaches outside the team's memory.  fence() then
+  // reports the overflow and aborts.
   KOKKOS_INLINE_FUNCTION void* get_shmem(std::size_t bytes) const {
     const std::size_t b = (bytes + align - 1) & ~(align - 1);
     if (used_ + b > size_) {
-      Kokkos::abort("team scratch request exceeds the size set on the policy");
-      return b <= size_ ? static_cast<void*>(base_) : nullptr;
+#if defined(TO_KOKKOS_DEVICE_PASS)
+      if (status_) {
+        *static_cast<volatile int*>(status_) = 1;
+        __threadfence_system();
+      }
+      if (threadIdx.x == 0)
+        printf("Kokkos: team scratch request of %llu bytes exceeds the %llu left of the size set "
+               "on the policy; team %d stops\n",
+               static_cast<unsigned long long>(b), static_cast<unsigned long long>(size_ - used_),
+               static_cast<int>(blockIdx.x));
+      asm volatile("exit;");
+      return nullptr;  // not reached
+#else
+      if (status_) *status_ = 1;
+      throw Impl::ScratchOverflow{};
+#endif
     }
     void* p = base_ + used_;
     used_ += b;
@@ -666,8 +739,10 @@ class TeamMember {
   scratch_memory_space scratch_;
 
  public:
-  KOKKOS_INLINE_FUNCTION TeamMember(int lr, int ls, int tr, int ts, void* smem, std::size_t bytes)
-      : league_rank_(lr), league_size_(ls), team_rank_(tr), team_size_(ts), scratch_(smem, bytes) {}
+  KOKKOS_INLINE_FUNCTION TeamMember(int lr, int ls, int tr, int ts, void* smem, std::size_t bytes,
+                                    int* status = nullptr)
+      : league_rank_(lr), league_size_(ls), team_rank_(tr), team_size_(ts),
+        scratch_(smem, bytes, status) {}
   KOKKOS_INLINE_FUNCTION int league_rank() const { return league_rank_; }
   KOKKOS_INLINE_FUNCTION int league_size() const { return league_size_; }
   KOKKOS_INLINE_FUNCTION int team_rank() const { return team_rank_; }
@@ -857,11 +932,11 @@ KOKKOS_INLINE_FUNCTION void parallel_for(const VectorRange<Member>& r, const F& 
 namespace Impl {
 #ifdef KOKKOS_ENABLE_CUDA
 template <class F>
-__global__ void team_kernel(const F f, std::size_t scratch_bytes) {
+__global__ void team_kernel(const F f, std::size_t scratch_bytes, int* status) {
   extern __shared__ __align__(16) unsigned char team_smem[];
   TeamMember<Cuda> m(static_cast<int>(blockIdx.x), static_cast<int>(gridDim.x),
                      static_cast<int>(threadIdx.x), static_cast<int>(blockDim.x), team_smem,
-                     scratch_bytes);
+                     scratch_bytes, status);
   f(m);
 }
 template <class F>
@@ -892,7 +967,7 @@ void parallel_for(const char* label, const TeamPolicy<Props...>& p, const F& f) 
     if (bytes > 48 * 1024)
       cudaFuncSetAttribute(Impl::team_kernel<F>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(bytes));
-    Impl::team_kernel<F><<<p.league_size(), team, bytes>>>(f, bytes);
+    Impl::team_kernel<F><<<p.league_size(), team, bytes>>>(f, bytes, Impl::scratch_status());
     Impl::check_launch(label);
   } else
 #endif
@@ -900,8 +975,12 @@ void parallel_for(const char* label, const TeamPolicy<Props...>& p, const F& f) 
     (void)label;
     void* buf = bytes ? std::malloc(bytes) : nullptr;
     for (int lr = 0; lr < p.league_size(); ++lr) {
-      TeamMember<Serial> m(lr, p.league_size(), 0, 1, buf, bytes);
-      f(m);
+      TeamMember<Serial> m(lr, p.league_size(), 0, 1, buf, bytes, Impl::scratch_status());
+      try {
+        f(m);
+      } catch (const Impl::ScratchOverflow&) {
+        // this team stopped at its over-sized request; the status word says so
+      }
     }
     std::free(buf);
   }

@@ -28,6 +28,7 @@
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 
 #include <TensorOperations/b200/Dag.hpp>
 
@@ -240,21 +241,36 @@ __global__ void tc_unpack_kernel(const Node node, const View out, const float* _
   }
 }
 
-// The packed operands and the GEMM output, one buffer kept for the process.
+// The packed operands and the GEMM output: one buffer per CUDA device, kept
+// for the process and grown when a larger contraction needs it.  The current
+// device picks the buffer, so a process that runs the frontend on several GPUs
+// never hands one device's memory to another.  Reuse is stream-ordered: the
+// frontend launches every evaluation on the default stream.
 inline float* tc_workspace(std::size_t floats) {
-  static float* ptr = nullptr;
-  static std::size_t cap = 0;
-  if (floats > cap) {
-    if (ptr) cudaFree(ptr);
-    ptr = nullptr;
-    cap = 0;
-    if (cudaMalloc(&ptr, floats * sizeof(float)) != cudaSuccess) {
+  struct Slot {
+    float* ptr = nullptr;
+    std::size_t cap = 0;
+  };
+  static std::mutex mu;
+  static Slot slots[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    throw LevelGraphError(TO_ERR_CUDA, "tensor-core contraction: no usable current device");
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  Slot& s = slots[dev];
+  if (floats > s.cap) {
+    if (s.ptr) cudaFree(s.ptr);
+    s.ptr = nullptr;
+    s.cap = 0;
+    if (cudaMalloc(&s.ptr, floats * sizeof(float)) != cudaSuccess) {
       cudaGetLastError();
       throw LevelGraphError(TO_ERR_CUDA, "tensor-core contraction: workspace allocation failed");
     }
-    cap = floats;
+    s.cap = floats;
   }
-  return ptr;
+  return s.ptr;
 }
 
 // Runs the contraction on the tensor cores when it is large enough; returns

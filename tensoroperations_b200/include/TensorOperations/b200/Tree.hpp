@@ -166,8 +166,11 @@ struct TreeLowering {
 
 // Device buffers for those intermediates: kept and reused across launches and
 // never handed back to the driver (a cudaFree would synchronise the device on
-// every execute).  Reuse is stream-ordered: the frontend launches every
-// evaluation on the default stream.
+// every execute).  A buffer belongs to the memory it was allocated in -- the
+// host, or one CUDA device -- and is only handed out again for that same
+// memory, so a process that runs the frontend on several GPUs never gets one
+// device's buffer on another.  Reuse is stream-ordered: the frontend launches
+// every evaluation on the default stream.
 class IntermediateLease {
  public:
   IntermediateLease() = default;
@@ -179,18 +182,30 @@ class IntermediateLease {
     pool()[idx_].busy = false;
   }
 
-  // The smallest idle buffer of at least `bytes` in that memory, else a new one.
+  // The smallest idle buffer of at least `bytes` in that memory (the host, or
+  // the current CUDA device), else a new one.
   void* acquire(std::size_t bytes, bool device) {
+    int where = kHost;
+#ifdef KOKKOS_ENABLE_CUDA
+    if (device) {
+      int dev = 0;
+      if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        throw LevelGraphError(TO_ERR_CUDA, "intermediate buffer: no usable current device");
+      }
+      where = dev;
+    }
+#endif
     std::lock_guard<std::mutex> lk(mu());
     auto& p = pool();
     std::size_t best = kNone;
     for (std::size_t i = 0; i < p.size(); ++i)
-      if (!p[i].busy && p[i].device == device && p[i].bytes >= bytes &&
+      if (!p[i].busy && p[i].where == where && p[i].bytes >= bytes &&
           (best == kNone || p[i].bytes < p[best].bytes))
         best = i;
     if (best == kNone) {
       p.push_back({Kokkos::Impl::alloc_bytes(bytes, device, "TensorOperations intermediate"), bytes,
-                   device, false});
+                   where, false});
       best = p.size() - 1;
     }
     p[best].busy = true;
@@ -202,10 +217,11 @@ class IntermediateLease {
   struct Buf {
     void* ptr;
     std::size_t bytes;
-    bool device;
+    int where;  // kHost, or the CUDA device ordinal
     bool busy;
   };
   static constexpr std::size_t kNone = ~std::size_t(0);
+  static constexpr int kHost = -1;
   static std::vector<Buf>& pool() {
     static auto* v = new std::vector<Buf>;  // intentionally never destroyed
     return *v;

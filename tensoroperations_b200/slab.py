@@ -6,13 +6,16 @@ planes it touches, [z0*(N-1), z1*(N-1)], are a contiguous range of global
 nodes.  Rank r owns layers [z0, z1) and all of their node planes; the first
 and last planes are duplicated on the neighbours (r-1 and r+1).
 
-One application on a rank (`SlabOperator.apply`):
-  1. zero f; scatter the element layers next to a neighbour (compute stream);
-  2. on a second stream: pack the shared planes, exchange them with the
-     neighbours (NCCL send/recv through torch.distributed), add the
-     neighbour's partial sums in;
-  3. meanwhile scatter the interior layers on the compute stream -- they touch
-     no shared plane, so 2 and 3 overlap;
+One application on a rank (`SlabOperator.apply`, one call of the C ABI's
+to_sem3d_elastic_mgpu on CUDA tensors):
+  1. zero f; scatter the element layers next to a neighbour (compute stream,
+     both layers in one launch);
+  2. on a second, high-priority stream: exchange the shared planes with the
+     neighbours (one NCCL group of send/recv, sent in place from f) and add
+     the neighbour's partial sums in;
+  3. meanwhile scatter the interior layers on the compute stream (batches
+     handed out by a ticket counter) -- they touch no shared plane, so 2 and
+     3 overlap;
   4. the compute stream waits for 2.
 Afterwards every copy of a shared node holds the full sum: f on each rank
 equals the slice of the single-mesh result for its nodes.
@@ -125,18 +128,29 @@ class SlabPartition:
         return bnd, interior
 
 
-def slab_problem(part: SlabPartition, dtype=np.float32, seed: int = DEFAULT_SEED) -> Sem3dProblem:
-    """This rank's slice of structured_problem(nex, ney, nez, ...) (same seeds)."""
+def layer_problem(nex: int, ney: int, za: int, zb: int, ngll: int, dtype=np.float32,
+                  seed: int = DEFAULT_SEED) -> Sem3dProblem:
+    """Element layers [za, zb) of structured_problem(nex, ney, nez, ...) for any
+    nez >= zb (same seeds): its elements, the nodes they touch, numbered from
+    the first of those nodes."""
     dt = np.dtype(dtype)
-    N = part.ngll
+    N = ngll
     P = N ** 3
     _, w, H, Hw = abi.gll_operators(N)
-    arrays = point_arrays(part.nelem * P, dt, seed, first=part.elem_first * P)
-    ibool = abi.structured_ibool(part.nex, part.ney, part.nez_local, N).reshape(-1)
-    u = [abi.synth_fill(part.nglob, dt, seed + c, "normal", 0.0, 1.0, first=part.node_first)
+    layer = nex * ney
+    plane = (nex * (N - 1) + 1) * (ney * (N - 1) + 1)
+    nel = (zb - za) * layer
+    nglob = plane * ((zb - za) * (N - 1) + 1)
+    arrays = point_arrays(nel * P, dt, seed, first=za * layer * P)
+    ibool = abi.structured_ibool(nex, ney, zb - za, N).reshape(-1)
+    u = [abi.synth_fill(nglob, dt, seed + c, "normal", 0.0, 1.0, first=za * (N - 1) * plane)
          for c in range(3)]
-    return Sem3dProblem(N, part.nelem, dt, H, Hw, w, arrays, u, ibool, part.nglob,
-                        (part.nex, part.ney, part.nez_local))
+    return Sem3dProblem(N, nel, dt, H, Hw, w, arrays, u, ibool, nglob, (nex, ney, zb - za))
+
+
+def slab_problem(part: SlabPartition, dtype=np.float32, seed: int = DEFAULT_SEED) -> Sem3dProblem:
+    """This rank's slice of structured_problem(nex, ney, nez, ...) (same seeds)."""
+    return layer_problem(part.nex, part.ney, part.z0, part.z1, part.ngll, dtype, seed)
 
 
 def slab_problem_device(part: SlabPartition, dtype, device, seed: int = DEFAULT_SEED,
@@ -212,15 +226,25 @@ class SlabOperator:
     """f = K u on this rank's slab, interface planes summed with the neighbours.
 
     `plan` is a Sem3dPlan over the rank's elements (assembled); `u`, `f`, the
-    per-point arrays and ibool are this rank's device tensors.  Exchange
-    buffers are allocated once here; apply() allocates nothing.
+    per-point arrays and ibool are this rank's device tensors.
+
+    On CUDA tensors (the product path) apply() is ONE call of the C ABI,
+    to_sem3d_elastic_mgpu: the boundary layers, then the interior with the
+    shared planes exchanged over NCCL on a high-priority second stream.  The
+    NCCL communicator is this library's own, created here from a unique id
+    that rank 0 broadcasts through `group` (torch.distributed); a single rank
+    needs none.  `native=False` keeps the step-by-step host orchestration
+    (torch.distributed send/recv of packed planes), which the gloo tests run
+    on the CPU.  Exchange buffers are allocated once here; apply() allocates
+    nothing.
 
     power_step(): one step of u <- K u / ||K u|| (the steady-state loop of the
     large configuration): apply, sum of squares over the nodes this rank owns
     (shared planes counted once, by the lower rank), all-reduce of that one
     double across ranks, and u rescaled on the device -- no host round trip."""
 
-    def __init__(self, part: SlabPartition, plan, fields, f, device, group=None, u=None):
+    def __init__(self, part: SlabPartition, plan, fields, f, device, group=None, u=None,
+                 native=None, comm=None):
         import torch
         self.part = part
         self.plan = plan
@@ -228,29 +252,89 @@ class SlabOperator:
         self.f = f
         self.group = group
         self.dtype = np.dtype(plan.dtype)
+        device = torch.device(device)
         tdt = torch.float32 if self.dtype == np.float32 else torch.float64
         n = 3 * part.plane
-        k = len(part.interfaces())
-        self.send = [torch.empty(n, dtype=tdt, device=device) for _ in range(k)]
-        self.recv = [torch.empty(n, dtype=tdt, device=device) for _ in range(k)]
-        self.comm = torch.cuda.Stream(device=device)
-        self.ev_bnd = torch.cuda.Event()
-        self.ev_done = torch.cuda.Event()
+        self.native = (device.type == "cuda") if native is None else bool(native)
         self.boundary, self.interior = part.element_ranges()
         self.u = u
         self.sumsq = torch.zeros(1, dtype=torch.float64, device=device)
         nown = part.nglob - part.owned_first
         self.sumsq_ws = torch.empty(max(1, abi.sumsq3_workspace_bytes(nown)), dtype=torch.uint8,
                                     device=device)
+        self.comm = None  # this library's NCCL communicator (native, world > 1)
+        self._own_comm = False
+        if self.native:
+            self.xstream = torch.cuda.Stream(device=device, priority=-100)  # highest priority
+            self.recv = [torch.empty(n, dtype=tdt, device=device) if side else None
+                         for side in (part.rank > 0, part.rank < part.world - 1)]
+            self.sync = torch.zeros(abi.slab_sync_bytes(), dtype=torch.uint8, device=device)
+            sl = abi.Slab()
+            sl.prev = part.rank - 1 if part.rank > 0 else -1
+            sl.next = part.rank + 1 if part.rank < part.world - 1 else -1
+            sl.layer_elems = part.layer
+            sl.plane_nodes = part.plane
+            sl.recv[0] = self.recv[0].data_ptr() if self.recv[0] is not None else None
+            sl.recv[1] = self.recv[1].data_ptr() if self.recv[1] is not None else None
+            sl.sync = self.sync.data_ptr()
+            self.slab = sl
+            if part.world > 1:
+                if comm:  # share another operator's communicator (same ranks)
+                    self.comm = comm
+                else:
+                    self.comm = self._make_comm(device)
+                    self._own_comm = True
+        else:
+            k = len(part.interfaces())
+            self.send = [torch.empty(n, dtype=tdt, device=device) for _ in range(k)]
+            self.recv = [torch.empty(n, dtype=tdt, device=device) for _ in range(k)]
+            self.xstream = torch.cuda.Stream(device=device) if device.type == "cuda" else None
+            self.ev_bnd = torch.cuda.Event() if device.type == "cuda" else None
+            self.ev_done = torch.cuda.Event() if device.type == "cuda" else None
+
+    def _make_comm(self, device) -> int:
+        """NCCL communicator over the slab's ranks: id from rank 0, broadcast via `group`."""
+        import torch
+        import torch.distributed as dist
+        uid = abi.nccl_unique_id() if self.part.rank == 0 else bytes(abi.NCCL_UNIQUE_ID_BYTES)
+        backend = dist.get_backend(self.group)
+        where = device if backend == "nccl" else "cpu"
+        t = torch.tensor(list(uid), dtype=torch.uint8, device=where)
+        dist.broadcast(t, src=dist.get_global_rank(self.group, 0) if self.group else 0,
+                       group=self.group)
+        with torch.cuda.device(device):
+            return abi.nccl_comm_init(self.part.world, self.part.rank, bytes(t.cpu().tolist()))
+
+    def close(self):
+        """Release the NCCL communicator this operator created (every rank calls
+        it, after the operators sharing it are done; idempotent)."""
+        if self.comm and self._own_comm:
+            abi.nccl_comm_destroy(self.comm)
+        self.comm = None
 
     def kernel_launches(self) -> int:
         """Launches of this library's kernels per apply (fills excluded)."""
         k = len(self.part.interfaces())
+        if self.native:
+            return (1 if self.boundary else 0) + (1 if self.interior[1] else 0) + k
         return len(self.boundary) + (1 if self.interior[1] else 0) + 2 * k
 
     def apply(self, stream, events=None):
         """One application on `stream`; `events` = (start, end) CUDA events are
-        recorded on it around this rank's operator kernels (fills excluded)."""
+        recorded on it around this rank's operator (f's zeroing excluded)."""
+        if self.native:
+            import torch
+            with torch.cuda.stream(stream):
+                for x in self.f:
+                    x.zero_()
+            self.slab.f_is_zero = 1
+            if events is not None:
+                events[0].record(stream)
+            abi.sem3d_elastic_mgpu(self.plan, self.fields, self.slab, self.comm,
+                                   stream.cuda_stream, self.xstream.cuda_stream)
+            if events is not None:
+                events[1].record(stream)
+            return
         import torch
         s = stream.cuda_stream
         for x in self.f:
@@ -262,15 +346,15 @@ class SlabOperator:
         faces = self.part.interfaces()
         if faces:
             self.ev_bnd.record(stream)
-            self.comm.wait_event(self.ev_bnd)
-            cs = self.comm.cuda_stream
-            with torch.cuda.stream(self.comm):
+            self.xstream.wait_event(self.ev_bnd)
+            cs = self.xstream.cuda_stream
+            with torch.cuda.stream(self.xstream):
                 for (_, off), buf in zip(faces, self.send):
                     abi.halo_pack(self.dtype, self.f, off, self.part.plane, buf, cs)
                 exchange_planes(self.part, self.send, self.recv, self.group)
                 for (_, off), buf in zip(faces, self.recv):
                     abi.halo_accumulate(self.dtype, self.f, off, self.part.plane, buf, cs)
-            self.ev_done.record(self.comm)
+            self.ev_done.record(self.xstream)
         first, count = self.interior
         if count:
             self.plan.apply_elements(self.fields, first, count, s)
@@ -289,6 +373,9 @@ class SlabOperator:
         first = self.part.owned_first
         abi.sumsq3(self.dtype, self.f, first, self.part.nglob - first, self.sumsq, self.sumsq_ws, s)
         if self.part.world > 1:
-            with torch.cuda.stream(stream):
-                dist.all_reduce(self.sumsq, group=self.group)
+            if self.comm:
+                abi.nccl_allreduce_sum_f64(self.sumsq, 1, self.comm, s)
+            else:
+                with torch.cuda.stream(stream):
+                    dist.all_reduce(self.sumsq, group=self.group)
         abi.scale3(self.dtype, self.u, self.f, self.part.nglob, self.sumsq, s)

@@ -5,6 +5,9 @@
 //     multilevel/team contraction benchmarks call it as a statement), and a
 //     team that carves exactly that many bytes of scratch views gets distinct,
 //     in-bounds regions;
+//   * a scratch request past the policy's size (larger than the whole region,
+//     or than what is left of it) hands out no pointer: the team stops and
+//     the status word that fence() checks is set;
 //   * LayoutLeft views: first index fastest, strides, mirrors keep the layout;
 //   * MDRangePolicy<Rank<N>> visits every point of the box exactly once.
 #include <Kokkos_Core.hpp>
@@ -45,6 +48,25 @@ int main() {
       ok[t.league_rank()] = in && a(2, 4) == 14.f;
     });
     for (int r = 0; r < 4; ++r) CHECK(ok[r] == 1);
+    CHECK(Kokkos::Impl::take_scratch_status() == 0);
+
+    // ---- a request past the policy's size never gets a pointer ----
+    // (one view larger than the whole region, and one that only overflows
+    // what is left): the team stops at the request, the status word is set,
+    // and no view of the team was handed memory outside its region
+    for (const std::size_t first : {std::size_t(0), bytes - 16}) {
+      std::vector<int> reached(3, 0);
+      Kokkos::TeamPolicy<> small(3, 1);
+      small.set_scratch_size(0, Kokkos::PerTeam(bytes));
+      Kokkos::parallel_for("overflow", small, [&](const Kokkos::TeamPolicy<>::member_type& t) {
+        if (first) Scratch2 pre(t.team_scratch(0), 1, first / 4);
+        Scratch2 big(t.team_scratch(0), 64, 64);  // 16 KiB > bytes
+        reached[t.league_rank()] = big.data() ? 1 : 2;
+      });
+      for (int r = 0; r < 3; ++r) CHECK(reached[r] == 0);
+      CHECK(Kokkos::Impl::take_scratch_status() == 1);
+      CHECK(Kokkos::Impl::take_scratch_status() == 0);
+    }
 
     // ---- LayoutLeft ----
     Kokkos::View<float**, Kokkos::LayoutLeft, Kokkos::HostSpace> L("L", 3, 4);

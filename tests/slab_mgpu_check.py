@@ -50,6 +50,7 @@ def main(out_dir, nex, ney, nez, seed, mode="apply", ngll=5):
         out = f if mode == "apply" else u
         np.save(os.path.join(out_dir, f"{'f' if mode == 'apply' else 'u'}{rank}.npy"),
                 np.stack([x.cpu().numpy() for x in out]))
+        op.close()
         dist.barrier()
     finally:
         dist.destroy_process_group()

@@ -12,7 +12,6 @@ reference (max error / max |ref| < 1e-4) and returns 0 only if all three pass.
 Profile mode (5 arguments) runs one launch of the DAG and the hand kernel at
 one TE and team size and prints both errors.
 """
-import os
 import re
 import subprocess
 from pathlib import Path
@@ -28,9 +27,6 @@ pytestmark = [pytest.mark.gpu,
 def _run(args, timeout=900):
     r = subprocess.run([str(BIN)] + [str(a) for a in args], capture_output=True, text=True,
                        timeout=timeout)
-    out_dir = Path(os.environ.get("GRAFT_REPO_ROOT", ".")) / "gpurun_out"
-    if out_dir.is_dir():
-        (out_dir / f"dropin_dag3d_{'_'.join(map(str, args))}.txt").write_text(r.stdout + r.stderr)
     return r
 
 

@@ -9,7 +9,6 @@ builds the SEM graph through the public API, static_asserts the plan (6 levels,
 hand-written Kokkos team kernel, and checks both against its own host
 reference (max error / max |ref| < 1e-4), returning 0 only if both pass.
 """
-import os
 import subprocess
 from pathlib import Path
 
@@ -24,9 +23,6 @@ pytestmark = [pytest.mark.gpu,
 def _run(args, timeout=900):
     r = subprocess.run([str(BIN)] + [str(a) for a in args], capture_output=True, text=True,
                        timeout=timeout)
-    out_dir = Path(os.environ.get("GRAFT_REPO_ROOT", ".")) / "gpurun_out"
-    if out_dir.is_dir():
-        (out_dir / f"dropin_sem3d_{'_'.join(map(str, args))}.txt").write_text(r.stdout + r.stderr)
     return r
 
 

@@ -1,0 +1,107 @@
+"""The z-slab operator's C ABI (to_sem3d_elastic_mgpu) on one GPU.
+
+* A slab with no neighbours (a single rank, no communicator): the interior is
+  the whole mesh, scattered by one launch of the line-owner kernel with
+  ticketed batches; f must equal the CPU oracle's assembled result.
+* A slab that is its own neighbour on both sides, through a one-rank NCCL
+  communicator: the two boundary layers run as one launch, the shared planes
+  go through the real NCCL group (send to self, receive into `recv`) and are
+  added back, so f must equal the oracle with its first and last node planes
+  doubled.  Meshes whose layers are a multiple of 4 elements take the bulk-copy
+  kernel (12 elements per layer: one full and one partial batch); 30 elements
+  per layer take the per-range fallback; one layer touching both planes is
+  scattered once.
+* Two applications in a row give the same f (tickets and f are reset).
+"""
+import numpy as np
+import pytest
+
+from oracle import sem as osem
+from tensoroperations_b200 import abi
+from tensoroperations_b200.sem3d import structured_problem, to_device
+
+pytestmark = pytest.mark.gpu
+N = 5
+TOL = 1e-5
+
+
+def _oracle(prob):
+    return osem.assembled(prob.nelem, N, prob.nglob, prob.ibool, prob.u, prob.arrays, prob.H,
+                          prob.Hw, prob.w, np.float32)
+
+
+def _slab(torch, nex, ney, prev, nxt, f_is_zero=0):
+    plane = (nex * (N - 1) + 1) * (ney * (N - 1) + 1)
+    recv = [torch.empty(3 * plane, device="cuda") for _ in range(2)]
+    sync = torch.zeros(abi.slab_sync_bytes(), dtype=torch.uint8, device="cuda")
+    sl = abi.Slab()
+    sl.prev, sl.next = prev, nxt
+    sl.layer_elems = nex * ney
+    sl.plane_nodes = plane
+    sl.recv[0], sl.recv[1] = recv[0].data_ptr(), recv[1].data_ptr()
+    sl.sync = sync.data_ptr()
+    sl.f_is_zero = f_is_zero
+    return sl, (recv, sync), plane
+
+
+@pytest.mark.parametrize("mesh", [(4, 3, 5), (6, 5, 3), (8, 2, 2)])
+def test_single_rank_without_neighbours(mesh):
+    import torch
+    prob = structured_problem(*mesh, ngll=N, dtype=np.float32, assembled=True, seed=31)
+    u, f, arrays, ibool = to_device(prob, "cuda")
+    plan = prob.plan()
+    sl, keep, _ = _slab(torch, mesh[0], mesh[1], -1, -1)
+    cs = torch.cuda.Stream()
+    xs = torch.cuda.Stream(priority=-100)
+    fl = plan.fields(u, f, arrays, ibool)
+    abi.sem3d_elastic_mgpu(plan, fl, sl, None, cs.cuda_stream, xs.cuda_stream)
+    torch.cuda.synchronize()
+    first = [x.cpu().numpy().copy() for x in f]
+    abi.sem3d_elastic_mgpu(plan, fl, sl, None, cs.cuda_stream, xs.cuda_stream)
+    torch.cuda.synchronize()
+    got = [x.cpu().numpy() for x in f]
+    ref = _oracle(prob)
+    assert osem.rel_l2(got, ref) < TOL
+    assert osem.rel_l2(first, got) < 1e-6  # atomics may reorder the sums: not bitwise
+
+
+@pytest.mark.parametrize("mesh", [(4, 3, 5), (6, 5, 3), (4, 4, 1)])
+def test_self_exchange_through_nccl(mesh):
+    import torch
+    nex, ney, nez = mesh
+    prob = structured_problem(nex, ney, nez, ngll=N, dtype=np.float32, assembled=True, seed=32)
+    u, f, arrays, ibool = to_device(prob, "cuda")
+    plan = prob.plan()
+    sl, keep, plane = _slab(torch, nex, ney, 0, 0)
+    cs = torch.cuda.Stream()
+    xs = torch.cuda.Stream(priority=-100)
+    comm = abi.nccl_comm_init(1, 0, abi.nccl_unique_id())
+    try:
+        fl = plan.fields(u, f, arrays, ibool)
+        for _ in range(2):
+            abi.sem3d_elastic_mgpu(plan, fl, sl, comm, cs.cuda_stream, xs.cuda_stream)
+        torch.cuda.synchronize()
+    finally:
+        abi.nccl_comm_destroy(comm)
+    got = [x.cpu().numpy() for x in f]
+    want = [x.copy() for x in _oracle(prob)]
+    for x in want:
+        x[:plane] *= 2
+        x[-plane:] *= 2
+    assert osem.rel_l2(got, want) < TOL
+
+
+def test_rejects_partial_layers_and_missing_communicator():
+    import torch
+    prob = structured_problem(4, 3, 2, ngll=N, dtype=np.float32, assembled=True, seed=33)
+    u, f, arrays, ibool = to_device(prob, "cuda")
+    plan = prob.plan()
+    fl = plan.fields(u, f, arrays, ibool)
+    sl, keep, _ = _slab(torch, 5, 3, -1, -1)  # 15-element layers do not divide 24 elements
+    with pytest.raises(abi.ToError) as e:
+        abi.sem3d_elastic_mgpu(plan, fl, sl, None, 0, 0)
+    assert e.value.status == abi.TO_ERR_INVALID_ARGUMENT
+    sl, keep, _ = _slab(torch, 4, 3, 0, -1)  # a neighbour but no communicator
+    with pytest.raises(abi.ToError) as e:
+        abi.sem3d_elastic_mgpu(plan, fl, sl, None, 0, 0)
+    assert e.value.status == abi.TO_ERR_INVALID_ARGUMENT

@@ -108,12 +108,15 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_nccl_ranks_reproduce_the_whole_mesh(tmp_path):
+@pytest.mark.parametrize("layer", [(6, 5), (4, 3)])
+def test_nccl_ranks_reproduce_the_whole_mesh(tmp_path, layer):
+    """30-element layers take the per-range fallback; 12-element layers the
+    bulk-copy kernel with ticketed batches (one full, one partial batch)."""
     torch = _torch()
     world = min(torch.cuda.device_count(), 4)
     if world < 2:
         pytest.skip("needs 2 GPUs")
-    nex, ney, nez, seed = 6, 5, 4 * world, 99
+    (nex, ney), nez, seed = layer, 4 * world, 99
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run",
            "--nnodes=1", f"--nproc-per-node={world}", "--master-addr", "127.0.0.1",
