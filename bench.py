@@ -5,7 +5,11 @@ Workload (the configuration the headline metric and the
 north star are quoted on): 3D SEM isotropic-elastic stiffness, NGLL=5, f32,
 structured 64x64x64 hexes per GPU (262,144 elements, 257^3 global nodes on one
 GPU), assembled through ibool (gather u, scatter-add f).  One step = one
-application f = K u: zero f, then the fused kernel.
+application f = K u: zero f, then the fused kernel.  On the device u and f are
+interleaved per node ([nglob][4] f32: one 16-byte gather and one 16-byte
+scatter-add per point; --layout components keeps one array per component);
+the end-to-end leg moves one array per component over PCIe and converts on
+the device inside its timed region.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
@@ -56,6 +60,16 @@ NCU_TRAFFIC_PER_LAUNCH = {"0": 276.76e6 * 8, "5": 2225873664.0 + 214804736.0}
 NCU_TRAFFIC_SOURCE = {"0": "ncu dram__bytes_read+write of the 32^3 case x8",
                       "5": "ncu dram__bytes_read+write of one 64^3 launch"}
 DEFAULT_VARIANT = "5"
+# The z-slab call's kernel (ticketed batches) per node layout, and its DRAM bytes per
+# 64^3 launch from one ncu capture (profiles/sem3d_elastic_v5_64cube_mix.md,
+# profiles/sem3d_elastic_v5_il_64cube.md).
+KERNEL_BY_LAYOUT = {"components": "sem3d_elastic_v5_kernel<8,3,true,false,6>",
+                    "interleaved": "sem3d_elastic_v5_kernel<8,3,true,true,6>"}
+NCU_TRAFFIC_BY_LAYOUT = {
+    "components": (2225873664.0 + 214804736.0,
+                   "ncu dram__bytes_read+write of one 64^3 launch (grid-stride build of the "
+                   "same kernel, identical data movement)"),
+    "interleaved": (None, None)}
 KERNEL_NAMES = {"0": "sem3d_elastic_v3_kernel<5,8,2,true>",
                 "1": "sem3d_elastic_tma_kernel<float,5,8,2,true>",
                 "2": "sem3d_elastic_kernel<float,5,32,true>",
@@ -850,9 +864,10 @@ def main():
     ap.add_argument("--large-mesh", type=int, default=128, help="hexes per side for --workload large")
     ap.add_argument("--gemm-size", type=int, default=4096, help="M = N = K for --workload gemm")
     ap.add_argument("--chain-extent", type=int, default=64)
-    ap.add_argument("--layout", default="components", choices=["components", "interleaved"],
-                    help="assembled u / f: one array per component, or interleaved per node "
-                         "(x, y, z, unused; 1 GPU)")
+    ap.add_argument("--layout", default="interleaved", choices=["components", "interleaved"],
+                    help="assembled u / f on the device: interleaved per node as (x, y, z, "
+                         "unused) (default; the host data stays one array per component), or "
+                         "one array per component")
     ap.add_argument("--mesh", type=int, nargs=3, default=[64, 64, 64],
                     metavar=("NEX", "NEY", "NEZ"), help="hexes per GPU (profiling runs)")
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
@@ -900,20 +915,21 @@ def main():
     part, prob = make_problem(rank, world, strong)
     u, f, arrays, ibool = to_device(prob, dev)
     stream = torch.cuda.Stream(device=dev)
-    if args.layout == "interleaved":
-        if world > 1:
-            raise SystemExit("--layout interleaved runs on one GPU")
-        u4 = torch.zeros((prob.nglob, 4), dtype=torch.float32, device=dev)
-        for c in range(3):
-            u4[:, c] = u[c]
+    il = args.layout == "interleaved"
+    if il:
+        # the device copy of u and f: one 16-byte node each ([nglob][4] f32)
+        u4 = torch.empty((prob.nglob, 4), dtype=torch.float32, device=dev)
+        abi.nodes_interleave(u, u4, prob.nglob, stream.cuda_stream)
         f4 = torch.zeros((prob.nglob, 4), dtype=torch.float32, device=dev)
-        u, f = [u4, None, None], [f4, None, None]
+        dev_u, dev_f = [u4, None, None], [f4, None, None]
         plan = abi.Sem3dPlan(np.float32, prob.ngll, prob.nelem, prob.H, prob.Hw, prob.w,
                              nglob=prob.nglob, assembled=True, interleaved=True)
+        f = None  # the planar f of to_device is not used
     else:
+        dev_u, dev_f = u, f
         plan = prob.plan()
-    fields = plan.fields(u, f, arrays, ibool)
-    op = SlabOperator(part, plan, fields, [x for x in f if x is not None], dev)
+    fields = plan.fields(dev_u, dev_f, arrays, ibool)
+    op = SlabOperator(part, plan, fields, [x for x in dev_f if x is not None], dev)
 
     clocks = ClockSampler(gpu_id_for(dev))
     clocks.__enter__()
@@ -955,8 +971,15 @@ def main():
     # ---- correctness of the timed path: f of the last step against the one-GPU
     # operator on the rank's layers plus their neighbours (max over ranks) ----
     check = None
-    if not args.no_check and args.layout == "components":
-        rel = check_against_one_gpu(part, u, f, arrays, dev, stream)
+    if not args.no_check:
+        if il:
+            f_planar = [torch.empty(prob.nglob, dtype=torch.float32, device=dev) for _ in range(3)]
+            abi.nodes_deinterleave(dev_f[0], f_planar, prob.nglob, stream.cuda_stream)
+            torch.cuda.synchronize()
+        else:
+            f_planar = dev_f
+        rel = check_against_one_gpu(part, u, f_planar, arrays, dev, stream)
+        del f_planar
         t = torch.tensor([rel], device=dev, dtype=torch.float64)
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -973,15 +996,28 @@ def main():
     # and kernels are done.
     # 24 steps (about 0.1 s) whatever --steps is, so the one pipeline fill and
     # drain inside the timed region weigh about 4 % of it
-    e2e_steps = 0 if (args.no_e2e or args.layout == "interleaved") else 24
+    e2e_steps = 0 if args.no_e2e else 24
     if e2e_steps:
+        # host data is one array per component; with interleaved nodes each step
+        # also runs the layout kernels (planar u -> [nglob][4] before the operator,
+        # [nglob][4] f -> planar after it) inside the timed region
         u_host = [torch.from_numpy(x).pin_memory() for x in prob.u]
         f_host = [[torch.empty(prob.nglob, dtype=torch.float32).pin_memory() for _ in range(3)]
                   for _ in range(2)]
-        u_set = [[torch.empty_like(x) for x in u] for _ in range(2)]
-        f_set = [f, [torch.empty_like(x) for x in f]]
-        ops = [SlabOperator(part, plan, plan.fields(u_set[k], f_set[k], arrays, ibool), f_set[k],
-                            dev, comm=op.comm) for k in range(2)]
+        u_set = [[torch.empty(prob.nglob, dtype=torch.float32, device=dev) for _ in range(3)]
+                 for _ in range(2)]
+        f_set = [[torch.empty(prob.nglob, dtype=torch.float32, device=dev) for _ in range(3)]
+                 for _ in range(2)]
+        if il:
+            u4_set = [torch.empty((prob.nglob, 4), dtype=torch.float32, device=dev)
+                      for _ in range(2)]
+            f4_set = [dev_f[0], torch.empty((prob.nglob, 4), dtype=torch.float32, device=dev)]
+            ops = [SlabOperator(part, plan, plan.fields([u4_set[k], None, None],
+                                                        [f4_set[k], None, None], arrays, ibool),
+                                [f4_set[k]], dev, comm=op.comm) for k in range(2)]
+        else:
+            ops = [SlabOperator(part, plan, plan.fields(u_set[k], f_set[k], arrays, ibool),
+                                f_set[k], dev, comm=op.comm) for k in range(2)]
         s_in = torch.cuda.Stream(device=dev)
         s_out = torch.cuda.Stream(device=dev)
         ev_in = [torch.cuda.Event() for _ in range(2)]
@@ -1000,7 +1036,11 @@ def main():
         if i >= 2:
             stream.wait_event(ev_out[k])  # step i-2's f_set[k] has left the device
         with torch.cuda.stream(stream):
+            if il:
+                abi.nodes_interleave(u_set[k], u4_set[k], prob.nglob, stream.cuda_stream)
             ops[k].apply(stream)
+            if il:
+                abi.nodes_deinterleave(f4_set[k], f_set[k], prob.nglob, stream.cuda_stream)
         ev_comp[k].record(stream)
         s_out.wait_event(ev_comp[k])
         with torch.cuda.stream(s_out):
@@ -1033,6 +1073,13 @@ def main():
     alg = plan.algorithmic_bytes()
     peak, peak_src = measured_peak_hbm()
     achieved = alg / (kern_ms * 1e-3) / 1e9
+    variant = os.environ.get("TO_SEM3D_VARIANT", DEFAULT_VARIANT)
+    if il or variant == DEFAULT_VARIANT:  # the ticketed line-owner launches of the slab call
+        kernel_name = KERNEL_BY_LAYOUT[args.layout]
+        traffic = NCU_TRAFFIC_BY_LAYOUT[args.layout]
+    else:
+        kernel_name = KERNEL_NAMES.get(variant)
+        traffic = (NCU_TRAFFIC_PER_LAUNCH.get(variant), NCU_TRAFFIC_SOURCE.get(variant))
     if rank == 0:
         cpu = None if args.no_cpu_baseline else cpu_baseline(prob)
         line = {
@@ -1040,16 +1087,17 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
             "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded splitmix64 fields on a structured mesh, GLL operators)",
-            "config": config_dict(prob, world, part),
+            "config": dict(config_dict(prob, world, part),
+                           node_layout=("interleaved [nglob][4] f32 on the device (host data one "
+                                        "array per component)" if il else
+                                        "one [nglob] array per component")),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
-                         "traffic": (NCU_TRAFFIC_PER_LAUNCH.get(os.environ.get("TO_SEM3D_VARIANT", DEFAULT_VARIANT))
-                                     if tuple(MESH_PER_GPU) == (64, 64, 64) else None),
-                         "traffic_source": NCU_TRAFFIC_SOURCE.get(
-                             os.environ.get("TO_SEM3D_VARIANT", DEFAULT_VARIANT)),
+                         "traffic": (traffic[0] if tuple(MESH_PER_GPU) == (64, 64, 64) else None),
+                         "traffic_source": traffic[1],
                          "peak_source": peak_src,
                          "algorithmic_bytes_per_launch": alg, "kernel_ms": kern_ms,
-                         "kernel": KERNEL_NAMES.get(os.environ.get("TO_SEM3D_VARIANT", DEFAULT_VARIANT))},
+                         "kernel": kernel_name},
             "cpu_baseline": cpu,
             "e2e": None if not e2e_steps else
                    {"value": nelem_total / (e2e_ms * 1e-3) / 1e6, "unit": "Melem/s",

@@ -214,6 +214,14 @@ int to_sem3d_halo_pack(int32_t dtype, void* const f[3], int64_t offset, int64_t 
 int to_sem3d_halo_accumulate(int32_t dtype, void* const f[3], int64_t offset, int64_t n,
                              const void* buf, void* stream);
 
+/* Node layouts (f32): out[i] = (x[0][i], x[1][i], x[2][i], 0) for i < n, the
+ * interleaved [nglob][4] layout of node_layout 1, from one array per component,
+ * and back (x[c][i] = in[i].c).  `x` is a HOST array of 3 device pointers;
+ * the interleaved array is 16-byte aligned.  One kernel on `stream`.  No
+ * counterpart in the reference (it has no assembled fields). */
+int to_nodes_interleave(const float* const x[3], float* out, int64_t n, void* stream);
+int to_nodes_deinterleave(const float* in, float* const x[3], int64_t n, void* stream);
+
 /* ---------------------------------------------------------------------- */
 /* Z-slab operator over NCCL (one rank per GPU)                            */
 /* ---------------------------------------------------------------------- */
@@ -239,8 +247,9 @@ typedef struct to_slab {
   int32_t next;          /* rank above in `comm`, or -1                      */
   int64_t layer_elems;   /* elements per element layer (nex * ney)           */
   int64_t plane_nodes;   /* nodes per node plane                             */
-  void* recv[2];         /* device buffers of 3 * plane_nodes values: the
-                            partial sums received from prev ([0]) / next ([1]) */
+  void* recv[2];         /* device buffers of 3 * plane_nodes values (4 *
+                            plane_nodes with interleaved nodes): the partial
+                            sums received from prev ([0]) / next ([1])       */
   void* sync;            /* device buffer of to_slab_sync_bytes() bytes,
                             16-byte aligned (batch tickets of the launches)  */
   int32_t f_is_zero;     /* 0: the call zeroes f first (on compute_stream);
@@ -251,7 +260,9 @@ typedef struct to_slab {
 /*
  * f = K u on this rank's slab, with the shared planes summed across the
  * neighbours, so every copy of a shared node holds the full sum and f equals
- * the slice of the single-mesh result for this rank's nodes.
+ * the slice of the single-mesh result for this rank's nodes.  Either node
+ * layout of the plan: one array per component, or interleaved (u[0], f[0]
+ * [nglob][4]; each shared plane then travels as one contiguous range).
  * The reference evaluates the whole mesh in one Kokkos launch on one device
  * (include/TensorOperations/LevelGraph.hpp:576-628, bench_sem3d_levelgraph.cpp
  * :247-351); this is the same operator partitioned over ranks.

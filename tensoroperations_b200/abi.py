@@ -145,6 +145,8 @@ _sig("to_sem3d_plan_destroy", C.c_int, [C.c_void_p])
 _sig("to_sem3d_apply", C.c_int, [C.c_void_p, C.POINTER(Sem3dFields), C.c_int32, C.c_void_p])
 _sig("to_sem3d_algorithmic_bytes", C.c_double, [C.c_void_p])
 _sig("to_sem3d_flops", C.c_double, [C.c_void_p])
+_sig("to_nodes_interleave", C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p])
+_sig("to_nodes_deinterleave", C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p])
 _sig("to_slab_sync_bytes", C.c_size_t, [])
 _sig("to_sem3d_elastic_mgpu", C.c_int, [C.c_void_p, C.POINTER(Sem3dFields), C.POINTER(Slab),
                                         C.c_void_p, C.c_void_p, C.c_void_p])
@@ -333,6 +335,16 @@ def nccl_comm_destroy(comm: int):
 def nccl_allreduce_sum_f64(x, n: int, comm: int, stream: int = 0):
     """x[:n] (device doubles) <- their sum over the communicator's ranks, in place."""
     check(lib.to_nccl_allreduce_sum_f64(_ptr(x), n, comm, stream), "to_nccl_allreduce_sum_f64")
+
+
+def nodes_interleave(x, out, n: int, stream: int = 0):
+    """out ([n][4] f32, device) = (x[0], x[1], x[2], 0) per node."""
+    check(lib.to_nodes_interleave(_fptrs(x), _ptr(out), n, stream), "to_nodes_interleave")
+
+
+def nodes_deinterleave(inp, x, n: int, stream: int = 0):
+    """x[c][i] = inp[i][c] for c < 3 (inp [n][4] f32, device)."""
+    check(lib.to_nodes_deinterleave(_ptr(inp), _fptrs(x), n, stream), "to_nodes_deinterleave")
 
 
 def slab_sync_bytes() -> int:

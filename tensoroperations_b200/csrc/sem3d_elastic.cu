@@ -215,14 +215,15 @@ int launch_v5(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t
 }
 
 // The line-owner kernel over up to two element ranges with ticketed batches
-// (f32 NGLL 5, assembled; the z-slab operator's launches).
+// (f32 NGLL 5, assembled, either node layout; the z-slab operator's launches).
+template <bool IL>
 int launch_v5_ranges(const to_sem3d_plan* plan, const to_sem3d_fields* fl, const int64_t first[2],
                      const int64_t count[2], unsigned long long* ticket, cudaStream_t stream,
                      int dev, int sms) {
   constexpr int EB = 8, NT = EB * 25;
   constexpr int OPT = kV5Packed | kV5Ranges;
   const size_t smem = Sem3dV5Layout<EB, true>::kTotal;
-  auto kernel = sem3d_elastic_v5_kernel<EB, 3, true, false, OPT>;
+  auto kernel = sem3d_elastic_v5_kernel<EB, 3, true, IL, OPT>;
   static KernelSlot slot;
   int nb = 0;
   if (int st = configure(slot, kernel, dev, NT, smem, &nb)) return st;
@@ -413,18 +414,28 @@ int sem3d_apply_ranges(const to_sem3d_plan* plan, const to_sem3d_fields* fl,
   bool starts4 = true;
   for (int r = 0; r < 2; ++r)
     if (count[r] && first[r] % 4 != 0) starts4 = false;
-  const bool fast = d.dtype == TO_F32 && d.ngll == 5 && d.assembled && d.node_layout == 0 &&
-                    ticket != nullptr && sem3d_f32_variant() == 5 && starts4 &&
+  const bool il = d.node_layout == 1;
+  const bool fast = d.dtype == TO_F32 && d.ngll == 5 && d.assembled && ticket != nullptr &&
+                    (il || sem3d_f32_variant() == 5) && starts4 &&
                     staged_arrays_aligned(fl, true) && aligned(ticket, 8);
+  if (il && !fast)
+    return set_error(TO_ERR_ALIGNMENT,
+                     "sem3d ranges: interleaved nodes need 16-byte aligned per-point arrays and "
+                     "ranges starting at multiples of 4 elements");
   if (fast) {
     int dev = 0;
     const int sms = device_sm_count(&dev);
     if (sms <= 0) return -sms;
-    for (int q = 0; q < 6; ++q)
+    for (int q = 0; q < 6; ++q) {
+      if (il && q % 3 != 0) continue;  // one interleaved array each
       if (!(q < 3 ? fl->u[q] : fl->f[q - 3]))
         return set_error(TO_ERR_INVALID_ARGUMENT, "sem3d ranges: null u / f");
+    }
+    if (il && (!aligned(fl->u[0], 16) || !aligned(fl->f[0], 16)))
+      return set_error(TO_ERR_ALIGNMENT, "sem3d ranges: interleaved u / f not 16-byte aligned");
     if (!fl->ibool) return set_error(TO_ERR_INVALID_ARGUMENT, "sem3d ranges: null ibool");
-    return launch_v5_ranges(plan, fl, first, count, ticket, stream, dev, sms);
+    if (il) return launch_v5_ranges<true>(plan, fl, first, count, ticket, stream, dev, sms);
+    return launch_v5_ranges<false>(plan, fl, first, count, ticket, stream, dev, sms);
   }
   for (int r = 0; r < 2; ++r)
     if (count[r])

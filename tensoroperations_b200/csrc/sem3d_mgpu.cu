@@ -46,6 +46,7 @@ int sem3d_apply_ranges(const to_sem3d_plan* plan, const to_sem3d_fields* fl,
                        const int64_t first[2], const int64_t count[2],
                        unsigned long long* ticket, cudaStream_t stream);
 const to_sem3d_desc* sem3d_plan_desc(const to_sem3d_plan* plan);
+int flat_accumulate(int32_t dtype, void* dst, const void* buf, int64_t n, cudaStream_t s);
 
 namespace {
 
@@ -188,9 +189,7 @@ int to_sem3d_elastic_mgpu(const to_sem3d_plan* plan, const to_sem3d_fields* fiel
   const to_sem3d_desc& d = *sem3d_plan_desc(plan);
   if (!d.assembled)
     return set_error(TO_ERR_INVALID_ARGUMENT, "to_sem3d_elastic_mgpu: the plan must be assembled");
-  if (d.node_layout != 0)
-    return set_error(TO_ERR_UNSUPPORTED,
-                     "to_sem3d_elastic_mgpu: one array per component (node_layout 0) only");
+  const bool il = d.node_layout == 1;  // u[0], f[0]: [nglob][4] floats
   const bool lo = slab->prev >= 0, hi = slab->next >= 0;
   const int64_t L = slab->layer_elems, plane = slab->plane_nodes;
   if (L <= 0 || plane <= 0 || d.nelem % L != 0 || d.nelem < L)
@@ -206,7 +205,7 @@ int to_sem3d_elastic_mgpu(const to_sem3d_plan* plan, const to_sem3d_fields* fiel
     return set_error(TO_ERR_INVALID_ARGUMENT, "to_sem3d_elastic_mgpu: null recv / sync buffer");
   if (!aligned(slab->sync, 16))
     return set_error(TO_ERR_ALIGNMENT, "to_sem3d_elastic_mgpu: sync buffer not 16-byte aligned");
-  for (int c = 0; c < 3; ++c)
+  for (int c = 0; c < (il ? 1 : 3); ++c)
     if (!fields->f[c] || !fields->u[c])
       return set_error(TO_ERR_INVALID_ARGUMENT, "to_sem3d_elastic_mgpu: null u / f component");
   cudaStream_t cs = static_cast<cudaStream_t>(compute_stream);
@@ -226,8 +225,12 @@ int to_sem3d_elastic_mgpu(const to_sem3d_plan* plan, const to_sem3d_fields* fiel
   }
 
   // ---- compute stream: zero f and the tickets, boundary layers ----
-  if (!slab->f_is_zero)
-    for (int c = 0; c < 3; ++c) TO_CUDA_TRY(cudaMemsetAsync(fields->f[c], 0, vb * d.nglob, cs));
+  if (!slab->f_is_zero) {
+    if (il)
+      TO_CUDA_TRY(cudaMemsetAsync(fields->f[0], 0, 4 * vb * d.nglob, cs));
+    else
+      for (int c = 0; c < 3; ++c) TO_CUDA_TRY(cudaMemsetAsync(fields->f[c], 0, vb * d.nglob, cs));
+  }
   auto* tickets = static_cast<unsigned long long*>(slab->sync);
   TO_CUDA_TRY(cudaMemsetAsync(tickets, 0, 2 * sizeof(unsigned long long), cs));
   int64_t bfirst[2] = {0, 0}, bcount[2] = {0, 0};
@@ -252,6 +255,17 @@ int to_sem3d_elastic_mgpu(const to_sem3d_plan* plan, const to_sem3d_fields* fiel
     TO_NCCL_TRY(api, api->GroupStart());
     for (int side = 0; side < 2; ++side) {
       if (peer[side] < 0) continue;
+      if (il) {  // the plane is 4 * plane consecutive values of f[0]
+        const char* src = static_cast<const char*>(fields->f[0]) + 4 * vb * off[side];
+        ncclResult_t r = api->Send(src, static_cast<size_t>(4 * plane), nt, peer[side], comm, xs);
+        if (r == ncclSuccess)
+          r = api->Recv(slab->recv[side], static_cast<size_t>(4 * plane), nt, peer[side], comm, xs);
+        if (r != ncclSuccess) {
+          api->GroupEnd();
+          return nccl_fail(api, r, "to_sem3d_elastic_mgpu: ncclSend / ncclRecv");
+        }
+        continue;
+      }
       for (int c = 0; c < 3; ++c) {
         const char* src = static_cast<const char*>(fields->f[c]) + vb * off[side];
         char* dst = static_cast<char*>(slab->recv[side]) + vb * c * plane;
@@ -267,9 +281,13 @@ int to_sem3d_elastic_mgpu(const to_sem3d_plan* plan, const to_sem3d_fields* fiel
     TO_NCCL_TRY(api, api->GroupEnd());
     for (int side = 0; side < 2; ++side) {
       if (peer[side] < 0) continue;
-      if (int st = to_sem3d_halo_accumulate(d.dtype, fields->f, off[side], plane,
-                                            slab->recv[side], xs))
-        return st;
+      int st;
+      if (il)
+        st = flat_accumulate(d.dtype, static_cast<char*>(fields->f[0]) + 4 * vb * off[side],
+                             slab->recv[side], 4 * plane, xs);
+      else
+        st = to_sem3d_halo_accumulate(d.dtype, fields->f, off[side], plane, slab->recv[side], xs);
+      if (st) return st;
     }
     TO_CUDA_TRY(cudaEventRecord(ev->done, xs));
   }

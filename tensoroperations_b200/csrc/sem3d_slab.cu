@@ -38,6 +38,35 @@ __global__ void halo_accumulate_kernel(Planes3<T> dst, int64_t offset, int64_t n
   }
 }
 
+template <typename T>
+__global__ void flat_accumulate_kernel(T* __restrict__ dst, const T* __restrict__ buf, int64_t n) {
+  for (int64_t t = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; t < n;
+       t += int64_t(gridDim.x) * blockDim.x)
+    dst[t] += buf[t];
+}
+
+// u4[i] = (u0[i], u1[i], u2[i], 0) and back: the interleaved node layout
+// (one 16-byte node per point gather / scatter) from and to one array per
+// component.
+__global__ void interleave_kernel(float4* __restrict__ out, const float* __restrict__ x,
+                                  const float* __restrict__ y, const float* __restrict__ z,
+                                  int64_t n) {
+  for (int64_t t = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; t < n;
+       t += int64_t(gridDim.x) * blockDim.x)
+    out[t] = make_float4(x[t], y[t], z[t], 0.f);
+}
+
+__global__ void deinterleave_kernel(float* __restrict__ x, float* __restrict__ y,
+                                    float* __restrict__ z, const float4* __restrict__ in, int64_t n) {
+  for (int64_t t = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; t < n;
+       t += int64_t(gridDim.x) * blockDim.x) {
+    const float4 v = in[t];
+    x[t] = v.x;
+    y[t] = v.y;
+    z[t] = v.z;
+  }
+}
+
 int grid_for(int64_t total) {
   int dev = 0;
   const int sms = device_sm_count(&dev);
@@ -77,6 +106,23 @@ int halo_common(int32_t dtype, void* const f[3], int64_t offset, int64_t n, cons
 }
 
 }  // namespace
+
+// dst[t] += buf[t] for t < n (one contiguous range; the interleaved layout's
+// shared plane is 4 * plane_nodes consecutive values).
+int flat_accumulate(int32_t dtype, void* dst, const void* buf, int64_t n, cudaStream_t s) {
+  if (!dst || !buf || n < 0) return set_error(TO_ERR_INVALID_ARGUMENT, "flat accumulate: bad argument");
+  if (n == 0) return ok();
+  const int grid = grid_for(n);
+  if (dtype == TO_F32)
+    flat_accumulate_kernel<float><<<grid, 256, 0, s>>>(static_cast<float*>(dst),
+                                                       static_cast<const float*>(buf), n);
+  else
+    flat_accumulate_kernel<double><<<grid, 256, 0, s>>>(static_cast<double*>(dst),
+                                                        static_cast<const double*>(buf), n);
+  TO_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
 }  // namespace to_b200
 
 using namespace to_b200;
@@ -91,6 +137,28 @@ int to_sem3d_halo_pack(int32_t dtype, void* const f[3], int64_t offset, int64_t 
 int to_sem3d_halo_accumulate(int32_t dtype, void* const f[3], int64_t offset, int64_t n,
                              const void* buf, void* stream) {
   return halo_common(dtype, f, offset, n, buf, stream, false, "to_sem3d_halo_accumulate");
+}
+
+int to_nodes_interleave(const float* const x[3], float* out, int64_t n, void* stream) {
+  if (!x || !x[0] || !x[1] || !x[2] || !out || n < 0)
+    return set_error(TO_ERR_INVALID_ARGUMENT, "to_nodes_interleave: bad argument");
+  if (!aligned(out, 16)) return set_error(TO_ERR_ALIGNMENT, "to_nodes_interleave: out not 16-byte aligned");
+  if (n == 0) return ok();
+  interleave_kernel<<<grid_for(n), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<float4*>(out), x[0], x[1], x[2], n);
+  TO_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
+int to_nodes_deinterleave(const float* in, float* const x[3], int64_t n, void* stream) {
+  if (!x || !x[0] || !x[1] || !x[2] || !in || n < 0)
+    return set_error(TO_ERR_INVALID_ARGUMENT, "to_nodes_deinterleave: bad argument");
+  if (!aligned(in, 16)) return set_error(TO_ERR_ALIGNMENT, "to_nodes_deinterleave: in not 16-byte aligned");
+  if (n == 0) return ok();
+  deinterleave_kernel<<<grid_for(n), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      x[0], x[1], x[2], reinterpret_cast<const float4*>(in), n);
+  TO_CUDA_TRY(cudaGetLastError());
+  return ok();
 }
 
 }  // extern "C"

@@ -21,6 +21,7 @@
 #include <TensorOperations/b200/Plan.hpp>
 #if defined(__CUDACC__)
 #include <TensorOperations/b200/LevelKernel.cuh>
+#include <TensorOperations/b200/SemFused.cuh>
 #endif
 
 namespace TensorOperations {
@@ -235,8 +236,20 @@ struct LevelGraph {
       grid.ntiles[g] = static_cast<int>((gext[g] + gtile[g] - 1) / gtile[g]);
     using Views = DeviceTuple<ViewTs...>;
     const Views vt(views...);
-    auto kernel = b200::level_graph_kernel<ValueType, LabelTilesT, LevelsT, Views, Roots...>;
     if (ln.league == 0) return 0;
+    // the spectral-element stiffness shape: one fused line-owner kernel that
+    // calls this graph's combine functors (SemFused.cuh)
+    if constexpr (GS::rank == 1) {
+      cudaError_t fe = cudaSuccess;
+      if (b200::sem_fused_launch<ValueType, LabelTilesT, LevelsT, Views, Roots...>(levels, vt,
+                                                                                  gext[0], &fe)) {
+        if (fe != cudaSuccess)
+          throw LevelGraphError(TO_ERR_CUDA,
+                                std::string("level graph fused launch: ") + cudaGetErrorString(fe));
+        return static_cast<int>(ln.league);
+      }
+    }
+    auto kernel = b200::level_graph_kernel<ValueType, LabelTilesT, LevelsT, Views, Roots...>;
     if (ln.scratch_bytes > 48 * 1024) {
       cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            static_cast<int>(ln.scratch_bytes));

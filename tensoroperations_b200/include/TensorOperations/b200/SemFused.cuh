@@ -1,0 +1,611 @@
+// SemFused.cuh -- a LevelGraph with the spectral-element stiffness shape runs as
+// ONE fused line-owner kernel that calls the user's own combine functors,
+// instead of the generic level evaluator (LevelKernel.cuh).
+//
+// The shape (the reference's levelgraph_sem3d, benchmarks/sem_stiffness_3d/
+// bench_sem3d_levelgraph.cpp:247-351, built through include/TensorOperations/
+// LevelGraph.hpp:685-691):
+//   level 0  two stages of N x N operators (any labels, whole extents N)
+//   level 1  three stages of rank-4 fields u_c with labels F = (fe, f1, f2, f3):
+//            fe the one blocked label, f1..f3 whole labels of extent N
+//   level 2  nine contractions G_m = sum_p Op(x_a, p) u_c(x with x_a -> p): one
+//            operator slot, one field slot renamed along one axis a of f1..f3;
+//            output declared F.  Every (field, axis) pair exactly once.
+//   level 3  one combine of the nine gradients (operands labelled F) with nine
+//            outputs, called at the GLOBAL coordinate (e, x1, x2, x3)
+//   level 4  nine contractions of the operator slots with the combine's
+//            outputs, each output read once, three along each axis
+//   level 5  three combines of three level-4 slots each, the graph's roots
+// Everything else keeps the generic evaluator.  The recognition is a
+// compile-time walk of the level types (SemShape<...>::tables); the launch
+// selects the fused kernel when `ok` holds, the value type is float or double,
+// the whole labels are exactly N = 5 long and the operator views are dense
+// row-major N x N.  TO_LEVELGRAPH_FUSED=0 in the environment keeps the generic
+// evaluator (the tests compare the two).
+//
+// Kernel: a CTA takes batches of 8 elements with 200 threads; thread
+// (le, a, b) is at once the column owner of element le's points (k = 0..4,
+// j = a, i = b), the owner of the x3-line (k = b, j = a) and of the x2-line
+// (k = a, i = b), as in the library's line-owner kernel (csrc/
+// sem3d_elastic_v5.cuh): contractions along x1 run in registers, along x3 and
+// x2 through two shared buffers with conflict-free strides, values updated in
+// place.  The operators sit in constant memory (copied from the level-0 views
+// before the launch), so every coefficient is an immediate operand.  The
+// combine functors are inlined at each point with its global coordinate; the
+// fields they read themselves (the reference's metric and material arrays)
+// come straight from global memory with coalesced loads.
+#pragma once
+
+#include <cstdint>
+#include <cstdlib>
+#include <cstring>
+
+#include <TensorOperations/b200/Plan.hpp>
+
+namespace TensorOperations {
+namespace b200 {
+
+// ---- the recognised shape ----------------------------------------------------
+
+struct SemTables {
+  bool ok = false;
+  int why = 0;  // first failed check (0: none), for diagnosing a graph that is not recognised
+  // gradient member m (level 2): field index, axis (1..3 in F), operator slot
+  // (0/1 of level 0), transposed (Op(o,p) = S[p][o] instead of S[o][p])
+  int g_comp[9] = {}, g_axis[9] = {}, g_op[9] = {}, g_tr[9] = {};
+  int g_of[3][4] = {};  // [field][axis] -> gradient member
+  int c_in[9] = {};     // combine operand q -> gradient member
+  // divergence member m (level 4): combine output read, axis, operator, transposed,
+  // and its position among the members of its axis (0..2)
+  int d_src[9] = {}, d_axis[9] = {}, d_op[9] = {}, d_tr[9] = {}, d_slot[9] = {};
+  int d_of_src[9] = {};  // combine output o -> divergence member
+  int d_at[4][3] = {};   // [axis][slot] -> divergence member
+  int s_in[3][3] = {};   // final combine r, operand q -> divergence member
+  int s_root[3] = {};    // final combine r -> position of its slot in Roots
+};
+
+template <class A>
+constexpr bool identity_perm() {
+  constexpr auto p = to_array_int<typename A::decl_to_storage_seq>();
+  for (std::size_t d = 0; d < p.size(); ++d)
+    if (p[d] != static_cast<int>(d)) return false;
+  return true;
+}
+
+template <class Seq, std::size_t NF>
+constexpr bool labels_equal(const std::array<int32_t, NF>& f) {
+  constexpr auto s = to_array<Seq>();
+  if (s.size() != NF) return false;
+  for (std::size_t d = 0; d < NF; ++d)
+    if (s[d] != f[d]) return false;
+  return true;
+}
+
+// One contraction member of level 2 or 4: operator slot x field slot along one
+// axis of the frame F, output declared F.
+struct SemContraction {
+  bool ok = false;
+  std::size_t a_slot = 0, b_slot = 0;
+  int axis = 0, tr = 0;
+};
+
+template <class C>
+constexpr SemContraction sem_contraction(const std::array<int32_t, 4>& F) {
+  SemContraction r{};
+  if constexpr (member_traits<C>::kind != 1) {
+    return r;
+  } else if constexpr (C::NumContracted != 1 ||
+                       !std::is_same_v<typename C::hook_type, NoHook>) {
+    return r;
+  } else {
+    using A = typename C::node_a_type;
+    using B = typename C::node_b_type;
+    if constexpr (A::Rank != 2 || B::Rank != 4 || C::Rank != 4) {
+      return r;
+    } else {
+      constexpr auto al = to_array<typename A::modes_seq>();
+      constexpr auto bl = to_array<typename B::modes_seq>();
+      constexpr auto out = to_array<typename C::decl_seq>();
+      const int32_t c = C::contracted[0];
+      const int pa = index_of(al, c);
+      const int ax = index_of(bl, c);
+      if (pa < 0 || ax < 1) return r;
+      const int32_t fa = al[1 - pa];
+      for (int q = 0; q < 4; ++q) {
+        if (q == ax) {
+          if (out[q] != fa) return r;
+        } else if (out[q] != bl[q]) {
+          return r;
+        }
+        if (out[q] != F[q]) return r;  // the output keeps the frame's labels
+      }
+      if (!identity_perm<A>() || !identity_perm<B>()) return r;
+      r.a_slot = A::SlotIdx;
+      r.b_slot = B::SlotIdx;
+      r.axis = ax;
+      r.tr = pa == 0 ? 1 : 0;
+      r.ok = true;
+      return r;
+    }
+  }
+}
+
+template <class LT, class Levels, std::size_t... Roots>
+struct SemShape {
+  static constexpr int N = 5;
+  using Alg = Algebra<Levels>;
+
+  template <std::size_t L, std::size_t M>
+  using mem_t = tuple_element_t<M, tuple_element_t<L, Levels>>;
+
+  static constexpr bool level_sizes() {
+    if constexpr (tuple_size_v<Levels> != 6) {
+      return false;
+    } else {
+      constexpr std::array<std::size_t, 6> want{2, 3, 9, 1, 9, 3};
+      constexpr std::array<int, 6> kind{0, 0, 1, 2, 1, 2};
+      for (std::size_t l = 0; l < 6; ++l)
+        if (Alg::member_counts[l] != want[l]) return false;
+      bool k = true;
+      [&]<std::size_t... L>(std::index_sequence<L...>) {
+        ((k = k && member_traits<mem_t<L, 0>>::kind == kind[L]), ...);
+      }(std::make_index_sequence<6>{});
+      return k && sizeof...(Roots) == 3;
+    }
+  }
+
+  using Frame = std::array<int32_t, 4>;
+  static constexpr void fail(SemTables& t, bool& ok, int why) {
+    ok = false;
+    if (!t.why) t.why = why;
+  }
+
+  template <std::size_t M>
+  static constexpr void op_stage(SemTables& t, bool& ok) {
+    using S = mem_t<0, M>;
+    if constexpr (S::Rank != 2) {
+      fail(t, ok, 2);
+    } else {
+      constexpr auto l = to_array<typename S::modes_seq>();
+      for (int d = 0; d < 2; ++d)
+        if (LT::is_gridded(l[d]) || LT::tile(l[d]) != N) fail(t, ok, 3);
+    }
+  }
+
+  template <std::size_t M>
+  static constexpr void field_stage(SemTables& t, bool& ok, const Frame& F) {
+    if (!labels_equal<typename mem_t<1, M>::modes_seq>(F)) fail(t, ok, 4);
+  }
+
+  template <std::size_t M>
+  static constexpr void gradient(SemTables& t, bool& ok, const Frame& F, bool (&seen)[3][4]) {
+    const std::size_t op0 = Alg::member_base(0, 0), op1 = Alg::member_base(0, 1);
+    const std::size_t u0 = Alg::member_base(1, 0);
+    const SemContraction c = sem_contraction<mem_t<2, M>>(F);
+    if (!c.ok || (c.a_slot != op0 && c.a_slot != op1) || c.b_slot < u0 || c.b_slot >= u0 + 3) {
+      fail(t, ok, 5);
+      return;
+    }
+    const int comp = static_cast<int>(c.b_slot - u0);
+    t.g_comp[M] = comp;
+    t.g_axis[M] = c.axis;
+    t.g_op[M] = c.a_slot == op0 ? 0 : 1;
+    t.g_tr[M] = c.tr;
+    if (seen[comp][c.axis]) fail(t, ok, 6);
+    seen[comp][c.axis] = true;
+    t.g_of[comp][c.axis] = static_cast<int>(M);
+  }
+
+  template <std::size_t Q>
+  static constexpr void combine_operand(SemTables& t, bool& ok, const Frame& F, bool (&used)[9]) {
+    using Op = tuple_element_t<Q, typename mem_t<3, 0>::ops_tuple_t>;
+    if (!labels_equal<typename Op::modes_seq>(F)) fail(t, ok, 9);
+    const std::size_t g0 = Alg::member_base(2, 0);
+    const std::size_t slot = Op::SlotIdx;
+    if (slot < g0 || slot >= g0 + 9 || used[slot - g0]) {
+      fail(t, ok, 10);
+      return;
+    }
+    used[slot - g0] = true;
+    t.c_in[Q] = static_cast<int>(slot - g0);
+  }
+
+  template <std::size_t M>
+  static constexpr void divergence(SemTables& t, bool& ok, const Frame& F, bool (&used)[9],
+                                   int (&per_axis)[4]) {
+    const std::size_t op0 = Alg::member_base(0, 0), op1 = Alg::member_base(0, 1);
+    const std::size_t f0 = Alg::member_base(3, 0);
+    const SemContraction c = sem_contraction<mem_t<4, M>>(F);
+    if (!c.ok || (c.a_slot != op0 && c.a_slot != op1) || c.b_slot < f0 || c.b_slot >= f0 + 9 ||
+        used[c.b_slot - f0]) {
+      fail(t, ok, 11);
+      return;
+    }
+    const int src = static_cast<int>(c.b_slot - f0);
+    used[src] = true;
+    t.d_src[M] = src;
+    t.d_axis[M] = c.axis;
+    t.d_op[M] = c.a_slot == op0 ? 0 : 1;
+    t.d_tr[M] = c.tr;
+    if (per_axis[c.axis] >= 3) {
+      fail(t, ok, 12);
+      return;
+    }
+    t.d_slot[M] = per_axis[c.axis];
+    t.d_at[c.axis][per_axis[c.axis]] = static_cast<int>(M);
+    ++per_axis[c.axis];
+    t.d_of_src[src] = static_cast<int>(M);
+  }
+
+  template <std::size_t R, std::size_t Q>
+  static constexpr void sum_operand(SemTables& t, bool& ok, const Frame& F, bool (&used)[9]) {
+    using Op = tuple_element_t<Q, typename mem_t<5, R>::ops_tuple_t>;
+    if (!labels_equal<typename Op::modes_seq>(F)) fail(t, ok, 15);
+    const std::size_t d0 = Alg::member_base(4, 0);
+    const std::size_t slot = Op::SlotIdx;
+    if (slot < d0 || slot >= d0 + 9 || used[slot - d0]) {
+      fail(t, ok, 16);
+      return;
+    }
+    used[slot - d0] = true;
+    t.s_in[R][Q] = static_cast<int>(slot - d0);
+  }
+
+  template <std::size_t R>
+  static constexpr void sum_member(SemTables& t, bool& ok, const Frame& F, bool (&used)[9]) {
+    using S = mem_t<5, R>;
+    if constexpr (S::NumOps != 3 || S::NumOut != 1 || S::Rank != 4) {
+      fail(t, ok, 13);
+    } else {
+      if (!labels_equal<typename S::modes_seq>(F)) fail(t, ok, 14);
+      sum_operand<R, 0>(t, ok, F, used);
+      sum_operand<R, 1>(t, ok, F, used);
+      sum_operand<R, 2>(t, ok, F, used);
+      constexpr std::array<std::size_t, sizeof...(Roots)> roots{Roots...};
+      const std::size_t slot = Alg::member_base(5, R);
+      int pos = -1;
+      for (std::size_t i = 0; i < roots.size(); ++i)
+        if (roots[i] == slot) pos = static_cast<int>(i);
+      if (pos < 0) fail(t, ok, 17);
+      t.s_root[R] = pos;
+    }
+  }
+
+  template <std::size_t... I>
+  static constexpr void walk(SemTables& t, bool& ok, const Frame& F, std::index_sequence<I...>) {
+    op_stage<0>(t, ok);
+    op_stage<1>(t, ok);
+    field_stage<0>(t, ok, F);
+    field_stage<1>(t, ok, F);
+    field_stage<2>(t, ok, F);
+    bool seen[3][4] = {};
+    (gradient<I>(t, ok, F, seen), ...);
+    using Cb = mem_t<3, 0>;
+    if constexpr (Cb::NumOps != 9 || Cb::NumOut != 9 || Cb::Rank != 4) {
+      fail(t, ok, 7);
+    } else {
+      if (!labels_equal<typename Cb::modes_seq>(F)) fail(t, ok, 8);
+      bool used[9] = {};
+      (combine_operand<I>(t, ok, F, used), ...);
+    }
+    bool used_f[9] = {};
+    int per_axis[4] = {};
+    (divergence<I>(t, ok, F, used_f, per_axis), ...);
+    bool used_d[9] = {};
+    sum_member<0>(t, ok, F, used_d);
+    sum_member<1>(t, ok, F, used_d);
+    sum_member<2>(t, ok, F, used_d);
+    for (int a = 1; a < 4; ++a)
+      if (per_axis[a] != 3) fail(t, ok, 18);
+  }
+
+  static constexpr SemTables analyze() {
+    SemTables t{};
+    if constexpr (!level_sizes()) {
+      t.why = 1;
+      return t;
+    } else {
+      using U0 = mem_t<1, 0>;  // the frame: the first field stage's labels
+      if constexpr (U0::Rank != 4) {
+        t.why = 1;
+        return t;
+      } else {
+        constexpr auto Fa = to_array<typename U0::modes_seq>();
+        const Frame F{Fa[0], Fa[1], Fa[2], Fa[3]};
+        bool ok = LT::is_gridded(F[0]);
+        if (!ok) t.why = 100;
+        for (int d = 1; d < 4; ++d)
+          if (LT::is_gridded(F[d]) || LT::tile(F[d]) != N) fail(t, ok, 100);
+        walk(t, ok, F, std::make_index_sequence<9>{});
+        t.ok = ok;
+        return t;
+      }
+    }
+  }
+
+  static constexpr SemTables tables = analyze();
+  static constexpr bool ok = tables.ok;
+};
+
+// ---- the kernel ----------------------------------------------------------------
+
+// The two operators of the running launch, [op][o][p], row-major (per
+// translation unit; written by the launch, stream-ordered before the kernel).
+static __constant__ float sem_fused_ops_f32[2][5][5];
+static __constant__ double sem_fused_ops_f64[2][5][5];
+
+// Coefficient Op(o, p) of operator OP, transposed when TR: every index is a
+// compile-time constant once the loops are unrolled, so it is an immediate
+// constant-bank operand.
+template <class V, int OP, int TR>
+__device__ __forceinline__ V sem_op(int o, int p) {
+  if constexpr (std::is_same_v<V, float>)
+    return TR ? sem_fused_ops_f32[OP][p][o] : sem_fused_ops_f32[OP][o][p];
+  else
+    return TR ? sem_fused_ops_f64[OP][p][o] : sem_fused_ops_f64[OP][o][p];
+}
+
+struct SemFusedLayout {
+  static constexpr int N = 5, NN = 25, EB = 8, NT = EB * NN;
+  static constexpr int SKX = NT + 25, SKE = NT + 29;  // conflict-free k-strides (32-bit words)
+  static constexpr int CX = N * SKX, CE = N * SKE;
+  template <class V>
+  static constexpr std::size_t bytes() {
+    return sizeof(V) * (3 * CX + 3 * CE);
+  }
+};
+
+// out[o] = sum_p Op(o, p) in[p] for o, p < 5.
+template <class V, int OP, int TR>
+__device__ __forceinline__ void sem_line(const V* in, V* out) {
+#pragma unroll
+  for (int o = 0; o < 5; ++o) {
+    V s = V(0);
+#pragma unroll
+    for (int p = 0; p < 5; ++p) s = fma(sem_op<V, OP, TR>(o, p), in[p], s);
+    out[o] = s;
+  }
+}
+
+// Every table lookup below happens at compile time (static_for indices and
+// constexpr locals); a run-time index into the tables would put them in local
+// memory.
+template <class V, class Pat, class Levels, class Views>
+__global__ void __launch_bounds__(SemFusedLayout::NT, 2)
+    sem_fused_level_kernel(const Levels levels, const Views views, long long nelem) {
+  using LY = SemFusedLayout;
+  constexpr int N = LY::N, NN = LY::NN, EB = LY::EB;
+  constexpr int SKX = LY::SKX, SKE = LY::SKE, CX = LY::CX, CE = LY::CE;
+  extern __shared__ __align__(16) unsigned char sem_smem[];
+  V* X = reinterpret_cast<V*>(sem_smem);  // [3][N][SKX]: rows along x3 (i)
+  V* E = X + 3 * CX;                      // [3][N][SKE]: rows along x2 (j)
+
+  const int tid = threadIdx.x;
+  const int le = tid / NN;
+  const int ab = tid - le * NN;
+  const int ra = ab / N;        // column j / x3-line j / x2-line k
+  const int rb = ab - ra * N;   // column i / x3-line k / x2-line i
+  const int lx = rb * SKX + le * NN + ra * N;  // x3-line (k = rb, j = ra): + i
+  const int ly = ra * SKE + le * NN + rb;      // x2-line (k = ra, i = rb): + N j
+
+  const auto& lv1 = levels.template get<1>();
+  const auto& lv3 = levels.template get<3>();
+  const auto& lv5 = levels.template get<5>();
+  const auto& integrand = lv3.template get<0>().fn;
+
+  for (long long b = blockIdx.x; b * EB < nelem; b += gridDim.x) {
+    const long long e = b * EB + le;
+    const bool valid = e < nelem;
+    const int ei = valid ? static_cast<int>(e) : 0;
+
+    // ---- A: the column's fields -> X, E; gradients along x1 in registers ----
+    V dg[3][N];
+    static_for<3>([&](auto cc) {
+      constexpr int c = decltype(cc)::value;
+      const auto& u = lv1.template get<c>().operand_.handle.tensor;
+      V uc[N];
+#pragma unroll
+      for (int k = 0; k < N; ++k) uc[k] = valid ? static_cast<V>(u(ei, k, ra, rb)) : V(0);
+#pragma unroll
+      for (int k = 0; k < N; ++k) {
+        X[c * CX + k * SKX + tid] = uc[k];
+        E[c * CE + k * SKE + tid] = uc[k];
+      }
+      constexpr int m = Pat::tables.g_of[c][1];
+      sem_line<V, Pat::tables.g_op[m], Pat::tables.g_tr[m]>(uc, dg[c]);
+    });
+    __syncthreads();
+
+    // ---- B1: gradients along x3 (X rows) and x2 (E rows), in place ----
+    static_for<3>([&](auto cc) {
+      constexpr int c = decltype(cc)::value;
+      constexpr int mx = Pat::tables.g_of[c][3], me = Pat::tables.g_of[c][2];
+      V v[N], w[N], ov[N], ow[N];
+#pragma unroll
+      for (int p = 0; p < N; ++p) {
+        v[p] = X[c * CX + lx + p];
+        w[p] = E[c * CE + ly + p * N];
+      }
+      sem_line<V, Pat::tables.g_op[mx], Pat::tables.g_tr[mx]>(v, ov);
+      sem_line<V, Pat::tables.g_op[me], Pat::tables.g_tr[me]>(w, ow);
+#pragma unroll
+      for (int o = 0; o < N; ++o) {
+        X[c * CX + lx + o] = ov[o];
+        E[c * CE + ly + o * N] = ow[o];
+      }
+    });
+    __syncthreads();
+
+    // ---- B2: the nine-output combine at every point of the column ----
+    V Fg[3][N];
+#pragma unroll
+    for (int k = 0; k < N; ++k) {
+      V g[9];
+      static_for<9>([&](auto qq) {
+        constexpr int q = decltype(qq)::value;
+        constexpr int m = Pat::tables.c_in[q];
+        constexpr int comp = Pat::tables.g_comp[m], ax = Pat::tables.g_axis[m];
+        if constexpr (ax == 3)
+          g[q] = X[comp * CX + k * SKX + tid];
+        else if constexpr (ax == 2)
+          g[q] = E[comp * CE + k * SKE + tid];
+        else
+          g[q] = dg[comp][k];
+      });
+      V F[9];
+      if (valid) {
+        const auto r = integrand(ei, k, ra, rb, g[0], g[1], g[2], g[3], g[4], g[5], g[6], g[7], g[8]);
+#pragma unroll
+        for (int o = 0; o < 9; ++o) F[o] = static_cast<V>(r[o]);
+      } else {
+#pragma unroll
+        for (int o = 0; o < 9; ++o) F[o] = V(0);
+      }
+      static_for<9>([&](auto oo) {
+        constexpr int o = decltype(oo)::value;
+        constexpr int md = Pat::tables.d_of_src[o];
+        constexpr int ax = Pat::tables.d_axis[md], sl = Pat::tables.d_slot[md];
+        if constexpr (ax == 3)
+          X[sl * CX + k * SKX + tid] = F[o];
+        else if constexpr (ax == 2)
+          E[sl * CE + k * SKE + tid] = F[o];
+        else
+          Fg[sl][k] = F[o];
+      });
+    }
+    __syncthreads();
+
+    // ---- C1: divergences along x3 and x2, in place ----
+    static_for<3>([&](auto ss) {
+      constexpr int sl = decltype(ss)::value;
+      constexpr int mx = Pat::tables.d_at[3][sl], me = Pat::tables.d_at[2][sl];
+      V v[N], w[N], ov[N], ow[N];
+#pragma unroll
+      for (int q = 0; q < N; ++q) {
+        v[q] = X[sl * CX + lx + q];
+        w[q] = E[sl * CE + ly + q * N];
+      }
+      sem_line<V, Pat::tables.d_op[mx], Pat::tables.d_tr[mx]>(v, ov);
+      sem_line<V, Pat::tables.d_op[me], Pat::tables.d_tr[me]>(w, ow);
+#pragma unroll
+      for (int o = 0; o < N; ++o) {
+        X[sl * CX + lx + o] = ov[o];
+        E[sl * CE + ly + o * N] = ow[o];
+      }
+    });
+    __syncthreads();
+
+    // ---- C2: divergences along x1, the three combines, the roots ----
+    V tgc[3][N];
+    static_for<3>([&](auto ss) {
+      constexpr int sl = decltype(ss)::value;
+      constexpr int m = Pat::tables.d_at[1][sl];
+      sem_line<V, Pat::tables.d_op[m], Pat::tables.d_tr[m]>(Fg[sl], tgc[sl]);
+    });
+#pragma unroll
+    for (int k = 0; k < N; ++k) {
+      static_for<3>([&](auto rr) {
+        constexpr int R = decltype(rr)::value;
+        V t3[3];
+        static_for<3>([&](auto qq) {
+          constexpr int q = decltype(qq)::value;
+          constexpr int md = Pat::tables.s_in[R][q];
+          constexpr int ax = Pat::tables.d_axis[md], sl = Pat::tables.d_slot[md];
+          if constexpr (ax == 3)
+            t3[q] = X[sl * CX + k * SKX + tid];
+          else if constexpr (ax == 2)
+            t3[q] = E[sl * CE + k * SKE + tid];
+          else
+            t3[q] = tgc[sl][k];
+        });
+        if (valid) {
+          const V r = static_cast<V>(lv5.template get<R>().fn(ei, k, ra, rb, t3[0], t3[1], t3[2]));
+          views.template get<Pat::tables.s_root[R]>()(ei, k, ra, rb) = r;
+        }
+      });
+    }
+    __syncthreads();  // the next batch overwrites X and E
+  }
+}
+
+// Fused launch, or false when this graph / these views do not qualify (the
+// caller then runs the generic evaluator).  Throws nothing; CUDA errors come
+// back as the status in *err.
+template <class V, class LT, class Levels, class Views, std::size_t... Roots>
+bool sem_fused_launch(const Levels& levels, const Views& views, long long nelem, cudaError_t* err) {
+  using Pat = SemShape<LT, Levels, Roots...>;
+  *err = cudaSuccess;
+  if constexpr (!Pat::ok || !(std::is_same_v<V, float> || std::is_same_v<V, double>)) {
+    return false;
+  } else {
+    static const bool enabled = [] {
+      const char* e = std::getenv("TO_LEVELGRAPH_FUSED");
+      return !(e && std::strcmp(e, "0") == 0);
+    }();
+    if (!enabled) return false;
+    // every field and root: whole labels exactly 5; operators dense row-major 5 x 5
+    bool shapes = true;
+    [&]<std::size_t... C>(std::index_sequence<C...>) {
+      (
+          [&] {
+            const auto& u = levels.template get<1>().template get<C>().operand_.handle.tensor;
+            shapes = shapes && static_cast<long long>(u.extent(0)) == nelem;
+            for (int d = 1; d < 4; ++d) shapes = shapes && u.extent(d) == 5;
+          }(),
+          ...);
+    }(std::make_index_sequence<3>{});
+    [&]<std::size_t... R>(std::index_sequence<R...>) {
+      (
+          [&] {
+            const auto& f = views.template get<R>();
+            shapes = shapes && static_cast<long long>(f.extent(0)) == nelem;
+            for (int d = 1; d < 4; ++d) shapes = shapes && f.extent(d) == 5;
+          }(),
+          ...);
+    }(std::make_index_sequence<3>{});
+    const V* opdata[2] = {nullptr, nullptr};
+    [&]<std::size_t... S>(std::index_sequence<S...>) {
+      (
+          [&] {
+            const auto& h = levels.template get<0>().template get<S>().operand_.handle.tensor;
+            shapes = shapes && h.extent(0) == 5 && h.extent(1) == 5 && h.stride(0) == 5 &&
+                     h.stride(1) == 1;
+            opdata[S] = reinterpret_cast<const V*>(h.data());
+          }(),
+          ...);
+    }(std::make_index_sequence<2>{});
+    if (!shapes || nelem <= 0) return false;
+    using LY = SemFusedLayout;
+    constexpr std::size_t smem = LY::bytes<V>();
+    auto kernel = sem_fused_level_kernel<V, Pat, Levels, Views>;
+    int dev = 0, sms = 0, nb = 0;
+    if ((*err = cudaGetDevice(&dev)) != cudaSuccess) return true;
+    if ((*err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+      return true;
+    if (smem > 48 * 1024 &&
+        (*err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(smem))) != cudaSuccess)
+      return true;
+    if ((*err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kernel, LY::NT, smem)) !=
+        cudaSuccess)
+      return true;
+    for (int s = 0; s < 2; ++s) {
+      if constexpr (std::is_same_v<V, float>)
+        *err = cudaMemcpyToSymbolAsync(sem_fused_ops_f32, opdata[s], 25 * sizeof(V),
+                                       s * 25 * sizeof(V), cudaMemcpyDeviceToDevice, 0);
+      else
+        *err = cudaMemcpyToSymbolAsync(sem_fused_ops_f64, opdata[s], 25 * sizeof(V),
+                                       s * 25 * sizeof(V), cudaMemcpyDeviceToDevice, 0);
+      if (*err != cudaSuccess) return true;
+    }
+    const long long nbatch = (nelem + LY::EB - 1) / LY::EB;
+    const long long cap = static_cast<long long>(sms) * (nb > 0 ? nb : 1);
+    const int grid = static_cast<int>(nbatch < cap ? nbatch : cap);
+    kernel<<<grid, LY::NT, smem, 0>>>(levels, views, nelem);
+    *err = cudaGetLastError();
+    return true;
+  }
+}
+
+}  // namespace b200
+}  // namespace TensorOperations

@@ -266,7 +266,8 @@ class SlabOperator:
         self._own_comm = False
         if self.native:
             self.xstream = torch.cuda.Stream(device=device, priority=-100)  # highest priority
-            self.recv = [torch.empty(n, dtype=tdt, device=device) if side else None
+            nrecv = 4 * part.plane if getattr(plan, "interleaved", False) else n
+            self.recv = [torch.empty(nrecv, dtype=tdt, device=device) if side else None
                          for side in (part.rank > 0, part.rank < part.world - 1)]
             self.sync = torch.zeros(abi.slab_sync_bytes(), dtype=torch.uint8, device=device)
             sl = abi.Slab()

@@ -21,7 +21,8 @@ NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O2", "-std=c++20",
 
 GPU_PROGRAMS = {"kokkos_subset_gpu": HERE / "kokkos_subset_gpu.cpp",
                 "level_graph_runtime_gpu": HERE / "level_graph_runtime_gpu.cpp",
-                "tc_contract_gpu": HERE / "tc_contract_gpu.cpp"}
+                "tc_contract_gpu": HERE / "tc_contract_gpu.cpp",
+                "sem_fused_gpu": HERE / "sem_fused_gpu.cpp"}
 
 
 def _headers():

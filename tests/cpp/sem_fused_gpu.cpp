@@ -1,0 +1,318 @@
+// sem_fused_gpu.cpp -- TEST ONLY: LevelGraphs with the spectral-element
+// stiffness shape through the public API, run on the GPU and compared with a
+// double-precision host loop of the same operator.
+//
+// The launch picks the fused line-owner kernel for this shape
+// (b200/SemFused.cuh) unless TO_LEVELGRAPH_FUSED=0; the pytest driver runs
+// this program both ways.  Two spellings of the same operator:
+//   natural   the reference program's construction (bench_sem3d_levelgraph.cpp
+//             :247-351): H as (i,p), Hw as (p,i), members in gx, ge, gg order;
+//   shuffled  members of every level in another order, the combine's operands
+//             and outputs permuted (its functor permutes back), the second
+//             operator staged as H^T-weighted in (r,p) labels and used
+//             transposed, the roots designated out of order;
+// and the compile-time check that both are recognised.  E = 37 elements (a
+// partial last batch), TE = 1 and 2.  Max abs error / max abs value < 1e-5.
+#include <Kokkos_Core.hpp>
+#include <TensorOperations/LevelGraph.hpp>
+#include <TensorOperations/LevelPlan.hpp>
+
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+
+using namespace TensorOperations;
+using ES = Kokkos::DefaultExecutionSpace;
+constexpr int N = 5;
+using V4 = Kokkos::View<float* [N][N][N], Kokkos::LayoutRight>;
+using V2 = Kokkos::View<float**, Kokkos::LayoutRight>;
+using V1 = Kokkos::View<float*, Kokkos::LayoutRight>;
+
+struct Fields {
+  V4 u[3], m[12], f[3];
+  V2 H, Hw, HwT;  // HwT(r,p) = Hw(p,r)
+  V1 w;
+};
+
+static float val(int s, long long t) {
+  const double x = std::sin(0.37 * (s + 1) + 0.011 * double(t % 9973)) * 0.5;
+  return float(x);
+}
+
+static Fields make_fields(int E) {
+  Fields d;
+  for (int c = 0; c < 3; ++c) {
+    d.u[c] = V4("u", E);
+    d.f[c] = V4("f", E);
+  }
+  for (int q = 0; q < 12; ++q) d.m[q] = V4("m", E);
+  d.H = V2("H", N, N);
+  d.Hw = V2("Hw", N, N);
+  d.HwT = V2("HwT", N, N);
+  d.w = V1("w", N);
+  auto fill4 = [&](V4 v, int s, float base) {
+    auto h = Kokkos::create_mirror_view(v);
+    for (int e = 0; e < E; ++e)
+      for (int k = 0; k < N; ++k)
+        for (int j = 0; j < N; ++j)
+          for (int i = 0; i < N; ++i) h(e, k, j, i) = base + val(s, ((e * N + k) * N + j) * N + i);
+    Kokkos::deep_copy(v, h);
+  };
+  for (int c = 0; c < 3; ++c) fill4(d.u[c], c, 0.f);
+  for (int q = 0; q < 12; ++q) fill4(d.m[q], 10 + q, (q == 0 || q == 4 || q == 8 || q >= 9) ? 1.5f : 0.f);
+  auto hH = Kokkos::create_mirror_view(d.H);
+  auto hW = Kokkos::create_mirror_view(d.Hw);
+  auto hT = Kokkos::create_mirror_view(d.HwT);
+  auto hw = Kokkos::create_mirror_view(d.w);
+  for (int a = 0; a < N; ++a) hw(a) = 0.2f + 0.05f * a;
+  for (int a = 0; a < N; ++a)
+    for (int b = 0; b < N; ++b) hH(a, b) = 0.3f * std::sin(1.3f * a + 0.7f * b) + (a == b ? 0.1f : 0.f);
+  for (int a = 0; a < N; ++a)
+    for (int b = 0; b < N; ++b) {
+      hW(a, b) = hH(b, a) * hw(b);
+      hT(b, a) = hW(a, b);
+    }
+  Kokkos::deep_copy(d.H, hH);
+  Kokkos::deep_copy(d.Hw, hW);
+  Kokkos::deep_copy(d.HwT, hT);
+  Kokkos::deep_copy(d.w, hw);
+  return d;
+}
+
+// Isotropic elastic integrand: gradients dxi, det, dgm (3 components each) ->
+// fluxes F[r][c] = jac sum_d sigma[c][d] J[r][d], J[r][d] = m[3r+d], jac = m[9],
+// l2m = m[10], mu = m[11].
+template <class T>
+KOKKOS_INLINE_FUNCTION void physics(const T dxi[3], const T det[3], const T dgm[3], const T J[3][3],
+                                    T jac, T l2m, T mu, T F[3][3]) {
+  T ds[3][3];
+  for (int c = 0; c < 3; ++c)
+    for (int d = 0; d < 3; ++d) ds[c][d] = dxi[c] * J[0][d] + det[c] * J[1][d] + dgm[c] * J[2][d];
+  const T lam = l2m - T(2) * mu;
+  const T tr = ds[0][0] + ds[1][1] + ds[2][2];
+  T s[3][3];
+  for (int c = 0; c < 3; ++c)
+    for (int d = 0; d < 3; ++d) s[c][d] = mu * (ds[c][d] + ds[d][c]) + (c == d ? lam * tr : T(0));
+  for (int r = 0; r < 3; ++r)
+    for (int c = 0; c < 3; ++c) F[r][c] = jac * (s[c][0] * J[r][0] + s[c][1] * J[r][1] + s[c][2] * J[r][2]);
+}
+
+struct Integrand {
+  Fields d;
+  KOKKOS_FUNCTION Kokkos::Array<float, 9> operator()(int e, int k, int j, int i, float x0, float x1,
+                                                     float x2, float y0, float y1, float y2, float z0,
+                                                     float z1, float z2) const {
+    const float dxi[3] = {x0, x1, x2}, det[3] = {y0, y1, y2}, dgm[3] = {z0, z1, z2};
+    float J[3][3];
+    for (int r = 0; r < 3; ++r)
+      for (int q = 0; q < 3; ++q) J[r][q] = d.m[3 * r + q](e, k, j, i);
+    float F[3][3];
+    physics(dxi, det, dgm, J, d.m[9](e, k, j, i), d.m[10](e, k, j, i), d.m[11](e, k, j, i), F);
+    return {F[0][0], F[0][1], F[0][2], F[1][0], F[1][1], F[1][2], F[2][0], F[2][1], F[2][2]};
+  }
+};
+
+// The same maths with the operands in the shuffled order
+// (z2, x0, y1, z0, x2, y0, x1, z1, y2) and the outputs in the order
+// (F[2][1], F[0][0], F[1][2], F[2][0], F[0][2], F[1][1], F[0][1], F[2][2], F[1][0]).
+struct IntegrandShuffled {
+  Integrand in;
+  KOKKOS_FUNCTION Kokkos::Array<float, 9> operator()(int e, int k, int j, int i, float z2, float x0,
+                                                     float y1, float z0, float x2, float y0, float x1,
+                                                     float z1, float y2) const {
+    const auto r = in(e, k, j, i, x0, x1, x2, y0, y1, y2, z0, z1, z2);
+    return {r[7], r[0], r[5], r[6], r[2], r[4], r[1], r[8], r[3]};
+  }
+};
+
+struct WeightedSum {
+  Fields d;
+  KOKKOS_FUNCTION float operator()(int, int k, int j, int i, float t1, float t2, float t3) const {
+    return d.w(j) * d.w(k) * t1 + d.w(i) * d.w(k) * t2 + d.w(i) * d.w(j) * t3;
+  }
+};
+// operands (gamma, xi, eta)
+struct WeightedSumRot {
+  WeightedSum s;
+  KOKKOS_FUNCTION float operator()(int e, int k, int j, int i, float t3, float t1, float t2) const {
+    return s(e, k, j, i, t1, t2, t3);
+  }
+};
+
+template <int TE>
+using GMap = LabelTiles<LabelTile<'e', TE>, LabelWhole<'k', N>, LabelWhole<'j', N>,
+                        LabelWhole<'i', N>, LabelWhole<'p', N>, LabelWhole<'r', N>>;
+
+template <int TE>
+void natural(const Fields& d) {
+  const Integrand integ{d};
+  const WeightedSum ws{d};
+  auto g0 = make_level_graph<float, ES>(GMap<TE>{});
+  auto [g1, h, hw] = g0.add(make_stage_node(make_input_node(make_handle<'r', 'p'>(d.H))),
+                            make_stage_node(make_input_node(make_handle<'p', 'r'>(d.Hw))));
+  auto [g2, u0, u1, u2] = g1.add(make_stage_node(make_input_node(make_handle<'e', 'k', 'j', 'i'>(d.u[0]))),
+                                 make_stage_node(make_input_node(make_handle<'e', 'k', 'j', 'i'>(d.u[1]))),
+                                 make_stage_node(make_input_node(make_handle<'e', 'k', 'j', 'i'>(d.u[2]))));
+  auto gx = [&](auto u) {
+    return make_contraction_node<'e', 'k', 'j', 'i'>(h.template as<'i', 'p'>(), u.template as<'e', 'k', 'j', 'p'>());
+  };
+  auto ge = [&](auto u) {
+    return make_contraction_node<'e', 'k', 'j', 'i'>(h.template as<'j', 'p'>(), u.template as<'e', 'k', 'p', 'i'>());
+  };
+  auto gg = [&](auto u) {
+    return make_contraction_node<'e', 'k', 'j', 'i'>(h.template as<'k', 'p'>(), u.template as<'e', 'p', 'j', 'i'>());
+  };
+  auto [g3, a0, a1, a2, b0, b1, b2, c0, c1, c2] =
+      g2.add(gx(u0), gx(u1), gx(u2), ge(u0), ge(u1), ge(u2), gg(u0), gg(u1), gg(u2));
+  auto [g4, fx0, fx1, fx2, fe0, fe1, fe2, fg0, fg1, fg2] =
+      g3.add(make_combine_node<'e', 'k', 'j', 'i'>(a0, a1, a2, b0, b1, b2, c0, c1, c2, integ));
+  auto dx = [&](auto f) {
+    return make_contraction_node<'e', 'k', 'j', 'i'>(hw.template as<'p', 'i'>(), f.template as<'e', 'k', 'j', 'p'>());
+  };
+  auto de = [&](auto f) {
+    return make_contraction_node<'e', 'k', 'j', 'i'>(hw.template as<'p', 'j'>(), f.template as<'e', 'k', 'p', 'i'>());
+  };
+  auto dg = [&](auto f) {
+    return make_contraction_node<'e', 'k', 'j', 'i'>(hw.template as<'p', 'k'>(), f.template as<'e', 'p', 'j', 'i'>());
+  };
+  auto [g5, tx0, tx1, tx2, te0, te1, te2, tg0, tg1, tg2] =
+      g4.add(dx(fx0), dx(fx1), dx(fx2), de(fe0), de(fe1), de(fe2), dg(fg0), dg(fg1), dg(fg2));
+  auto [g6, r0, r1, r2] = g5.add(make_combine_node<'e', 'k', 'j', 'i'>(tx0, te0, tg0, ws),
+                                 make_combine_node<'e', 'k', 'j', 'i'>(tx1, te1, tg1, ws),
+                                 make_combine_node<'e', 'k', 'j', 'i'>(tx2, te2, tg2, ws));
+  using Shape = b200::SemShape<GMap<TE>, std::decay_t<decltype(g6.levels)>, decltype(r0)::SlotIdx,
+                               decltype(r1)::SlotIdx, decltype(r2)::SlotIdx>;
+  static_assert(Shape::ok, "the reference's SEM graph is recognised");
+  g6.outputs(r0, r1, r2).team_size(64).execute(TeamPolicyTag2<ES>{}, d.f[0], d.f[1], d.f[2]);
+}
+
+template <int TE>
+void shuffled(const Fields& d) {
+  const IntegrandShuffled integ{Integrand{d}};
+  const WeightedSumRot ws{WeightedSum{d}};
+  auto g0 = make_level_graph<float, ES>(GMap<TE>{});
+  // the transposed weighted operator first, H second
+  auto [g1, hwt, h] = g0.add(make_stage_node(make_input_node(make_handle<'r', 'p'>(d.HwT))),
+                             make_stage_node(make_input_node(make_handle<'r', 'p'>(d.H))));
+  auto [g2, u2, u0, u1] = g1.add(make_stage_node(make_input_node(make_handle<'e', 'k', 'j', 'i'>(d.u[2]))),
+                                 make_stage_node(make_input_node(make_handle<'e', 'k', 'j', 'i'>(d.u[0]))),
+                                 make_stage_node(make_input_node(make_handle<'e', 'k', 'j', 'i'>(d.u[1]))));
+  auto gx = [&](auto u) {
+    return make_contraction_node<'e', 'k', 'j', 'i'>(h.template as<'i', 'p'>(), u.template as<'e', 'k', 'j', 'p'>());
+  };
+  auto ge = [&](auto u) {
+    return make_contraction_node<'e', 'k', 'j', 'i'>(h.template as<'j', 'p'>(), u.template as<'e', 'k', 'p', 'i'>());
+  };
+  auto gg = [&](auto u) {
+    return make_contraction_node<'e', 'k', 'j', 'i'>(h.template as<'k', 'p'>(), u.template as<'e', 'p', 'j', 'i'>());
+  };
+  auto [g3, c2, a0, b1, c0, a2, b0, a1, c1, b2] =
+      g2.add(gg(u2), gx(u0), ge(u1), gg(u0), gx(u2), ge(u0), gx(u1), gg(u1), ge(u2));
+  auto [g4, o0, o1, o2, o3, o4, o5, o6, o7, o8] =
+      g3.add(make_combine_node<'e', 'k', 'j', 'i'>(c2, a0, b1, c0, a2, b0, a1, c1, b2, integ));
+  // outputs: o0=F[2][1] o1=F[0][0] o2=F[1][2] o3=F[2][0] o4=F[0][2] o5=F[1][1] o6=F[0][1] o7=F[2][2] o8=F[1][0]
+  // Hw(p,i) = HwT(i,p): the weighted transpose used with its summed label second
+  auto dx = [&](auto f) {
+    return make_contraction_node<'e', 'k', 'j', 'i'>(hwt.template as<'i', 'p'>(), f.template as<'e', 'k', 'j', 'p'>());
+  };
+  auto de = [&](auto f) {
+    return make_contraction_node<'e', 'k', 'j', 'i'>(hwt.template as<'j', 'p'>(), f.template as<'e', 'k', 'p', 'i'>());
+  };
+  auto dg = [&](auto f) {
+    return make_contraction_node<'e', 'k', 'j', 'i'>(hwt.template as<'k', 'p'>(), f.template as<'e', 'p', 'j', 'i'>());
+  };
+  auto [g5, tg1, tx0, te2, tg0, tx2, te1, tx1, tg2, te0] =
+      g4.add(dg(o0), dx(o1), de(o2), dg(o3), dx(o4), de(o5), dx(o6), dg(o7), de(o8));
+  auto [g6, s2, s0, s1] = g5.add(make_combine_node<'e', 'k', 'j', 'i'>(tg2, tx2, te2, ws),
+                                 make_combine_node<'e', 'k', 'j', 'i'>(tg0, tx0, te0, ws),
+                                 make_combine_node<'e', 'k', 'j', 'i'>(tg1, tx1, te1, ws));
+  using Shape = b200::SemShape<GMap<TE>, std::decay_t<decltype(g6.levels)>, decltype(s1)::SlotIdx,
+                               decltype(s0)::SlotIdx, decltype(s2)::SlotIdx>;
+  static_assert(Shape::ok, "the shuffled spelling is recognised");
+  g6.outputs(s1, s0, s2).team_size(64).execute(TeamPolicyTag2<ES>{}, d.f[1], d.f[0], d.f[2]);
+}
+
+// Host reference in double.
+static double check(const Fields& d, int E) {
+  auto h = [&](const V4& v) {
+    auto m = Kokkos::create_mirror_view(v);
+    Kokkos::deep_copy(m, v);
+    return m;
+  };
+  auto H = Kokkos::create_mirror_view(d.H);
+  auto Hw = Kokkos::create_mirror_view(d.Hw);
+  auto w = Kokkos::create_mirror_view(d.w);
+  Kokkos::deep_copy(H, d.H);
+  Kokkos::deep_copy(Hw, d.Hw);
+  Kokkos::deep_copy(w, d.w);
+  decltype(h(d.u[0])) u[3] = {h(d.u[0]), h(d.u[1]), h(d.u[2])};
+  decltype(h(d.u[0])) f[3] = {h(d.f[0]), h(d.f[1]), h(d.f[2])};
+  decltype(h(d.u[0])) m[12] = {h(d.m[0]), h(d.m[1]), h(d.m[2]), h(d.m[3]), h(d.m[4]), h(d.m[5]),
+                               h(d.m[6]), h(d.m[7]), h(d.m[8]), h(d.m[9]), h(d.m[10]), h(d.m[11])};
+  double err = 0, mx = 0;
+  static double Fx[3][N][N][N], Fe[3][N][N][N], Fg[3][N][N][N];
+  for (int e = 0; e < E; ++e) {
+    for (int k = 0; k < N; ++k)
+      for (int j = 0; j < N; ++j)
+        for (int i = 0; i < N; ++i) {
+          double dxi[3], det[3], dgm[3], J[3][3], F[3][3];
+          for (int c = 0; c < 3; ++c) {
+            dxi[c] = det[c] = dgm[c] = 0;
+            for (int p = 0; p < N; ++p) {
+              dxi[c] += double(H(i, p)) * u[c](e, k, j, p);
+              det[c] += double(H(j, p)) * u[c](e, k, p, i);
+              dgm[c] += double(H(k, p)) * u[c](e, p, j, i);
+            }
+          }
+          for (int r = 0; r < 3; ++r)
+            for (int q = 0; q < 3; ++q) J[r][q] = m[3 * r + q](e, k, j, i);
+          physics<double>(dxi, det, dgm, J, m[9](e, k, j, i), m[10](e, k, j, i), m[11](e, k, j, i), F);
+          for (int c = 0; c < 3; ++c) {
+            Fx[c][k][j][i] = F[0][c];
+            Fe[c][k][j][i] = F[1][c];
+            Fg[c][k][j][i] = F[2][c];
+          }
+        }
+    for (int c = 0; c < 3; ++c)
+      for (int k = 0; k < N; ++k)
+        for (int j = 0; j < N; ++j)
+          for (int i = 0; i < N; ++i) {
+            double tx = 0, te = 0, tg = 0;
+            for (int p = 0; p < N; ++p) {
+              tx += double(Hw(p, i)) * Fx[c][k][j][p];
+              te += double(Hw(p, j)) * Fe[c][k][p][i];
+              tg += double(Hw(p, k)) * Fg[c][p][j][i];
+            }
+            const double want = double(w(j)) * w(k) * tx + double(w(i)) * w(k) * te +
+                                double(w(i)) * w(j) * tg;
+            err = std::fmax(err, std::fabs(want - f[c](e, k, j, i)));
+            mx = std::fmax(mx, std::fabs(want));
+          }
+  }
+  return err / mx;
+}
+
+int main(int argc, char** argv) {
+  Kokkos::initialize(argc, argv);
+  int fails = 0;
+  {
+    const int E = 37;
+    Fields d = make_fields(E);
+    auto run = [&](const char* name, auto fn) {
+      for (int c = 0; c < 3; ++c) Kokkos::deep_copy(d.f[c], 0.f);
+      fn(d);
+      Kokkos::fence();
+      const double rel = check(d, E);
+      const bool ok = rel < 1e-5;
+      std::printf("%-24s max rel err %.3e  %s\n", name, rel, ok ? "PASS" : "FAIL");
+      fails += !ok;
+    };
+    run("natural TE=1", natural<1>);
+    run("natural TE=2", natural<2>);
+    run("shuffled TE=1", shuffled<1>);
+    run("shuffled TE=2", shuffled<2>);
+  }
+  Kokkos::finalize();
+  std::printf("%s\n", fails ? "SOME FAILED" : "ALL PASS");
+  return fails ? 1 : 0;
+}

@@ -15,6 +15,11 @@
   combines) lowered onto the level plan -- 6 levels, 57 slots, the grid from
   the last node -- and run through the same host-compiled evaluator under
   AddressSanitizer/UBSan against a direct loop, with a partial last tile.
+* the reference's own negative-compilation files, unmodified, from where they
+  lie (tests/negative/level_guard_negative.cpp cases 0-5 and
+  labeltiles_guard_negative.cpp cases 0-2): each failing case must fail with
+  the regular expression the reference's CMakeLists.txt:231-295 pins for it,
+  and the controls must compile (skipped where the reference tree is absent).
 * dag_guard_negative.cpp: each DagGraph diagnostic fires on the graph it
   forbids; the control graph compiles.
 * kokkos_subset_host_check.cpp: the Kokkos subset on the host -- scratch
@@ -47,6 +52,24 @@ GUARDS = {
     7: "must appear in the graph's tile",
 }
 ALL_MESSAGES = set(GUARDS.values())
+
+
+# The reference's own negative files and the message its CMakeLists.txt
+# requires of each failing case (PASS_REGULAR_EXPRESSION, :231-238, :285-295).
+REF_NEGATIVE = {
+    ("level_guard_negative.cpp", "LEVEL_NEG_CASE"): {
+        0: None, 1: "a level must be NON-EMPTY and HOMOGENEOUS",
+        2: "must share ONE iteration space", 3: "must share ONE iteration space",
+        4: "may not read a slot ITS OWN LEVEL", 5: "must share ONE iteration space"},
+    ("labeltiles_guard_negative.cpp", "LABELTILES_NEG_CASE"): {
+        0: None, 1: "may appear at most once in the map", 2: "must appear in the graph's tile"},
+}
+
+
+def _reference_root():
+    import os
+    root = Path(os.environ.get("TO_REFERENCE_ROOT", str(ROOT.parent / "reference")))
+    return root if (root / "tests" / "negative").is_dir() else None
 
 
 def _compile(args, timeout=300):
@@ -149,3 +172,18 @@ def test_kokkos_subset_on_the_host(tmp_path):
     assert r.returncode == 0, r.stderr[-3000:]
     run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
     assert run.returncode == 0 and "kokkos subset host ok" in run.stdout, run.stdout + run.stderr
+
+
+@pytest.mark.parametrize("fname,macro,case", [(f, m, c) for (f, m), cases in REF_NEGATIVE.items()
+                                              for c in cases])
+def test_reference_negative_file_unmodified(fname, macro, case):
+    ref = _reference_root()
+    if ref is None:
+        pytest.skip("reference tree not mounted")
+    want = REF_NEGATIVE[(fname, macro)][case]
+    r = _compile(["-fsyntax-only", f"-D{macro}={case}", str(ref / "tests" / "negative" / fname)])
+    if want is None:
+        assert r.returncode == 0, r.stderr[-3000:]
+    else:
+        assert r.returncode != 0
+        assert want in r.stderr, r.stderr[-3000:]

@@ -12,6 +12,9 @@
   per layer take the per-range fallback; one layer touching both planes is
   scattered once.
 * Two applications in a row give the same f (tickets and f are reset).
+* The interleaved node layout (u, f as [nglob][4]) through the same call:
+  the planes travel as one contiguous range each; f, de-interleaved, equals
+  the planar result.
 """
 import numpy as np
 import pytest
@@ -105,3 +108,57 @@ def test_rejects_partial_layers_and_missing_communicator():
     with pytest.raises(abi.ToError) as e:
         abi.sem3d_elastic_mgpu(plan, fl, sl, None, 0, 0)
     assert e.value.status == abi.TO_ERR_INVALID_ARGUMENT
+
+
+@pytest.mark.parametrize("mesh", [(4, 3, 5), (4, 4, 1)])
+@pytest.mark.parametrize("self_exchange", [False, True])
+def test_interleaved_nodes(mesh, self_exchange):
+    import torch
+    nex, ney, nez = mesh
+    prob = structured_problem(nex, ney, nez, ngll=N, dtype=np.float32, assembled=True, seed=34)
+    u, f, arrays, ibool = to_device(prob, "cuda")
+    u4 = torch.empty((prob.nglob, 4), dtype=torch.float32, device="cuda")
+    f4 = torch.full((prob.nglob, 4), 7.0, dtype=torch.float32, device="cuda")  # zeroed by the call
+    abi.nodes_interleave(u, u4, prob.nglob)
+    plan = abi.Sem3dPlan(np.float32, N, prob.nelem, prob.H, prob.Hw, prob.w, nglob=prob.nglob,
+                         assembled=True, interleaved=True)
+    nb = -1 if not self_exchange else 0
+    sl, keep, plane = _slab(torch, nex, ney, nb, nb)
+    recv4 = [torch.empty(4 * plane, device="cuda") for _ in range(2)]
+    sl.recv[0], sl.recv[1] = recv4[0].data_ptr(), recv4[1].data_ptr()
+    cs = torch.cuda.Stream()
+    xs = torch.cuda.Stream(priority=-100)
+    comm = abi.nccl_comm_init(1, 0, abi.nccl_unique_id()) if self_exchange else None
+    try:
+        fl = plan.fields([u4, None, None], [f4, None, None], arrays, ibool)
+        for _ in range(2):
+            abi.sem3d_elastic_mgpu(plan, fl, sl, comm, cs.cuda_stream, xs.cuda_stream)
+        torch.cuda.synchronize()
+    finally:
+        if comm:
+            abi.nccl_comm_destroy(comm)
+    back = [torch.empty(prob.nglob, device="cuda") for _ in range(3)]
+    abi.nodes_deinterleave(f4, back, prob.nglob)
+    torch.cuda.synchronize()
+    assert float(f4[:, 3].abs().max()) == 0.0  # the unused lane stays zero
+    got = [x.cpu().numpy() for x in back]
+    want = [x.copy() for x in _oracle(prob)]
+    if self_exchange:
+        for x in want:
+            x[:plane] *= 2
+            x[-plane:] *= 2
+    assert osem.rel_l2(got, want) < TOL
+
+
+def test_node_layout_round_trip():
+    import torch
+    n = 1001
+    x = [torch.randn(n, device="cuda") for _ in range(3)]
+    x4 = torch.empty((n, 4), device="cuda")
+    abi.nodes_interleave(x, x4, n)
+    y = [torch.empty(n, device="cuda") for _ in range(3)]
+    abi.nodes_deinterleave(x4, y, n)
+    torch.cuda.synchronize()
+    for a, b in zip(x, y):
+        assert torch.equal(a, b)
+    assert torch.equal(x4[:, 1], x[1]) and float(x4[:, 3].abs().max()) == 0.0
