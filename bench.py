@@ -24,9 +24,10 @@ timed with CUDA events on the launching stream over exactly K steps between
 barriers, max over ranks.  `roofline.achieved` = algorithmic bytes per launch
 (12 per-point f32 arrays + ibool per point, u read and f written once per
 global node) / the kernel's average CUDA-event duration.  `e2e` times the same
-operator through the C ABI with pinned HOST u and f (H2D of u and D2H of f
-of every step inside the timed region, mesh resident; consecutive steps'
-copies overlap on separate streams).  The CPU baseline is the OpenMP C++
+operator through the C ABI's host-buffer call (to_sem3d_elastic_mgpu_host) with
+pinned HOST u and f: H2D of u and D2H of f of every step inside the timed
+region, mesh resident; two buffer sets on two streams overlap consecutive
+steps' copies.  The CPU baseline is the OpenMP C++
 restatement of the reference's host loop (the reference itself needs Kokkos,
 which is not installed), timed on this host on a bounded number of full
 applications.
@@ -69,7 +70,7 @@ NCU_TRAFFIC_BY_LAYOUT = {
     "components": (2225873664.0 + 214804736.0,
                    "ncu dram__bytes_read+write of one 64^3 launch (grid-stride build of the "
                    "same kernel, identical data movement)"),
-    "interleaved": (None, None)}
+    "interleaved": (2248828672.0 + 242721792.0, "ncu dram__bytes_read+write of one 64^3 launch")}
 KERNEL_NAMES = {"0": "sem3d_elastic_v3_kernel<5,8,2,true>",
                 "1": "sem3d_elastic_tma_kernel<float,5,8,2,true>",
                 "2": "sem3d_elastic_kernel<float,5,32,true>",
@@ -998,55 +999,49 @@ def main():
     # drain inside the timed region weigh about 4 % of it
     e2e_steps = 0 if args.no_e2e else 24
     if e2e_steps:
-        # host data is one array per component; with interleaved nodes each step
-        # also runs the layout kernels (planar u -> [nglob][4] before the operator,
-        # [nglob][4] f -> planar after it) inside the timed region
+        # Every step is ONE call of the C ABI's host-buffer entry
+        # (to_sem3d_elastic_mgpu_host): copy u in from pinned host memory (one
+        # array per component), convert it to the device layout, apply with the
+        # neighbour exchange, convert f back and copy it out -- all inside the
+        # timed region.  Two device buffer sets on two streams overlap one
+        # step's copy-out with the next step's copy-in (PCIe is full duplex).
         u_host = [torch.from_numpy(x).pin_memory() for x in prob.u]
         f_host = [[torch.empty(prob.nglob, dtype=torch.float32).pin_memory() for _ in range(3)]
                   for _ in range(2)]
-        u_set = [[torch.empty(prob.nglob, dtype=torch.float32, device=dev) for _ in range(3)]
-                 for _ in range(2)]
-        f_set = [[torch.empty(prob.nglob, dtype=torch.float32, device=dev) for _ in range(3)]
-                 for _ in range(2)]
-        if il:
-            u4_set = [torch.empty((prob.nglob, 4), dtype=torch.float32, device=dev)
-                      for _ in range(2)]
-            f4_set = [dev_f[0], torch.empty((prob.nglob, 4), dtype=torch.float32, device=dev)]
-            ops = [SlabOperator(part, plan, plan.fields([u4_set[k], None, None],
-                                                        [f4_set[k], None, None], arrays, ibool),
-                                [f4_set[k]], dev, comm=op.comm) for k in range(2)]
-        else:
-            ops = [SlabOperator(part, plan, plan.fields(u_set[k], f_set[k], arrays, ibool),
-                                f_set[k], dev, comm=op.comm) for k in range(2)]
-        s_in = torch.cuda.Stream(device=dev)
-        s_out = torch.cuda.Stream(device=dev)
-        ev_in = [torch.cuda.Event() for _ in range(2)]
-        ev_comp = [torch.cuda.Event() for _ in range(2)]
-        ev_out = [torch.cuda.Event() for _ in range(2)]
+        ops, hosts, keep = [], [], []
+        for k in range(2):
+            if il:
+                u4k = torch.empty((prob.nglob, 4), dtype=torch.float32, device=dev)
+                f4k = dev_f[0] if k == 0 else torch.empty((prob.nglob, 4), dtype=torch.float32,
+                                                          device=dev)
+                stage = [torch.empty(prob.nglob, dtype=torch.float32, device=dev)
+                         for _ in range(3)]
+                flk = plan.fields([u4k, None, None], [f4k, None, None], arrays, ibool)
+                keep += [u4k, f4k] + stage
+                fo = [f4k]
+            else:
+                uk = [torch.empty(prob.nglob, dtype=torch.float32, device=dev) for _ in range(3)]
+                fk = [torch.empty(prob.nglob, dtype=torch.float32, device=dev) for _ in range(3)]
+                stage = [None, None, None]
+                flk = plan.fields(uk, fk, arrays, ibool)
+                keep += uk + fk
+                fo = fk
+            o = SlabOperator(part, plan, flk, fo, dev, comm=op.comm)
+            o.slab.f_is_zero = 0  # the call zeroes f itself
+            ops.append(o)
+            h = abi.HostNodes()
+            for c in range(3):
+                h.u[c] = u_host[c].data_ptr()
+                h.f[c] = f_host[k][c].data_ptr()
+                h.stage[c] = stage[c].data_ptr() if stage[c] is not None else None
+            hosts.append(h)
+        e2e_streams = [torch.cuda.Stream(device=dev) for _ in range(2)]
+        xs = ops[0].xstream  # one exchange stream: NCCL calls on one communicator in order
 
     def e2e_step(i):
         k = i % 2
-        if i >= 2:
-            s_in.wait_event(ev_comp[k])  # step i-2's kernels are done reading u_set[k]
-        with torch.cuda.stream(s_in):
-            for c in range(3):
-                u_set[k][c].copy_(u_host[c], non_blocking=True)
-        ev_in[k].record(s_in)
-        stream.wait_event(ev_in[k])
-        if i >= 2:
-            stream.wait_event(ev_out[k])  # step i-2's f_set[k] has left the device
-        with torch.cuda.stream(stream):
-            if il:
-                abi.nodes_interleave(u_set[k], u4_set[k], prob.nglob, stream.cuda_stream)
-            ops[k].apply(stream)
-            if il:
-                abi.nodes_deinterleave(f4_set[k], f_set[k], prob.nglob, stream.cuda_stream)
-        ev_comp[k].record(stream)
-        s_out.wait_event(ev_comp[k])
-        with torch.cuda.stream(s_out):
-            for c in range(3):
-                f_host[k][c].copy_(f_set[k][c], non_blocking=True)
-        ev_out[k].record(s_out)
+        abi.sem3d_elastic_mgpu_host(plan, ops[k].fields, ops[k].slab, ops[k].comm, hosts[k],
+                                    e2e_streams[k].cuda_stream, xs.cuda_stream)
 
     e2e_ms = 0.0
     if e2e_steps:
@@ -1058,10 +1053,14 @@ def main():
     if e2e_steps:
         a0 = torch.cuda.Event(enable_timing=True)
         a1 = torch.cuda.Event(enable_timing=True)
-        a0.record(s_in)
+        ev1 = torch.cuda.Event()
+        a0.record(e2e_streams[0])
+        e2e_streams[1].wait_event(a0)
         for i in range(e2e_steps):
             e2e_step(i)
-        a1.record(s_out)
+        ev1.record(e2e_streams[1])
+        e2e_streams[0].wait_event(ev1)
+        a1.record(e2e_streams[0])
         torch.cuda.synchronize()
         e2e_ms = a0.elapsed_time(a1) / e2e_steps
     t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
@@ -1102,7 +1101,9 @@ def main():
             "e2e": None if not e2e_steps else
                    {"value": nelem_total / (e2e_ms * 1e-3) / 1e6, "unit": "Melem/s",
                     "h2d_bytes_per_step": bytes_uf, "d2h_bytes_per_step": bytes_uf,
-                    "steps": e2e_steps},
+                    "steps": e2e_steps,
+                    "call": "to_sem3d_elastic_mgpu_host (pinned host u / f, one array per "
+                            "component; copies and layout conversion inside the call)"},
             "check": check,
             "gpu_launches": args.steps * op.kernel_launches(),
             "clocks": clocks.summary(),

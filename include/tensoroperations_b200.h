@@ -283,6 +283,26 @@ int to_sem3d_elastic_mgpu(const to_sem3d_plan* plan, const to_sem3d_fields* fiel
                           const to_slab* slab, ncclComm_t comm, void* compute_stream,
                           void* comm_stream);
 
+/*
+ * The same call with u and f in HOST memory, one array per component (pinned
+ * memory for asynchronous copies): on compute_stream it copies u in (and,
+ * with interleaved nodes, converts it into fields->u[0] through host->stage),
+ * applies the operator as to_sem3d_elastic_mgpu, and copies f out (converting
+ * from fields->f[0] through host->stage).  fields->u / f are the device
+ * buffers the operator uses; `stage` holds three device arrays of nglob values
+ * (interleaved plans only; NULL otherwise).  Two calls on two streams with
+ * two sets of device buffers overlap one call's copy-out with the next one's
+ * copy-in.  The end-to-end path a caller with host data takes.
+ */
+typedef struct to_host_nodes {
+  const void* u[3];      /* HOST: nglob values per component, read            */
+  void* f[3];            /* HOST: nglob values per component, written         */
+  void* stage[3];        /* DEVICE: nglob values each (interleaved plans)     */
+} to_host_nodes;
+int to_sem3d_elastic_mgpu_host(const to_sem3d_plan* plan, const to_sem3d_fields* fields,
+                               const to_slab* slab, ncclComm_t comm, const to_host_nodes* host,
+                               void* compute_stream, void* comm_stream);
+
 /* NCCL set-up for callers without their own: rank 0 makes an id (bytes
  * TO_NCCL_UNIQUE_ID_BYTES), every rank receives it by its own means and
  * creates its communicator (the current device is the rank's GPU).  These and

@@ -85,6 +85,11 @@ class Acoustic2dFields(C.Structure):
         [(n, C.c_void_p) for n in ("xix", "xiz", "gamx", "gamz", "jac", "rho")]
 
 
+class HostNodes(C.Structure):
+    """to_host_nodes: host u / f (one array per component) and device stage arrays."""
+    _fields_ = [("u", C.c_void_p * 3), ("f", C.c_void_p * 3), ("stage", C.c_void_p * 3)]
+
+
 class Slab(C.Structure):
     """to_slab: one rank's z-slab of a structured mesh (see to_sem3d_elastic_mgpu)."""
     _fields_ = [("prev", C.c_int32), ("next", C.c_int32), ("layer_elems", C.c_int64),
@@ -150,6 +155,9 @@ _sig("to_nodes_deinterleave", C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_v
 _sig("to_slab_sync_bytes", C.c_size_t, [])
 _sig("to_sem3d_elastic_mgpu", C.c_int, [C.c_void_p, C.POINTER(Sem3dFields), C.POINTER(Slab),
                                         C.c_void_p, C.c_void_p, C.c_void_p])
+_sig("to_sem3d_elastic_mgpu_host", C.c_int, [C.c_void_p, C.POINTER(Sem3dFields), C.POINTER(Slab),
+                                             C.c_void_p, C.POINTER(HostNodes), C.c_void_p,
+                                             C.c_void_p])
 _sig("to_nccl_unique_id", C.c_int, [C.c_void_p])
 _sig("to_nccl_comm_init", C.c_int, [C.c_int32, C.c_int32, C.c_void_p, C.POINTER(C.c_void_p)])
 _sig("to_nccl_comm_destroy", C.c_int, [C.c_void_p])
@@ -355,6 +363,14 @@ def sem3d_elastic_mgpu(plan, fields, slab: Slab, comm: int, compute_stream: int,
     """f = K u on a z-slab rank, shared planes summed across its neighbours (NCCL)."""
     check(lib.to_sem3d_elastic_mgpu(plan._h, C.byref(fields), C.byref(slab), comm or None,
                                     compute_stream, comm_stream), "to_sem3d_elastic_mgpu")
+
+
+def sem3d_elastic_mgpu_host(plan, fields, slab: Slab, comm: int, host: HostNodes,
+                            compute_stream: int, comm_stream: int):
+    """to_sem3d_elastic_mgpu with host u / f: copies in, applies, copies out."""
+    check(lib.to_sem3d_elastic_mgpu_host(plan._h, C.byref(fields), C.byref(slab), comm or None,
+                                         C.byref(host), compute_stream, comm_stream),
+          "to_sem3d_elastic_mgpu_host")
 
 
 def sm_count() -> int:

@@ -216,12 +216,11 @@ int launch_v5(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t
 
 // The line-owner kernel over up to two element ranges with ticketed batches
 // (f32 NGLL 5, assembled, either node layout; the z-slab operator's launches).
-template <bool IL>
+template <bool IL, int OPT = kV5Packed | kV5Ranges>
 int launch_v5_ranges(const to_sem3d_plan* plan, const to_sem3d_fields* fl, const int64_t first[2],
                      const int64_t count[2], unsigned long long* ticket, cudaStream_t stream,
                      int dev, int sms) {
   constexpr int EB = 8, NT = EB * 25;
-  constexpr int OPT = kV5Packed | kV5Ranges;
   const size_t smem = Sem3dV5Layout<EB, true>::kTotal;
   auto kernel = sem3d_elastic_v5_kernel<EB, 3, true, IL, OPT>;
   static KernelSlot slot;
@@ -272,12 +271,12 @@ int launch_lo(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t
 }
 
 // The half-column line-owner kernel (NGLL 8): two owners per column.
-template <typename T, int EB, int MINB, bool ASM>
+template <typename T, int EB, int MINB, bool ASM, bool PIPE = false>
 int launch_hc(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t stream,
               int dev, int sms) {
   constexpr int NT = EB * 128;
   const size_t smem = Sem3dHcLayout<T, EB>::kTotal;
-  auto kernel = sem3d_elastic_hc_kernel<T, EB, MINB, ASM>;
+  auto kernel = sem3d_elastic_hc_kernel<T, EB, MINB, ASM, PIPE>;
   static KernelSlot slot;
   int nb = 0;
   if (int st = configure(slot, kernel, dev, NT, smem, &nb)) return st;
@@ -306,6 +305,15 @@ int sem3d_f32_variant() {
     return e ? std::atoi(e) : 5;
   }();
   return v;
+}
+
+// Warp-aggregated scatter-add in the ticketed launches (TO_SEM3D_WARP_AGG=1).
+bool sem3d_warp_agg() {
+  static const bool on = [] {
+    const char* e = std::getenv("TO_SEM3D_WARP_AGG");
+    return e && std::atoi(e) != 0;
+  }();
+  return on;
 }
 
 template <typename T, int N, bool ASM>
@@ -339,9 +347,13 @@ int launch_sem3d(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStrea
     // whole-column one (the half-column kernel measured 1.91 vs 1.59 ms at
     // E=196,608); TO_SEM3D_VARIANT 10 / 12 force one or the other, 2 the
     // streaming kernel
+    // (the half-column kernel loads the next point's geometry ahead: 58.7 vs
+    // 60.3 ms per 128^3 power step; TO_SEM3D_VARIANT 14 keeps per-point loads)
     const int v = sem3d_f32_variant();
-    if (v == 10 || (sizeof(T) == 8 && v != 2 && v != 12))
-      return launch_hc<T, 2, sizeof(T) == 8 ? 2 : 3, ASM>(plan, fl, stream, dev, sms);
+    if (v == 14)
+      return launch_hc<T, 2, sizeof(T) == 8 ? 2 : 3, ASM, false>(plan, fl, stream, dev, sms);
+    if (v == 10 || v == 13 || (sizeof(T) == 8 && v != 2 && v != 12))
+      return launch_hc<T, 2, sizeof(T) == 8 ? 2 : 3, ASM, true>(plan, fl, stream, dev, sms);
     if (v != 2)
       return launch_lo<T, N, 2, sizeof(T) == 8 ? 2 : 3, ASM>(plan, fl, stream, dev, sms);
   }
@@ -434,6 +446,11 @@ int sem3d_apply_ranges(const to_sem3d_plan* plan, const to_sem3d_fields* fl,
     if (il && (!aligned(fl->u[0], 16) || !aligned(fl->f[0], 16)))
       return set_error(TO_ERR_ALIGNMENT, "sem3d ranges: interleaved u / f not 16-byte aligned");
     if (!fl->ibool) return set_error(TO_ERR_INVALID_ARGUMENT, "sem3d ranges: null ibool");
+    if (sem3d_warp_agg()) {
+      constexpr int kAggOpt = kV5Packed | kV5Ranges | kV5WarpAgg;
+      if (il) return launch_v5_ranges<true, kAggOpt>(plan, fl, first, count, ticket, stream, dev, sms);
+      return launch_v5_ranges<false, kAggOpt>(plan, fl, first, count, ticket, stream, dev, sms);
+    }
     if (il) return launch_v5_ranges<true>(plan, fl, first, count, ticket, stream, dev, sms);
     return launch_v5_ranges<false>(plan, fl, first, count, ticket, stream, dev, sms);
   }

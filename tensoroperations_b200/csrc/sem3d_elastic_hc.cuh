@@ -43,7 +43,11 @@ struct Sem3dHcLayout {
   static constexpr size_t kTotal = kXBytes + kEBytes + kGBytes;
 };
 
-template <typename T, int EB, int MINB, bool ASM>
+// PIPE: the next point's geometry is loaded before the current point is
+// computed, so its twelve loads are in flight during that point's physics and
+// ahead of its shared-memory stores (which the compiler may not move loads
+// through generic pointers across).
+template <typename T, int EB, int MINB, bool ASM, bool PIPE = false>
 __global__ void __launch_bounds__(EB * 128, MINB)
     sem3d_elastic_hc_kernel(const __grid_constant__ Sem3dArgs<T, 8> a) {
   using LY = Sem3dHcLayout<T, EB>;
@@ -177,19 +181,35 @@ __global__ void __launch_bounds__(EB * 128, MINB)
     __syncthreads();
 
     // ---- B2: Integrand9 at the half-column's points; geometry from global ----
-#pragma unroll
-    for (int kk = 0; kk < H; ++kk) {
-      const int k = k0 + kk;
-      const long long pidx = base + k * NN;
-      T J[3][3], jac = T(0), l2m = T(0), mu = T(0);
+    T Jn[3][3], jacn = T(0), l2mn = T(0), mun = T(0);  // the next point's (PIPE)
+    auto load_geom = [&](int kk, T (&Jd)[3][3], T& jd, T& ld, T& md) {
+      const long long pidx = base + (k0 + kk) * NN;
 #pragma unroll
       for (int rr = 0; rr < 3; ++rr)
 #pragma unroll
-        for (int d = 0; d < 3; ++d) J[rr][d] = valid ? __ldcs(a.m[kXIX + 3 * rr + d] + pidx) : T(0);
+        for (int d = 0; d < 3; ++d) Jd[rr][d] = valid ? __ldcs(a.m[kXIX + 3 * rr + d] + pidx) : T(0);
       if (valid) {
-        jac = __ldcs(a.m[kJAC] + pidx);
-        l2m = __ldcs(a.m[kL2M] + pidx);
-        mu = __ldcs(a.m[kMU] + pidx);
+        jd = __ldcs(a.m[kJAC] + pidx);
+        ld = __ldcs(a.m[kL2M] + pidx);
+        md = __ldcs(a.m[kMU] + pidx);
+      }
+    };
+    if constexpr (PIPE) load_geom(0, Jn, jacn, l2mn, mun);
+#pragma unroll
+    for (int kk = 0; kk < H; ++kk) {
+      const int k = k0 + kk;
+      T J[3][3], jac = T(0), l2m = T(0), mu = T(0);
+      if constexpr (PIPE) {
+#pragma unroll
+        for (int rr = 0; rr < 3; ++rr)
+#pragma unroll
+          for (int d = 0; d < 3; ++d) J[rr][d] = Jn[rr][d];
+        jac = jacn;
+        l2m = l2mn;
+        mu = mun;
+        if (kk + 1 < H) load_geom(kk + 1, Jn, jacn, l2mn, mun);
+      } else {
+        load_geom(kk, J, jac, l2m, mu);
       }
       T dxi[3], det[3], dg[3];
 #pragma unroll

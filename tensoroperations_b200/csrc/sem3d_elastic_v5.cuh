@@ -99,7 +99,15 @@ struct Sem3dV5Args {
 // bulk copies also overlap A and B1, measured 0.597 vs 0.592 ms and was
 // removed.)
 //   kV5Ranges    the element ranges of Sem3dV5Args::rg with ticketed batches.
-enum : int { kV5Packed = 2, kV5Ranges = 4 };
+//   kV5WarpAgg   warp-aggregated scatter-add (assembled): the point (le, j, i=4, k)
+//                and (le+1, j, i=0, k) of x-adjacent elements are one node; when
+//                the two owners sit in one warp (lanes 21 apart) and ibool gives
+//                them the same node, the i=4 owner adds its partner's
+//                contribution (one shuffle per component) and only it issues the
+//                atomic.  Opt-in (TO_SEM3D_WARP_AGG=1): it removes about 6 % of
+//                the atomics but the shuffles cost more of the L1 pipe than they
+//                save (64^3, interleaved: 0.550 vs 0.497 ms).
+enum : int { kV5Packed = 2, kV5Ranges = 4, kV5WarpAgg = 8 };
 
 // IL: assembled u and f interleaved per node (x, y, z, unused) -- one 128-bit
 // gather and one 128-bit atomicAdd per point instead of three of each.
@@ -109,6 +117,7 @@ __global__ void __launch_bounds__(EB * 25, MINB)
   const Sem3dArgs<float, 5>& a = args.a;
   constexpr bool kPk = (OPT & kV5Packed) != 0;
   constexpr bool kRg = (OPT & kV5Ranges) != 0;
+  constexpr bool kAgg = ASM && (OPT & kV5WarpAgg) != 0;
   using LY = Sem3dV5Layout<EB, ASM>;
   constexpr int N = 5, NN = 25, P = 125, NT = LY::NT, EP = LY::EP;
   constexpr int SKX = LY::SKX, SKE = LY::SKE;
@@ -474,7 +483,27 @@ __global__ void __launch_bounds__(EB * 25, MINB)
           const float te = RDE[c * CE + k * SKE + tid];
           fc[c] = fmaf(wij, g, fmaf(wik, te, wjk * tx));
         }
-        if (valid) {
+        bool issue = valid;
+        if constexpr (kAgg) {
+          // x-face partners: lane + 21 holds (le+1, j, 0) when this is (le, j, 4);
+          // they are combined only when ibool gives them the same node (any mesh)
+          const int lane = tid & 31;
+          const unsigned mask = __activemask();
+          float pv[3];
+#pragma unroll
+          for (int c = 0; c < 3; ++c) pv[c] = __shfl_down_sync(mask, fc[c], 21);
+          const int pnode = __shfl_down_sync(mask, node[k], 21);  // partner's node
+          const int onode = __shfl_up_sync(mask, node[k], 21);    // owner's node
+          const bool owner = rb == N - 1 && lane + 21 < 32 && tid + 21 < NT &&
+                             le + 1 < batch_elems(b) && pnode == node[k];
+          if (owner) {
+#pragma unroll
+            for (int c = 0; c < 3; ++c) fc[c] += pv[c];
+          }
+          if (rb == 0 && le >= 1 && lane >= 21 && onode == node[k])
+            issue = false;  // the owner (lane - 21) adds it
+        }
+        if (issue) {
           if (ASM && IL) {
             atomicAdd(reinterpret_cast<float4*>(a.f[0]) + node[k],
                       make_float4(fc[0], fc[1], fc[2], 0.f));

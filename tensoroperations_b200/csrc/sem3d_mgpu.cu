@@ -302,4 +302,52 @@ int to_sem3d_elastic_mgpu(const to_sem3d_plan* plan, const to_sem3d_fields* fiel
   return ok();
 }
 
+int to_sem3d_elastic_mgpu_host(const to_sem3d_plan* plan, const to_sem3d_fields* fields,
+                               const to_slab* slab, ncclComm_t comm, const to_host_nodes* host,
+                               void* compute_stream, void* comm_stream) {
+  if (!plan || !fields || !slab || !host)
+    return set_error(TO_ERR_INVALID_ARGUMENT, "to_sem3d_elastic_mgpu_host: null argument");
+  const to_sem3d_desc& d = *sem3d_plan_desc(plan);
+  const bool il = d.node_layout == 1;
+  const size_t vb = d.dtype == TO_F64 ? 8 : 4;
+  const size_t bytes = vb * static_cast<size_t>(d.nglob);
+  for (int c = 0; c < 3; ++c) {
+    if (!host->u[c] || !host->f[c])
+      return set_error(TO_ERR_INVALID_ARGUMENT, "to_sem3d_elastic_mgpu_host: null host array");
+    if (il && !host->stage[c])
+      return set_error(TO_ERR_INVALID_ARGUMENT,
+                       "to_sem3d_elastic_mgpu_host: interleaved nodes need three stage arrays");
+  }
+  if (!fields->u[0] || !fields->f[0])
+    return set_error(TO_ERR_INVALID_ARGUMENT, "to_sem3d_elastic_mgpu_host: null device u / f");
+  cudaStream_t cs = static_cast<cudaStream_t>(compute_stream);
+  // copy in (and interleave)
+  for (int c = 0; c < 3; ++c) {
+    void* dst = il ? host->stage[c] : const_cast<void*>(fields->u[c]);
+    TO_CUDA_TRY(cudaMemcpyAsync(dst, host->u[c], bytes, cudaMemcpyHostToDevice, cs));
+  }
+  if (il) {
+    const float* x[3] = {static_cast<const float*>(host->stage[0]),
+                         static_cast<const float*>(host->stage[1]),
+                         static_cast<const float*>(host->stage[2])};
+    if (int st = to_nodes_interleave(x, static_cast<float*>(const_cast<void*>(fields->u[0])),
+                                     d.nglob, cs))
+      return st;
+  }
+  if (int st = to_sem3d_elastic_mgpu(plan, fields, slab, comm, compute_stream, comm_stream))
+    return st;
+  // (de-interleave and) copy out
+  if (il) {
+    float* x[3] = {static_cast<float*>(host->stage[0]), static_cast<float*>(host->stage[1]),
+                   static_cast<float*>(host->stage[2])};
+    if (int st = to_nodes_deinterleave(static_cast<const float*>(fields->f[0]), x, d.nglob, cs))
+      return st;
+  }
+  for (int c = 0; c < 3; ++c) {
+    const void* src = il ? host->stage[c] : fields->f[c];
+    TO_CUDA_TRY(cudaMemcpyAsync(host->f[c], src, bytes, cudaMemcpyDeviceToHost, cs));
+  }
+  return ok();
+}
+
 }  // extern "C"

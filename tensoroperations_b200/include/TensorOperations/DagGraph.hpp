@@ -29,6 +29,9 @@
 #include <TensorOperations/LevelGraph.hpp>
 #include <TensorOperations/Tiling.hpp>
 #include <TensorOperations/b200/Dag.hpp>
+#if defined(__CUDACC__)
+#include <TensorOperations/b200/SemFusedDag.hpp>
+#endif
 #include <TensorOperations/b200/TcContract.hpp>
 
 namespace TensorOperations {
@@ -184,6 +187,19 @@ struct DagGraph {
           "DagGraph: a node's mode is either tiled differently from the grid node's or is "
           "multi-tiled and absent from it, so its tile index cannot be gathered from the grid "
           "node's. Retile so every shared mode matches and every unshared mode has one tile.");
+#if defined(__CUDACC__)
+    // the spectral-element stiffness shape: one fused line-owner kernel that
+    // calls this graph's combine functors (b200/SemFusedDag.hpp)
+    if constexpr (b200::SemDagShape<NodesT, Roots...>::ok) {
+      cudaError_t fe = cudaSuccess;
+      const int league = b200::sem_fused_dag_launch<ValueType, NodesT, Roots...>(nodes, &fe, views...);
+      if (league >= 0) {
+        if (fe != cudaSuccess)
+          throw LevelGraphError(TO_ERR_CUDA, std::string("DagGraph fused launch: ") + cudaGetErrorString(fe));
+        return league;
+      }
+    }
+#endif
     if constexpr (b200::tc_candidate<NodesT, ValueType>() && sizeof...(ViewTs) == 1) {
       // one large fp32 contraction of two inputs: a GEMM on the tensor cores
       const int league = b200::tc_try_contract(nodes.template get<0>(), views...);

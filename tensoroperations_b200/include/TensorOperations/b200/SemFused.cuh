@@ -62,6 +62,17 @@ struct SemTables {
   int d_at[4][3] = {};   // [axis][slot] -> divergence member
   int s_in[3][3] = {};   // final combine r, operand q -> divergence member
   int s_root[3] = {};    // final combine r -> position of its slot in Roots
+  // The kernel reads the tables below, which both spellings fill.  Physical
+  // axes: 0 the element, 1..3 the field views' other dimensions (k, j, i).
+  int nops = 0;          // operators in constant memory; gradient m uses g_op[m],
+                         // divergence m uses d_op[m]
+  int nint = 0;          // integrand combines (the nine gradients in, nine fluxes out)
+  int i_in[3][9] = {};   // integrand c, operand q -> gradient member
+  int i_nout[3] = {};    // integrand c: outputs
+  int i_out_div[3][9] = {};  // integrand c, output o -> divergence member
+  int i_coord[3][4] = {};    // integrand c: physical axis of its functor coordinate t
+  int s_coord[3][4] = {};    // final combine r: the same for its coordinates (and root view)
+  int g_node[9] = {}, i_node[3] = {}, d_node[9] = {}, s_node[3] = {};  // DAG node indices
 };
 
 template <class A>
@@ -317,6 +328,17 @@ struct SemShape {
         for (int d = 1; d < 4; ++d)
           if (LT::is_gridded(F[d]) || LT::tile(F[d]) != N) fail(t, ok, 100);
         walk(t, ok, F, std::make_index_sequence<9>{});
+        t.nops = 2;
+        t.nint = 1;
+        t.i_nout[0] = 9;
+        for (int q = 0; q < 9; ++q) {
+          t.i_in[0][q] = t.c_in[q];
+          t.i_out_div[0][q] = t.d_of_src[q];
+        }
+        for (int d = 0; d < 4; ++d) {
+          t.i_coord[0][d] = d;
+          for (int r = 0; r < 3; ++r) t.s_coord[r][d] = d;
+        }
         t.ok = ok;
         return t;
       }
@@ -329,10 +351,42 @@ struct SemShape {
 
 // ---- the kernel ----------------------------------------------------------------
 
-// The two operators of the running launch, [op][o][p], row-major (per
-// translation unit; written by the launch, stream-ordered before the kernel).
-static __constant__ float sem_fused_ops_f32[2][5][5];
-static __constant__ double sem_fused_ops_f64[2][5][5];
+// The operators of the running launch, [op][o][p], row-major: two for a
+// LevelGraph (its level-0 stages), eighteen for a DagGraph (gradient m uses
+// operator m, divergence m operator 9 + m).  Per translation unit; gathered by
+// sem_fused_gather_ops into the staging array and copied here by the launch,
+// stream-ordered before the kernel.
+inline constexpr int kSemFusedMaxOps = 18;
+static __constant__ float sem_fused_ops_f32[kSemFusedMaxOps][5][5];
+static __constant__ double sem_fused_ops_f64[kSemFusedMaxOps][5][5];
+static __device__ float sem_fused_stage_f32[kSemFusedMaxOps * 25];
+static __device__ double sem_fused_stage_f64[kSemFusedMaxOps * 25];
+
+template <class V>
+struct SemOpPtrs {
+  const V* p[kSemFusedMaxOps];
+};
+
+template <class V>
+__global__ void sem_fused_gather_ops(const SemOpPtrs<V> ops, int nops) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= nops * 25) return;
+  if constexpr (std::is_same_v<V, float>)
+    sem_fused_stage_f32[t] = ops.p[t / 25][t % 25];
+  else
+    sem_fused_stage_f64[t] = ops.p[t / 25][t % 25];
+}
+
+// What the kernel reads besides the operators: the three field views (indexed
+// by the physical axes element, k, j, i), the integrand combine functors and
+// the three root combine functors -- copied out of the graph so the kernel's
+// parameters hold nothing else.
+template <class Fields, class Ints, class Sums>
+struct SemFusedSource {
+  Fields fields;
+  Ints ints;
+  Sums sums;
+};
 
 // Coefficient Op(o, p) of operator OP, transposed when TR: every index is a
 // compile-time constant once the loops are unrolled, so it is an immediate
@@ -370,9 +424,29 @@ __device__ __forceinline__ void sem_line(const V* in, V* out) {
 // Every table lookup below happens at compile time (static_for indices and
 // constexpr locals); a run-time index into the tables would put them in local
 // memory.
-template <class V, class Pat, class Levels, class Views>
-__global__ void __launch_bounds__(SemFusedLayout::NT, 2)
-    sem_fused_level_kernel(const Levels levels, const Views views, long long nelem) {
+// Resident CTAs per SM the kernel is compiled for (register budget), and the
+// points per group of functor calls in phase B2.
+#ifndef TO_SEM_FUSED_MIN_BLOCKS
+#define TO_SEM_FUSED_MIN_BLOCKS 2
+#endif
+#ifndef TO_SEM_FUSED_B2_GROUP
+#define TO_SEM_FUSED_B2_GROUP 1
+#endif
+
+// Integrand combine C at one point: its coordinates in its own label order,
+// its nine gradient operands in its own operand order.
+template <class Pat, int C, class Fn, class V, std::size_t... Q>
+__device__ __forceinline__ auto sem_call_integrand(const Fn& fn, const int (&P)[4], const V (&g)[9],
+                                                   std::index_sequence<Q...>) {
+  constexpr int c0 = Pat::tables.i_coord[C][0], c1 = Pat::tables.i_coord[C][1];
+  constexpr int c2 = Pat::tables.i_coord[C][2], c3 = Pat::tables.i_coord[C][3];
+  constexpr int q[9] = {Pat::tables.i_in[C][Q]...};
+  return fn(P[c0], P[c1], P[c2], P[c3], g[q[Q]]...);
+}
+
+template <class V, class Pat, class Src, class Views>
+__global__ void __launch_bounds__(SemFusedLayout::NT, TO_SEM_FUSED_MIN_BLOCKS)
+    sem_fused_kernel(const Src src, const Views views, long long nelem) {
   using LY = SemFusedLayout;
   constexpr int N = LY::N, NN = LY::NN, EB = LY::EB;
   constexpr int SKX = LY::SKX, SKE = LY::SKE, CX = LY::CX, CE = LY::CE;
@@ -388,11 +462,6 @@ __global__ void __launch_bounds__(SemFusedLayout::NT, 2)
   const int lx = rb * SKX + le * NN + ra * N;  // x3-line (k = rb, j = ra): + i
   const int ly = ra * SKE + le * NN + rb;      // x2-line (k = ra, i = rb): + N j
 
-  const auto& lv1 = levels.template get<1>();
-  const auto& lv3 = levels.template get<3>();
-  const auto& lv5 = levels.template get<5>();
-  const auto& integrand = lv3.template get<0>().fn;
-
   for (long long b = blockIdx.x; b * EB < nelem; b += gridDim.x) {
     const long long e = b * EB + le;
     const bool valid = e < nelem;
@@ -402,7 +471,7 @@ __global__ void __launch_bounds__(SemFusedLayout::NT, 2)
     V dg[3][N];
     static_for<3>([&](auto cc) {
       constexpr int c = decltype(cc)::value;
-      const auto& u = lv1.template get<c>().operand_.handle.tensor;
+      const auto& u = src.fields.template get<c>();
       V uc[N];
 #pragma unroll
       for (int k = 0; k < N; ++k) uc[k] = valid ? static_cast<V>(u(ei, k, ra, rb)) : V(0);
@@ -436,43 +505,67 @@ __global__ void __launch_bounds__(SemFusedLayout::NT, 2)
     });
     __syncthreads();
 
-    // ---- B2: the nine-output combine at every point of the column ----
+    // ---- B2: the integrand combines at every point of the column ----
+    // All nine gradients of a point are read before any flux is stored (the
+    // fluxes go to the same places, and every integrand reads all nine).
+    // Points go in groups of TO_SEM_FUSED_B2_GROUP: every functor call of the
+    // group is made before any flux is stored, so the functors' own global
+    // loads (through generic pointers, which the compiler may not move across
+    // a shared-memory store) of the whole group are in flight together.
     V Fg[3][N];
-#pragma unroll
-    for (int k = 0; k < N; ++k) {
-      V g[9];
-      static_for<9>([&](auto qq) {
-        constexpr int q = decltype(qq)::value;
-        constexpr int m = Pat::tables.c_in[q];
-        constexpr int comp = Pat::tables.g_comp[m], ax = Pat::tables.g_axis[m];
-        if constexpr (ax == 3)
-          g[q] = X[comp * CX + k * SKX + tid];
-        else if constexpr (ax == 2)
-          g[q] = E[comp * CE + k * SKE + tid];
-        else
-          g[q] = dg[comp][k];
+    constexpr int KG = TO_SEM_FUSED_B2_GROUP;
+    static_for<(N + KG - 1) / KG>([&](auto gg) {
+      constexpr int k0 = decltype(gg)::value * KG;
+      constexpr int nk = (N - k0 < KG) ? (N - k0) : KG;
+      V F[nk][9];  // [point][divergence member]
+      static_for<nk>([&](auto kk) {
+        constexpr int k = k0 + decltype(kk)::value;
+        V g[9];  // [gradient member]
+        static_for<9>([&](auto mm) {
+          constexpr int m = decltype(mm)::value;
+          constexpr int comp = Pat::tables.g_comp[m], ax = Pat::tables.g_axis[m];
+          if constexpr (ax == 3)
+            g[m] = X[comp * CX + k * SKX + tid];
+          else if constexpr (ax == 2)
+            g[m] = E[comp * CE + k * SKE + tid];
+          else
+            g[m] = dg[comp][k];
+        });
+        const int P[4] = {ei, k, ra, rb};
+        static_for<Pat::tables.nint>([&](auto ci) {
+          constexpr int c = decltype(ci)::value;
+          constexpr int nout = Pat::tables.i_nout[c];
+          if (valid) {
+            const auto r = sem_call_integrand<Pat, c>(src.ints.template get<c>(), P, g,
+                                                      std::make_index_sequence<9>{});
+            static_for<nout>([&](auto oo) {
+              constexpr int o = decltype(oo)::value;
+              constexpr int md = Pat::tables.i_out_div[c][o];
+              F[decltype(kk)::value][md] = static_cast<V>(r[o]);
+            });
+          } else {
+            static_for<nout>([&](auto oo) {
+              constexpr int o = decltype(oo)::value;
+              constexpr int md = Pat::tables.i_out_div[c][o];
+              F[decltype(kk)::value][md] = V(0);
+            });
+          }
+        });
       });
-      V F[9];
-      if (valid) {
-        const auto r = integrand(ei, k, ra, rb, g[0], g[1], g[2], g[3], g[4], g[5], g[6], g[7], g[8]);
-#pragma unroll
-        for (int o = 0; o < 9; ++o) F[o] = static_cast<V>(r[o]);
-      } else {
-#pragma unroll
-        for (int o = 0; o < 9; ++o) F[o] = V(0);
-      }
-      static_for<9>([&](auto oo) {
-        constexpr int o = decltype(oo)::value;
-        constexpr int md = Pat::tables.d_of_src[o];
-        constexpr int ax = Pat::tables.d_axis[md], sl = Pat::tables.d_slot[md];
-        if constexpr (ax == 3)
-          X[sl * CX + k * SKX + tid] = F[o];
-        else if constexpr (ax == 2)
-          E[sl * CE + k * SKE + tid] = F[o];
-        else
-          Fg[sl][k] = F[o];
+      static_for<nk>([&](auto kk) {
+        constexpr int k = k0 + decltype(kk)::value;
+        static_for<9>([&](auto mm) {
+          constexpr int md = decltype(mm)::value;
+          constexpr int ax = Pat::tables.d_axis[md], sl = Pat::tables.d_slot[md];
+          if constexpr (ax == 3)
+            X[sl * CX + k * SKX + tid] = F[decltype(kk)::value][md];
+          else if constexpr (ax == 2)
+            E[sl * CE + k * SKE + tid] = F[decltype(kk)::value][md];
+          else
+            Fg[sl][k] = F[decltype(kk)::value][md];
+        });
       });
-    }
+    });
     __syncthreads();
 
     // ---- C1: divergences along x3 and x2, in place ----
@@ -495,7 +588,7 @@ __global__ void __launch_bounds__(SemFusedLayout::NT, 2)
     });
     __syncthreads();
 
-    // ---- C2: divergences along x1, the three combines, the roots ----
+    // ---- C2: divergences along x1, the three root combines, the roots ----
     V tgc[3][N];
     static_for<3>([&](auto ss) {
       constexpr int sl = decltype(ss)::value;
@@ -504,8 +597,11 @@ __global__ void __launch_bounds__(SemFusedLayout::NT, 2)
     });
 #pragma unroll
     for (int k = 0; k < N; ++k) {
+      const int P[4] = {ei, k, ra, rb};
       static_for<3>([&](auto rr) {
         constexpr int R = decltype(rr)::value;
+        constexpr int s0 = Pat::tables.s_coord[R][0], s1 = Pat::tables.s_coord[R][1];
+        constexpr int s2 = Pat::tables.s_coord[R][2], s3 = Pat::tables.s_coord[R][3];
         V t3[3];
         static_for<3>([&](auto qq) {
           constexpr int q = decltype(qq)::value;
@@ -519,8 +615,9 @@ __global__ void __launch_bounds__(SemFusedLayout::NT, 2)
             t3[q] = tgc[sl][k];
         });
         if (valid) {
-          const V r = static_cast<V>(lv5.template get<R>().fn(ei, k, ra, rb, t3[0], t3[1], t3[2]));
-          views.template get<Pat::tables.s_root[R]>()(ei, k, ra, rb) = r;
+          const V r = static_cast<V>(
+              src.sums.template get<R>()(P[s0], P[s1], P[s2], P[s3], t3[0], t3[1], t3[2]));
+          views.template get<Pat::tables.s_root[R]>()(P[s0], P[s1], P[s2], P[s3]) = r;
         }
       });
     }
@@ -528,9 +625,93 @@ __global__ void __launch_bounds__(SemFusedLayout::NT, 2)
   }
 }
 
-// Fused launch, or false when this graph / these views do not qualify (the
-// caller then runs the generic evaluator).  Throws nothing; CUDA errors come
-// back as the status in *err.
+// Fused launches made by this process (the tests check which route ran).
+inline long long& sem_fused_launch_count() {
+  static long long n = 0;
+  return n;
+}
+
+// The launch both spellings share, once the graph and its views qualify:
+// gathers the operators into constant memory and launches the fused kernel on
+// the legacy default stream, one CTA per batch up to the resident limit.
+// Returns the CUDA status.
+template <class V, class Pat, class Src, class Views>
+cudaError_t sem_fused_run(const Src& src, const Views& views, long long nelem,
+                          const SemOpPtrs<V>& ops, int nops) {
+  using LY = SemFusedLayout;
+  constexpr std::size_t smem = LY::bytes<V>();
+  auto kernel = sem_fused_kernel<V, Pat, Src, Views>;
+  int dev = 0, sms = 0, nb = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if ((err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+    return err;
+  if (smem > 48 * 1024 &&
+      (err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(smem))) != cudaSuccess)
+    return err;
+  if ((err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kernel, LY::NT, smem)) != cudaSuccess)
+    return err;
+  sem_fused_gather_ops<V><<<(nops * 25 + 127) / 128, 128, 0, 0>>>(ops, nops);
+  if ((err = cudaGetLastError()) != cudaSuccess) return err;
+  void* stage = nullptr;
+  if constexpr (std::is_same_v<V, float>) {
+    if ((err = cudaGetSymbolAddress(&stage, sem_fused_stage_f32)) != cudaSuccess) return err;
+    err = cudaMemcpyToSymbolAsync(sem_fused_ops_f32, stage, nops * 25 * sizeof(V), 0,
+                                  cudaMemcpyDeviceToDevice, 0);
+  } else {
+    if ((err = cudaGetSymbolAddress(&stage, sem_fused_stage_f64)) != cudaSuccess) return err;
+    err = cudaMemcpyToSymbolAsync(sem_fused_ops_f64, stage, nops * 25 * sizeof(V), 0,
+                                  cudaMemcpyDeviceToDevice, 0);
+  }
+  if (err != cudaSuccess) return err;
+  const long long nbatch = (nelem + LY::EB - 1) / LY::EB;
+  const long long cap = static_cast<long long>(sms) * (nb > 0 ? nb : 1);
+  const int grid = static_cast<int>(nbatch < cap ? nbatch : cap);
+  kernel<<<grid, LY::NT, smem, 0>>>(src, views, nelem);
+  err = cudaGetLastError();
+  if (err == cudaSuccess) ++sem_fused_launch_count();
+  return err;
+}
+
+inline bool sem_fused_enabled() {
+  static const bool enabled = [] {
+    const char* e = std::getenv("TO_LEVELGRAPH_FUSED");
+    return !(e && std::strcmp(e, "0") == 0);
+  }();
+  return enabled;
+}
+
+// A dense row-major 5 x 5 view.
+template <class H>
+bool sem_dense_operator(const H& h) {
+  return h.extent(0) == 5 && h.extent(1) == 5 && h.stride(0) == 5 && h.stride(1) == 1;
+}
+
+// Root view R of extents (nelem, 5, 5, 5) in physical order, permuted by the
+// root combine's coordinate order sc.
+template <class F>
+bool sem_root_extents(const F& f, const int (&sc)[4], long long nelem) {
+  bool ok = true;
+  for (int t = 0; t < 4; ++t) {
+    const long long want = sc[t] == 0 ? nelem : 5;
+    ok = ok && static_cast<long long>(f.extent(t)) == want;
+  }
+  return ok;
+}
+
+// Every root view: root combine r writes view s_root[r] in its own coordinate order.
+template <class Pat, class Views>
+bool sem_roots_fit(const Views& views, long long nelem) {
+  return [&]<std::size_t... R>(std::index_sequence<R...>) {
+    return (sem_root_extents(views.template get<Pat::tables.s_root[R]>(), Pat::tables.s_coord[R], nelem) &&
+            ...);
+  }(std::make_index_sequence<3>{});
+}
+
+// Fused launch of a LevelGraph, or false when this graph / these views do not
+// qualify (the caller then runs the generic evaluator).  Throws nothing; CUDA
+// errors come back as the status in *err.
 template <class V, class LT, class Levels, class Views, std::size_t... Roots>
 bool sem_fused_launch(const Levels& levels, const Views& views, long long nelem, cudaError_t* err) {
   using Pat = SemShape<LT, Levels, Roots...>;
@@ -538,71 +719,46 @@ bool sem_fused_launch(const Levels& levels, const Views& views, long long nelem,
   if constexpr (!Pat::ok || !(std::is_same_v<V, float> || std::is_same_v<V, double>)) {
     return false;
   } else {
-    static const bool enabled = [] {
-      const char* e = std::getenv("TO_LEVELGRAPH_FUSED");
-      return !(e && std::strcmp(e, "0") == 0);
-    }();
-    if (!enabled) return false;
+    if (!sem_fused_enabled()) return false;
     // every field and root: whole labels exactly 5; operators dense row-major 5 x 5
     bool shapes = true;
+    const auto& lv1 = levels.template get<1>();
     [&]<std::size_t... C>(std::index_sequence<C...>) {
       (
           [&] {
-            const auto& u = levels.template get<1>().template get<C>().operand_.handle.tensor;
+            const auto& u = lv1.template get<C>().operand_.handle.tensor;
             shapes = shapes && static_cast<long long>(u.extent(0)) == nelem;
             for (int d = 1; d < 4; ++d) shapes = shapes && u.extent(d) == 5;
           }(),
           ...);
     }(std::make_index_sequence<3>{});
-    [&]<std::size_t... R>(std::index_sequence<R...>) {
-      (
-          [&] {
-            const auto& f = views.template get<R>();
-            shapes = shapes && static_cast<long long>(f.extent(0)) == nelem;
-            for (int d = 1; d < 4; ++d) shapes = shapes && f.extent(d) == 5;
-          }(),
-          ...);
-    }(std::make_index_sequence<3>{});
-    const V* opdata[2] = {nullptr, nullptr};
+    shapes = shapes && sem_roots_fit<Pat>(views, nelem);
+    SemOpPtrs<V> ops{};
     [&]<std::size_t... S>(std::index_sequence<S...>) {
       (
           [&] {
             const auto& h = levels.template get<0>().template get<S>().operand_.handle.tensor;
-            shapes = shapes && h.extent(0) == 5 && h.extent(1) == 5 && h.stride(0) == 5 &&
-                     h.stride(1) == 1;
-            opdata[S] = reinterpret_cast<const V*>(h.data());
+            shapes = shapes && sem_dense_operator(h);
+            ops.p[S] = reinterpret_cast<const V*>(h.data());
           }(),
           ...);
     }(std::make_index_sequence<2>{});
     if (!shapes || nelem <= 0) return false;
-    using LY = SemFusedLayout;
-    constexpr std::size_t smem = LY::bytes<V>();
-    auto kernel = sem_fused_level_kernel<V, Pat, Levels, Views>;
-    int dev = 0, sms = 0, nb = 0;
-    if ((*err = cudaGetDevice(&dev)) != cudaSuccess) return true;
-    if ((*err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
-      return true;
-    if (smem > 48 * 1024 &&
-        (*err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(smem))) != cudaSuccess)
-      return true;
-    if ((*err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kernel, LY::NT, smem)) !=
-        cudaSuccess)
-      return true;
-    for (int s = 0; s < 2; ++s) {
-      if constexpr (std::is_same_v<V, float>)
-        *err = cudaMemcpyToSymbolAsync(sem_fused_ops_f32, opdata[s], 25 * sizeof(V),
-                                       s * 25 * sizeof(V), cudaMemcpyDeviceToDevice, 0);
-      else
-        *err = cudaMemcpyToSymbolAsync(sem_fused_ops_f64, opdata[s], 25 * sizeof(V),
-                                       s * 25 * sizeof(V), cudaMemcpyDeviceToDevice, 0);
-      if (*err != cudaSuccess) return true;
-    }
-    const long long nbatch = (nelem + LY::EB - 1) / LY::EB;
-    const long long cap = static_cast<long long>(sms) * (nb > 0 ? nb : 1);
-    const int grid = static_cast<int>(nbatch < cap ? nbatch : cap);
-    kernel<<<grid, LY::NT, smem, 0>>>(levels, views, nelem);
-    *err = cudaGetLastError();
+    const auto& lv3 = levels.template get<3>();
+    const auto& lv5 = levels.template get<5>();
+    using FieldsT = DeviceTuple<std::decay_t<decltype(lv1.template get<0>().operand_.handle.tensor)>,
+                                std::decay_t<decltype(lv1.template get<1>().operand_.handle.tensor)>,
+                                std::decay_t<decltype(lv1.template get<2>().operand_.handle.tensor)>>;
+    using IntsT = DeviceTuple<std::decay_t<decltype(lv3.template get<0>().fn)>>;
+    using SumsT = DeviceTuple<std::decay_t<decltype(lv5.template get<0>().fn)>,
+                              std::decay_t<decltype(lv5.template get<1>().fn)>,
+                              std::decay_t<decltype(lv5.template get<2>().fn)>>;
+    const SemFusedSource<FieldsT, IntsT, SumsT> src{
+        FieldsT(lv1.template get<0>().operand_.handle.tensor, lv1.template get<1>().operand_.handle.tensor,
+                lv1.template get<2>().operand_.handle.tensor),
+        IntsT(lv3.template get<0>().fn),
+        SumsT(lv5.template get<0>().fn, lv5.template get<1>().fn, lv5.template get<2>().fn)};
+    *err = sem_fused_run<V, Pat>(src, views, nelem, ops, Pat::tables.nops);
     return true;
   }
 }

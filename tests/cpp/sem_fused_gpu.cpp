@@ -1,4 +1,4 @@
-// sem_fused_gpu.cpp -- TEST ONLY: LevelGraphs with the spectral-element
+// sem_fused_gpu.cpp -- TEST ONLY: LevelGraphs and DagGraphs with the spectral-element
 // stiffness shape through the public API, run on the GPU and compared with a
 // double-precision host loop of the same operator.
 //
@@ -11,15 +11,24 @@
 //             and outputs permuted (its functor permutes back), the second
 //             operator staged as H^T-weighted in (r,p) labels and used
 //             transposed, the roots designated out of order;
-// and the compile-time check that both are recognised.  E = 37 elements (a
-// partial last batch), TE = 1 and 2.  Max abs error / max abs value < 1e-5.
+// and the compile-time check that both are recognised.  Three DagGraph
+// spellings of it (DagGraph.hpp takes the same fused kernel through
+// b200/SemFusedDag.hpp): three direction integrands with their coordinates in
+// their own label order, one nine-output integrand with the nodes in another
+// topological order, and one whose directions name the fields in different
+// orders, which must fall back to the generic evaluator.  E = 37 elements (a
+// partial last batch), TE = 1 and 2.  Max abs error / max abs value < 1e-5,
+// and the route taken (fused or generic) is the expected one.
 #include <Kokkos_Core.hpp>
+#include <TensorOperations/DagGraph.hpp>
 #include <TensorOperations/LevelGraph.hpp>
 #include <TensorOperations/LevelPlan.hpp>
 
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
+#include <utility>
 
 using namespace TensorOperations;
 using ES = Kokkos::DefaultExecutionSpace;
@@ -30,7 +39,7 @@ using V1 = Kokkos::View<float*, Kokkos::LayoutRight>;
 
 struct Fields {
   V4 u[3], m[12], f[3];
-  V2 H, Hw, HwT;  // HwT(r,p) = Hw(p,r)
+  V2 H, Hw, HwT, HT;  // HwT(r,p) = Hw(p,r), HT(r,p) = H(p,r)
   V1 w;
 };
 
@@ -49,6 +58,7 @@ static Fields make_fields(int E) {
   d.H = V2("H", N, N);
   d.Hw = V2("Hw", N, N);
   d.HwT = V2("HwT", N, N);
+  d.HT = V2("HT", N, N);
   d.w = V1("w", N);
   auto fill4 = [&](V4 v, int s, float base) {
     auto h = Kokkos::create_mirror_view(v);
@@ -63,10 +73,13 @@ static Fields make_fields(int E) {
   auto hH = Kokkos::create_mirror_view(d.H);
   auto hW = Kokkos::create_mirror_view(d.Hw);
   auto hT = Kokkos::create_mirror_view(d.HwT);
+  auto hHT = Kokkos::create_mirror_view(d.HT);
   auto hw = Kokkos::create_mirror_view(d.w);
   for (int a = 0; a < N; ++a) hw(a) = 0.2f + 0.05f * a;
   for (int a = 0; a < N; ++a)
     for (int b = 0; b < N; ++b) hH(a, b) = 0.3f * std::sin(1.3f * a + 0.7f * b) + (a == b ? 0.1f : 0.f);
+  for (int a = 0; a < N; ++a)
+    for (int b = 0; b < N; ++b) hHT(b, a) = hH(a, b);
   for (int a = 0; a < N; ++a)
     for (int b = 0; b < N; ++b) {
       hW(a, b) = hH(b, a) * hw(b);
@@ -75,6 +88,7 @@ static Fields make_fields(int E) {
   Kokkos::deep_copy(d.H, hH);
   Kokkos::deep_copy(d.Hw, hW);
   Kokkos::deep_copy(d.HwT, hT);
+  Kokkos::deep_copy(d.HT, hHT);
   Kokkos::deep_copy(d.w, hw);
   return d;
 }
@@ -232,6 +246,217 @@ void shuffled(const Fields& d) {
   g6.outputs(s1, s0, s2).team_size(64).execute(TeamPolicyTag2<ES>{}, d.f[1], d.f[0], d.f[2]);
 }
 
+// ---- the same operator as a DagGraph ---------------------------------------
+// Integrand of one reference direction R (0 xi, 1 eta, 2 gamma): a DAG combine
+// receives its coordinates in its output label order, here (q, e, a, b) with
+// q the direction's own axis; it returns the direction's three fluxes.
+template <int R>
+struct DirIntegrand {
+  Integrand in;
+  KOKKOS_FUNCTION Kokkos::Array<float, 3> operator()(int q, int e, int a, int b, float x0, float x1,
+                                                     float x2, float y0, float y1, float y2, float z0,
+                                                     float z1, float z2) const {
+    int k = a, j = b, i = q;
+    if constexpr (R == 1) {
+      j = q;
+      i = b;
+    } else if constexpr (R == 2) {
+      k = q;
+      j = a;
+      i = b;
+    }
+    const auto r = in(e, k, j, i, x0, x1, x2, y0, y1, y2, z0, z1, z2);
+    return {r[3 * R], r[3 * R + 1], r[3 * R + 2]};
+  }
+};
+
+template <int TE>
+struct DagTiles {
+  using T2 = StaticTile<N, N>;
+  using TE4 = StaticTile<TE, N, N, N>;  // (e, k, j, i)
+  using TQ4 = StaticTile<N, TE, N, N>;  // (q, e, ., .): an operator's free label first
+  using Grad = Tile<T2, TE4, TQ4>;
+  using Div3 = Tile<T2, TQ4, TE4>;      // of a three-output integrand's flux
+  using Div9 = Tile<T2, TE4, TE4>;      // of the nine-output integrand's flux
+  using Comb3 = CombineTile<TQ4, TQ4, TQ4, TQ4, TQ4, TQ4, TQ4, TQ4, TQ4, TQ4>;
+  using Comb9 = CombineTile<TE4, TE4, TE4, TE4, TE4, TE4, TE4, TE4, TE4, TE4>;
+  using Sum = CombineTile<TE4, TE4, TE4, TE4>;
+};
+
+// Gradient builders: the storage is (operator's free label, e, the others).
+// `T` picks the transposed operator HT(p, q) = H(q, p).
+template <bool T>
+auto dag_op(const Fields& d) {
+  if constexpr (T)
+    return make_input_node(make_handle<'p', 'q'>(d.HT));
+  else
+    return make_input_node(make_handle<'q', 'p'>(d.H));
+}
+template <bool T = false>
+auto dgx(const Fields& d, V4 u) {
+  return make_contraction_node<'q', 'e', 'k', 'j'>(dag_op<T>(d), make_input_node(make_handle<'e', 'k', 'j', 'p'>(u)));
+}
+template <bool T = false>
+auto dge(const Fields& d, V4 u) {
+  return make_contraction_node<'q', 'e', 'k', 'i'>(dag_op<T>(d), make_input_node(make_handle<'e', 'k', 'p', 'i'>(u)));
+}
+template <bool T = false>
+auto dgg(const Fields& d, V4 u) {
+  return make_contraction_node<'q', 'e', 'j', 'i'>(dag_op<T>(d), make_input_node(make_handle<'e', 'p', 'j', 'i'>(u)));
+}
+
+template <bool S, class A, class B>
+auto ordered(const A& a, const B& b) {
+  if constexpr (S)
+    return std::make_pair(b, a);
+  else
+    return std::make_pair(a, b);
+}
+
+// Three integrands (one per direction), nodes added field by field, the eta
+// gradients through HT, the integrands in the order gamma, xi, eta, the
+// divergences partly through HwT, the roots designated out of order.  `Swap`
+// lists the eta gradients of u0 and u1 the other way round: each direction
+// then names the fields in a different order, which the fused route does not
+// take (the launch falls back to the generic evaluator).
+template <int TE, bool Swap = false>
+void dag_three(const Fields& d) {
+  using T = DagTiles<TE>;
+  const WeightedSum ws{d};
+  const Integrand in{d};
+  auto [d0, x0] = make_dag<float, ES>().add(dgx(d, d.u[0]), typename T::Grad{});
+  auto [d1, y0] = d0.add(dge<true>(d, d.u[Swap ? 1 : 0]), typename T::Grad{});
+  auto [d2, z0] = d1.add(dgg(d, d.u[0]), typename T::Grad{});
+  auto [d3, x1] = d2.add(dgx(d, d.u[1]), typename T::Grad{});
+  auto [d4, y1] = d3.add(dge<true>(d, d.u[Swap ? 0 : 1]), typename T::Grad{});
+  auto [d5, z1] = d4.add(dgg(d, d.u[1]), typename T::Grad{});
+  auto [d6, x2] = d5.add(dgx(d, d.u[2]), typename T::Grad{});
+  auto [d7, y2] = d6.add(dge<true>(d, d.u[2]), typename T::Grad{});
+  auto [d8, z2] = d7.add(dgg(d, d.u[2]), typename T::Grad{});
+  // the eta gradients of u0 and u1, in field order either way
+  const auto [e0, e1] = ordered<Swap>(y0, y1);
+  auto [d9, g0, g1, g2] = d8.add(
+      make_combine_node<'q', 'e', 'j', 'i'>(
+          x0.template as<'i', 'e', 'q', 'j'>(), x1.template as<'i', 'e', 'q', 'j'>(),
+          x2.template as<'i', 'e', 'q', 'j'>(), e0.template as<'j', 'e', 'q', 'i'>(),
+          e1.template as<'j', 'e', 'q', 'i'>(), y2.template as<'j', 'e', 'q', 'i'>(),
+          z0.template as<'q', 'e', 'j', 'i'>(), z1.template as<'q', 'e', 'j', 'i'>(),
+          z2.template as<'q', 'e', 'j', 'i'>(), DirIntegrand<2>{in}),
+      typename T::Comb3{});
+  auto [d10, a0, a1, a2] = d9.add(
+      make_combine_node<'q', 'e', 'k', 'j'>(
+          x0.template as<'q', 'e', 'k', 'j'>(), x1.template as<'q', 'e', 'k', 'j'>(),
+          x2.template as<'q', 'e', 'k', 'j'>(), e0.template as<'j', 'e', 'k', 'q'>(),
+          e1.template as<'j', 'e', 'k', 'q'>(), y2.template as<'j', 'e', 'k', 'q'>(),
+          z0.template as<'k', 'e', 'j', 'q'>(), z1.template as<'k', 'e', 'j', 'q'>(),
+          z2.template as<'k', 'e', 'j', 'q'>(), DirIntegrand<0>{in}),
+      typename T::Comb3{});
+  auto [d11, b0, b1, b2] = d10.add(
+      make_combine_node<'q', 'e', 'k', 'i'>(
+          x0.template as<'i', 'e', 'k', 'q'>(), x1.template as<'i', 'e', 'k', 'q'>(),
+          x2.template as<'i', 'e', 'k', 'q'>(), e0.template as<'q', 'e', 'k', 'i'>(),
+          e1.template as<'q', 'e', 'k', 'i'>(), y2.template as<'q', 'e', 'k', 'i'>(),
+          z0.template as<'k', 'e', 'q', 'i'>(), z1.template as<'k', 'e', 'q', 'i'>(),
+          z2.template as<'k', 'e', 'q', 'i'>(), DirIntegrand<1>{in}),
+      typename T::Comb3{});
+  // T_x(i) = sum_q Hw(q, i) F(q), through Hw (summed label first) or HwT
+  auto dx = [&](auto f) {
+    return make_contraction_node<'e', 'k', 'j', 'i'>(make_input_node(make_handle<'i', 'q'>(d.HwT)),
+                                                     f.template as<'q', 'e', 'k', 'j'>());
+  };
+  auto de = [&](auto f) {
+    return make_contraction_node<'e', 'k', 'j', 'i'>(make_input_node(make_handle<'q', 'j'>(d.Hw)),
+                                                     f.template as<'q', 'e', 'k', 'i'>());
+  };
+  auto dg = [&](auto f) {
+    return make_contraction_node<'e', 'k', 'j', 'i'>(make_input_node(make_handle<'q', 'k'>(d.Hw)),
+                                                     f.template as<'q', 'e', 'j', 'i'>());
+  };
+  auto [d12, tg2] = d11.add(dg(g2), typename T::Div3{});
+  auto [d13, tx0] = d12.add(dx(a0), typename T::Div3{});
+  auto [d14, te1] = d13.add(de(b1), typename T::Div3{});
+  auto [d15, tx1] = d14.add(dx(a1), typename T::Div3{});
+  auto [d16, tg0] = d15.add(dg(g0), typename T::Div3{});
+  auto [d17, te2] = d16.add(de(b2), typename T::Div3{});
+  auto [d18, te0] = d17.add(de(b0), typename T::Div3{});
+  auto [d19, tx2] = d18.add(dx(a2), typename T::Div3{});
+  auto [d20, tg1] = d19.add(dg(g1), typename T::Div3{});
+  // storage: (i, e, k, j) along xi, (j, e, k, i) along eta, (k, e, j, i) along gamma
+  auto sum = [&](auto tx, auto te, auto tg) {
+    return make_combine_node<'e', 'k', 'j', 'i'>(tx.template as<'i', 'e', 'k', 'j'>(),
+                                                 te.template as<'j', 'e', 'k', 'i'>(),
+                                                 tg.template as<'k', 'e', 'j', 'i'>(), ws);
+  };
+  auto [d21, r2] = d20.add(sum(tx2, te2, tg2), typename T::Sum{});
+  auto [d22, r0] = d21.add(sum(tx0, te0, tg0), typename T::Sum{});
+  auto [d23, r1] = d22.add(sum(tx1, te1, tg1), typename T::Sum{});
+  using Shape = b200::SemDagShape<std::decay_t<decltype(d23.nodes)>, decltype(r1)::slot_index,
+                                  decltype(r2)::slot_index, decltype(r0)::slot_index>;
+  static_assert(Shape::ok, "the three-integrand DAG spelling is recognised");
+  d23.outputs(r1, r2, r0).team_size(64).execute(TeamPolicyTag<ES>{}, d.f[1], d.f[2], d.f[0]);
+}
+
+// One nine-output integrand labelled (e, k, j, i), nodes in another
+// topological order (gradients interleaved by direction, the gamma ones
+// through HT), divergences of the nine fluxes in reverse.
+template <int TE>
+void dag_one(const Fields& d) {
+  using T = DagTiles<TE>;
+  const WeightedSum ws{d};
+  const Integrand in{d};
+  auto [d0, z0] = make_dag<float, ES>().add(dgg<true>(d, d.u[0]), typename T::Grad{});
+  auto [d1, x0] = d0.add(dgx(d, d.u[0]), typename T::Grad{});
+  auto [d2, z1] = d1.add(dgg<true>(d, d.u[1]), typename T::Grad{});
+  auto [d3, y0] = d2.add(dge(d, d.u[0]), typename T::Grad{});
+  auto [d4, x1] = d3.add(dgx(d, d.u[1]), typename T::Grad{});
+  auto [d5, y1] = d4.add(dge(d, d.u[1]), typename T::Grad{});
+  auto [d6, z2] = d5.add(dgg<true>(d, d.u[2]), typename T::Grad{});
+  auto [d7, x2] = d6.add(dgx(d, d.u[2]), typename T::Grad{});
+  auto [d8, y2] = d7.add(dge(d, d.u[2]), typename T::Grad{});
+  auto [d9, f0, f1, f2, f3, f4, f5, f6, f7, f8] = d8.add(
+      make_combine_node<'e', 'k', 'j', 'i'>(
+          x0.template as<'i', 'e', 'k', 'j'>(), x1.template as<'i', 'e', 'k', 'j'>(),
+          x2.template as<'i', 'e', 'k', 'j'>(), y0.template as<'j', 'e', 'k', 'i'>(),
+          y1.template as<'j', 'e', 'k', 'i'>(), y2.template as<'j', 'e', 'k', 'i'>(),
+          z0.template as<'k', 'e', 'j', 'i'>(), z1.template as<'k', 'e', 'j', 'i'>(),
+          z2.template as<'k', 'e', 'j', 'i'>(), in),
+      typename T::Comb9{});
+  // flux F[r][c] is output 3 r + c
+  auto dx = [&](auto f) {
+    return make_contraction_node<'e', 'k', 'j', 'i'>(make_input_node(make_handle<'q', 'i'>(d.Hw)),
+                                                     f.template as<'e', 'k', 'j', 'q'>());
+  };
+  auto de = [&](auto f) {
+    return make_contraction_node<'e', 'k', 'j', 'i'>(make_input_node(make_handle<'j', 'q'>(d.HwT)),
+                                                     f.template as<'e', 'k', 'q', 'i'>());
+  };
+  auto dg = [&](auto f) {
+    return make_contraction_node<'e', 'k', 'j', 'i'>(make_input_node(make_handle<'q', 'k'>(d.Hw)),
+                                                     f.template as<'e', 'q', 'j', 'i'>());
+  };
+  auto [d10, tg2] = d9.add(dg(f8), typename T::Div9{});
+  auto [d11, tg1] = d10.add(dg(f7), typename T::Div9{});
+  auto [d12, tg0] = d11.add(dg(f6), typename T::Div9{});
+  auto [d13, te2] = d12.add(de(f5), typename T::Div9{});
+  auto [d14, te1] = d13.add(de(f4), typename T::Div9{});
+  auto [d15, te0] = d14.add(de(f3), typename T::Div9{});
+  auto [d16, tx2] = d15.add(dx(f2), typename T::Div9{});
+  auto [d17, tx1] = d16.add(dx(f1), typename T::Div9{});
+  auto [d18, tx0] = d17.add(dx(f0), typename T::Div9{});
+  auto sum = [&](auto tx, auto te, auto tg) {
+    return make_combine_node<'e', 'k', 'j', 'i'>(tx.template as<'i', 'e', 'k', 'j'>(),
+                                                 te.template as<'j', 'e', 'k', 'i'>(),
+                                                 tg.template as<'k', 'e', 'j', 'i'>(), ws);
+  };
+  auto [d19, r0] = d18.add(sum(tx0, te0, tg0), typename T::Sum{});
+  auto [d20, r1] = d19.add(sum(tx1, te1, tg1), typename T::Sum{});
+  auto [d21, r2] = d20.add(sum(tx2, te2, tg2), typename T::Sum{});
+  using Shape = b200::SemDagShape<std::decay_t<decltype(d21.nodes)>, decltype(r0)::slot_index,
+                                  decltype(r1)::slot_index, decltype(r2)::slot_index>;
+  static_assert(Shape::ok, "the nine-output DAG spelling is recognised");
+  d21.outputs(r0, r1, r2).team_size(64).execute(TeamPolicyTag<ES>{}, d.f[0], d.f[1], d.f[2]);
+}
+
 // Host reference in double.
 static double check(const Fields& d, int E) {
   auto h = [&](const V4& v) {
@@ -298,19 +523,29 @@ int main(int argc, char** argv) {
   {
     const int E = 37;
     Fields d = make_fields(E);
-    auto run = [&](const char* name, auto fn) {
+    const char* env = std::getenv("TO_LEVELGRAPH_FUSED");
+    const bool enabled = !(env && std::strcmp(env, "0") == 0);
+    // `fused`: the spelling takes the fused kernel when the route is enabled
+    auto run = [&](const char* name, auto fn, bool fused) {
       for (int c = 0; c < 3; ++c) Kokkos::deep_copy(d.f[c], 0.f);
+      const long long before = b200::sem_fused_launch_count();
       fn(d);
       Kokkos::fence();
+      const bool took = b200::sem_fused_launch_count() != before;
       const double rel = check(d, E);
-      const bool ok = rel < 1e-5;
-      std::printf("%-24s max rel err %.3e  %s\n", name, rel, ok ? "PASS" : "FAIL");
+      const bool ok = rel < 1e-5 && took == (fused && enabled);
+      std::printf("%-24s max rel err %.3e  %-7s %s\n", name, rel, took ? "fused" : "generic",
+                  ok ? "PASS" : "FAIL");
       fails += !ok;
     };
-    run("natural TE=1", natural<1>);
-    run("natural TE=2", natural<2>);
-    run("shuffled TE=1", shuffled<1>);
-    run("shuffled TE=2", shuffled<2>);
+    run("natural TE=1", natural<1>, true);
+    run("natural TE=2", natural<2>, true);
+    run("shuffled TE=1", shuffled<1>, true);
+    run("shuffled TE=2", shuffled<2>, true);
+    run("dag three TE=1", dag_three<1>, true);
+    run("dag three TE=2", dag_three<2>, true);
+    run("dag one TE=2", dag_one<2>, true);
+    run("dag fields swapped TE=2", dag_three<2, true>, false);
   }
   Kokkos::finalize();
   std::printf("%s\n", fails ? "SOME FAILED" : "ALL PASS");

@@ -162,3 +162,86 @@ def test_node_layout_round_trip():
     for a, b in zip(x, y):
         assert torch.equal(a, b)
     assert torch.equal(x4[:, 1], x[1]) and float(x4[:, 3].abs().max()) == 0.0
+
+
+_AGG_CHECK = r"""
+import sys, numpy as np, torch
+sys.path.insert(0, sys.argv[1])
+from oracle import sem as osem
+from tensoroperations_b200 import abi
+from tensoroperations_b200.sem3d import structured_problem, to_device
+nex, ney, nez, il = map(int, sys.argv[2:6])
+prob = structured_problem(nex, ney, nez, ngll=5, dtype=np.float32, assembled=True, seed=35)
+u, f, arrays, ibool = to_device(prob, "cuda")
+plan = abi.Sem3dPlan(np.float32, 5, prob.nelem, prob.H, prob.Hw, prob.w, nglob=prob.nglob,
+                     assembled=True, interleaved=bool(il))
+if il:
+    u4 = torch.empty((prob.nglob, 4), device="cuda"); abi.nodes_interleave(u, u4, prob.nglob)
+    f4 = torch.empty((prob.nglob, 4), device="cuda")
+    fl = plan.fields([u4, None, None], [f4, None, None], arrays, ibool)
+else:
+    fl = plan.fields(u, f, arrays, ibool)
+sl = abi.Slab(); sl.prev = sl.next = -1; sl.layer_elems = nex * ney
+sl.plane_nodes = (nex * 4 + 1) * (ney * 4 + 1)
+sync = torch.zeros(abi.slab_sync_bytes(), dtype=torch.uint8, device="cuda"); sl.sync = sync.data_ptr()
+abi.sem3d_elastic_mgpu(plan, fl, sl, None, 0, 0)
+if il:
+    abi.nodes_deinterleave(f4, f, prob.nglob)
+torch.cuda.synchronize()
+got = [x.cpu().numpy() for x in f]
+ref = osem.assembled(prob.nelem, 5, prob.nglob, prob.ibool, prob.u, prob.arrays, prob.H, prob.Hw,
+                     prob.w, np.float32)
+err = osem.rel_l2(got, ref)
+print("rel", err)
+sys.exit(0 if err < 1e-5 else 1)
+"""
+
+
+@pytest.mark.parametrize("mesh", [(8, 3, 2), (5, 4, 3), (12, 2, 2)])
+@pytest.mark.parametrize("il", [0, 1])
+def test_warp_aggregated_scatter(mesh, il):
+    """TO_SEM3D_WARP_AGG=1: x-face partners summed by a shuffle before the atomic;
+    rows of 5 elements (an x-row boundary inside a batch) check that only
+    equal nodes are combined."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parent.parent
+    env = dict(os.environ, TO_SEM3D_WARP_AGG="1")
+    r = subprocess.run([sys.executable, "-c", _AGG_CHECK, str(root), *map(str, mesh), str(il)],
+                       capture_output=True, text=True, timeout=300, env=env)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+
+
+@pytest.mark.parametrize("il", [False, True])
+def test_host_buffer_entry(il):
+    """to_sem3d_elastic_mgpu_host: host u in, host f out (one array per
+    component), with the device layout conversion inside the call."""
+    import torch
+    nex, ney, nez = 4, 3, 5
+    prob = structured_problem(nex, ney, nez, ngll=N, dtype=np.float32, assembled=True, seed=36)
+    _, f, arrays, ibool = to_device(prob, "cuda")
+    plan = abi.Sem3dPlan(np.float32, N, prob.nelem, prob.H, prob.Hw, prob.w, nglob=prob.nglob,
+                         assembled=True, interleaved=il)
+    u_host = [torch.from_numpy(x).pin_memory() for x in prob.u]
+    f_host = [torch.full((prob.nglob,), 5.0).pin_memory() for _ in range(3)]
+    if il:
+        du = [torch.empty((prob.nglob, 4), device="cuda"), None, None]
+        df = [torch.empty((prob.nglob, 4), device="cuda"), None, None]
+        stage = [torch.empty(prob.nglob, device="cuda") for _ in range(3)]
+    else:
+        du = [torch.empty(prob.nglob, device="cuda") for _ in range(3)]
+        df = f
+        stage = [None] * 3
+    sl, keep, _ = _slab(torch, nex, ney, -1, -1)
+    h = abi.HostNodes()
+    for c in range(3):
+        h.u[c], h.f[c] = u_host[c].data_ptr(), f_host[c].data_ptr()
+        h.stage[c] = stage[c].data_ptr() if stage[c] is not None else None
+    s = torch.cuda.Stream()
+    abi.sem3d_elastic_mgpu_host(plan, plan.fields(du, df, arrays, ibool), sl, None, h,
+                                s.cuda_stream, s.cuda_stream)
+    s.synchronize()
+    got = [x.numpy() for x in f_host]
+    assert osem.rel_l2(got, _oracle(prob)) < TOL
