@@ -161,6 +161,13 @@ typedef struct to_sem3d_fields {
   const void* etax; const void* etay; const void* etaz;
   const void* gamx; const void* gamy; const void* gamz;
   const void* jac;  const void* l2m;  const void* mu;
+  /* Assembled mode, optional (NULL: none): DEVICE double; every gathered u
+   * value is read as u * (1 / sqrt(*u_norm2)), the product taken in double
+   * and rounded once -- what to_scale3 writes, so a power iteration can keep
+   * the unnormalised K u and fold the normalisation into the next
+   * application (one pass over u and f less per step).  Appended last: a
+   * zero-initialised struct has none. */
+  const double* u_norm2;
 } to_sem3d_fields;
 
 typedef struct to_sem3d_plan to_sem3d_plan;
@@ -221,6 +228,7 @@ int to_sem3d_halo_accumulate(int32_t dtype, void* const f[3], int64_t offset, in
  * counterpart in the reference (it has no assembled fields). */
 int to_nodes_interleave(const float* const x[3], float* out, int64_t n, void* stream);
 int to_nodes_deinterleave(const float* in, float* const x[3], int64_t n, void* stream);
+
 
 /* ---------------------------------------------------------------------- */
 /* Z-slab operator over NCCL (one rank per GPU)                            */

@@ -63,7 +63,12 @@ POINT_ARRAYS = ("xix", "xiy", "xiz", "etax", "etay", "etaz", "gamx", "gamy", "ga
 
 class Sem3dFields(C.Structure):
     _fields_ = [("u", C.c_void_p * 3), ("f", C.c_void_p * 3), ("ibool", C.c_void_p)] + \
-        [(n, C.c_void_p) for n in POINT_ARRAYS]
+        [(n, C.c_void_p) for n in POINT_ARRAYS] + [("u_norm2", C.c_void_p)]
+
+    def copy(self) -> "Sem3dFields":
+        out = Sem3dFields()
+        C.pointer(out)[0] = self
+        return out
 
 
 class Sem2dFields(C.Structure):

@@ -96,6 +96,7 @@ Sem3dArgs<T, N> make_args(const to_sem3d_plan* plan, const to_sem3d_fields* fl) 
     a.f[c] = static_cast<T*>(fl->f[c]);
   }
   a.ibool = fl->ibool;
+  a.u_norm2 = plan->desc.assembled ? fl->u_norm2 : nullptr;
   const void* m[kNumPointArrays] = {fl->xix,  fl->xiy,  fl->xiz,  fl->etax,
                                     fl->etay, fl->etaz, fl->gamx, fl->gamy,
                                     fl->gamz, fl->jac,  fl->l2m,  fl->mu};
@@ -216,13 +217,13 @@ int launch_v5(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t
 
 // The line-owner kernel over up to two element ranges with ticketed batches
 // (f32 NGLL 5, assembled, either node layout; the z-slab operator's launches).
-template <bool IL, int OPT = kV5Packed | kV5Ranges>
+template <bool IL, int OPT = kV5Packed | kV5Ranges, int EB = 8, int MINB = 3>
 int launch_v5_ranges(const to_sem3d_plan* plan, const to_sem3d_fields* fl, const int64_t first[2],
                      const int64_t count[2], unsigned long long* ticket, cudaStream_t stream,
                      int dev, int sms) {
-  constexpr int EB = 8, NT = EB * 25;
+  constexpr int NT = EB * 25;
   const size_t smem = Sem3dV5Layout<EB, true>::kTotal;
-  auto kernel = sem3d_elastic_v5_kernel<EB, 3, true, IL, OPT>;
+  auto kernel = sem3d_elastic_v5_kernel<EB, MINB, true, IL, OPT>;
   static KernelSlot slot;
   int nb = 0;
   if (int st = configure(slot, kernel, dev, NT, smem, &nb)) return st;
@@ -276,18 +277,22 @@ int launch_hc(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t
               int dev, int sms) {
   constexpr int NT = EB * 128;
   const size_t smem = Sem3dHcLayout<T, EB>::kTotal;
-  auto kernel = sem3d_elastic_hc_kernel<T, EB, MINB, ASM, PIPE>;
-  static KernelSlot slot;
-  int nb = 0;
-  if (int st = configure(slot, kernel, dev, NT, smem, &nb)) return st;
   Sem3dArgs<T, 8> a = make_args<T, 8>(plan, fl);
   a.prefetch = staged_arrays_aligned(fl, ASM) ? 1 : 0;
-  const long long nbatch = (plan->desc.nelem + EB - 1) / EB;
-  const long long cap = static_cast<long long>(sms) * nb;
-  const int grid = static_cast<int>(nbatch < cap ? nbatch : cap);
-  kernel<<<grid, NT, smem, stream>>>(a);
-  TO_CUDA_TRY(cudaGetLastError());
-  return ok();
+  auto go = [&](auto kernel, KernelSlot& slot) -> int {
+    int nb = 0;
+    if (int st = configure(slot, kernel, dev, NT, smem, &nb)) return st;
+    const long long nbatch = (plan->desc.nelem + EB - 1) / EB;
+    const long long cap = static_cast<long long>(sms) * nb;
+    const int grid = static_cast<int>(nbatch < cap ? nbatch : cap);
+    kernel<<<grid, NT, smem, stream>>>(a);
+    TO_CUDA_TRY(cudaGetLastError());
+    return ok();
+  };
+  static KernelSlot slot, slot_scaled;
+  if (ASM && a.u_norm2)
+    return go(sem3d_elastic_hc_kernel<T, EB, MINB, ASM, PIPE, true>, slot_scaled);
+  return go(sem3d_elastic_hc_kernel<T, EB, MINB, ASM, PIPE, false>, slot);
 }
 
 // Kernel variant for f32 NGLL 5 (TO_SEM3D_VARIANT; default 5):
@@ -307,6 +312,16 @@ int sem3d_f32_variant() {
   return v;
 }
 
+// Elements per batch of the ticketed launches: 8 (3 CTAs of 200 threads per SM)
+// or 12 (TO_SEM3D_EB=12: 2 CTAs of 300 threads).
+int sem3d_batch_elems() {
+  static const int eb = [] {
+    const char* e = std::getenv("TO_SEM3D_EB");
+    return e && std::atoi(e) == 12 ? 12 : 8;
+  }();
+  return eb;
+}
+
 // Warp-aggregated scatter-add in the ticketed launches (TO_SEM3D_WARP_AGG=1).
 bool sem3d_warp_agg() {
   static const bool on = [] {
@@ -322,6 +337,13 @@ int launch_sem3d(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStrea
   const int sms = device_sm_count(&dev);
   if (sms <= 0) return -sms;
   if constexpr (std::is_same_v<T, float> && N == 5 && ASM) {
+    // u_norm2 (a power iteration's deferred normalisation) is read by the
+    // NGLL-8 kernels and the generic one, not by the NGLL-5 line-owner kernel
+    if (fl->u_norm2) {
+      if (plan->desc.node_layout == 1)
+        return set_error(TO_ERR_UNSUPPORTED, "to_sem3d_apply: u_norm2 with interleaved nodes");
+      return launch_ldg<T, N, ASM>(plan, fl, stream, dev, sms);
+    }
     if (plan->desc.node_layout == 1) {
       if (!staged_arrays_aligned(fl, ASM))
         return set_error(TO_ERR_ALIGNMENT,
@@ -377,6 +399,10 @@ int apply_typed(const to_sem3d_plan* plan, const to_sem3d_fields* fl, int accumu
       return set_error(TO_ERR_ALIGNMENT, "to_sem3d_apply: field pointer %p not %zu-byte aligned",
                        p, need);
   }
+  if (fl->u_norm2 && !plan->desc.assembled)
+    return set_error(TO_ERR_UNSUPPORTED, "to_sem3d_apply: u_norm2 needs assembled mode");
+  if (fl->u_norm2 && !aligned(fl->u_norm2, 8))
+    return set_error(TO_ERR_ALIGNMENT, "to_sem3d_apply: u_norm2 not 8-byte aligned");
   if (plan->desc.assembled) {
     if (!fl->ibool)
       return set_error(TO_ERR_INVALID_ARGUMENT, "to_sem3d_apply: assembled mode needs ibool");
@@ -427,8 +453,10 @@ int sem3d_apply_ranges(const to_sem3d_plan* plan, const to_sem3d_fields* fl,
   for (int r = 0; r < 2; ++r)
     if (count[r] && first[r] % 4 != 0) starts4 = false;
   const bool il = d.node_layout == 1;
-  const bool fast = d.dtype == TO_F32 && d.ngll == 5 && d.assembled && ticket != nullptr &&
-                    (il || sem3d_f32_variant() == 5) && starts4 &&
+  if (fl->u_norm2 && il)
+    return set_error(TO_ERR_UNSUPPORTED, "sem3d ranges: u_norm2 with interleaved nodes");
+  const bool fast = !fl->u_norm2 && d.dtype == TO_F32 && d.ngll == 5 && d.assembled &&
+                    ticket != nullptr && (il || sem3d_f32_variant() == 5) && starts4 &&
                     staged_arrays_aligned(fl, true) && aligned(ticket, 8);
   if (il && !fast)
     return set_error(TO_ERR_ALIGNMENT,
@@ -450,6 +478,11 @@ int sem3d_apply_ranges(const to_sem3d_plan* plan, const to_sem3d_fields* fl,
       constexpr int kAggOpt = kV5Packed | kV5Ranges | kV5WarpAgg;
       if (il) return launch_v5_ranges<true, kAggOpt>(plan, fl, first, count, ticket, stream, dev, sms);
       return launch_v5_ranges<false, kAggOpt>(plan, fl, first, count, ticket, stream, dev, sms);
+    }
+    if (sem3d_batch_elems() == 12) {
+      constexpr int kOpt = kV5Packed | kV5Ranges;
+      if (il) return launch_v5_ranges<true, kOpt, 12, 2>(plan, fl, first, count, ticket, stream, dev, sms);
+      return launch_v5_ranges<false, kOpt, 12, 2>(plan, fl, first, count, ticket, stream, dev, sms);
     }
     if (il) return launch_v5_ranges<true>(plan, fl, first, count, ticket, stream, dev, sms);
     return launch_v5_ranges<false>(plan, fl, first, count, ticket, stream, dev, sms);

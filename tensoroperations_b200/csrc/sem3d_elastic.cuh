@@ -45,7 +45,20 @@ struct Sem3dArgs {
   long long nelem;
   int prefetch;  // 1 if every streamed array is 16-byte aligned
   Sem3dOps<T, N> ops;
+  // assembled mode, optional: every gathered u value is multiplied by
+  // 1 / sqrt(*u_norm2) (computed and applied in double, as to_scale3 does)
+  const double* u_norm2;
 };
+
+// The factor of Sem3dArgs::u_norm2 (1 without it).
+__device__ __forceinline__ double sem_u_factor(const double* u_norm2) {
+  return u_norm2 ? 1.0 / sqrt(*u_norm2) : 1.0;
+}
+// x times the factor, rounded once to T (x itself when there is no factor).
+template <typename T>
+__device__ __forceinline__ T sem_u_scaled(T x, double s, bool scaled) {
+  return scaled ? static_cast<T>(static_cast<double>(x) * s) : x;
+}
 
 // Issue an L2 bulk prefetch of `bytes` (rounded down to 16) at `p`.
 __device__ __forceinline__ void l2_prefetch(const void* p, long long bytes) {
@@ -139,6 +152,8 @@ __global__ void __launch_bounds__(EB* N* N, 1)
     const long long base = e * P + ji;  // point (k=0, j, i); +k*NN per level
 
     // ---- stage u: gather (assembled) or stream (element-local) ----
+    const bool uscaled = ASSEMBLED && a.u_norm2 != nullptr;
+    const double usf = uscaled ? sem_u_factor(a.u_norm2) : 1.0;
     T uc[3][N];
 #pragma unroll
     for (int k = 0; k < N; ++k) {
@@ -146,7 +161,8 @@ __global__ void __launch_bounds__(EB* N* N, 1)
         const int node = valid ? __ldg(a.ibool + base + k * NN) : 0;
         snode[k * NT + tid] = node;
 #pragma unroll
-        for (int c = 0; c < 3; ++c) uc[c][k] = valid ? __ldg(a.u[c] + node) : T(0);
+        for (int c = 0; c < 3; ++c)
+          uc[c][k] = valid ? sem_u_scaled(__ldg(a.u[c] + node), usf, uscaled) : T(0);
       } else {
 #pragma unroll
         for (int c = 0; c < 3; ++c)

@@ -47,7 +47,10 @@ struct Sem3dHcLayout {
 // computed, so its twelve loads are in flight during that point's physics and
 // ahead of its shared-memory stores (which the compiler may not move loads
 // through generic pointers across).
-template <typename T, int EB, int MINB, bool ASM, bool PIPE = false>
+// SCALE: u is read times 1 / sqrt(*a.u_norm2) (assembled); thread 0 computes
+// the factor once into shared memory, so the batches only add a broadcast
+// load and one multiply per gathered value.
+template <typename T, int EB, int MINB, bool ASM, bool PIPE = false, bool SCALE = false>
 __global__ void __launch_bounds__(EB * 128, MINB)
     sem3d_elastic_hc_kernel(const __grid_constant__ Sem3dArgs<T, 8> a) {
   using LY = Sem3dHcLayout<T, EB>;
@@ -92,6 +95,11 @@ __global__ void __launch_bounds__(EB * 128, MINB)
   const T wi = a.ops.w[rb];
   const T wj = a.ops.w[ra];
   const T wij = wi * wj;
+  __shared__ double s_ufac;
+  if constexpr (SCALE) {
+    if (tid == 0) s_ufac = sem_u_factor(a.u_norm2);
+    __syncthreads();
+  }
   if (tid == 0) prefetch_batch(blockIdx.x);
 
   for (long long b = blockIdx.x; b < nbatch; b += G) {
@@ -118,7 +126,8 @@ __global__ void __launch_bounds__(EB * 128, MINB)
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
           if constexpr (ASM)
-            uc[c][kk] = valid ? __ldg(a.u[c] + node[kk]) : T(0);
+            uc[c][kk] = valid ? sem_u_scaled(__ldg(a.u[c] + node[kk]), SCALE ? s_ufac : 1.0, SCALE)
+                              : T(0);
           else
             uc[c][kk] = valid ? __ldcs(a.u[c] + base + (k0 + kk) * NN) : T(0);
         }

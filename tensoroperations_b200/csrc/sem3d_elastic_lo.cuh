@@ -94,10 +94,13 @@ __global__ void __launch_bounds__(EB * N * N, MINB)
       const long long base = e * P + ab;
 #pragma unroll
       for (int k = 0; k < N; ++k) node_n[k] = v ? __ldg(a.ibool + base + k * NN) : 0;
+      const bool uscaled = ASM && a.u_norm2 != nullptr;
+      const double usf = uscaled ? sem_u_factor(a.u_norm2) : 1.0;
 #pragma unroll
       for (int k = 0; k < N; ++k)
 #pragma unroll
-        for (int c = 0; c < 3; ++c) uc_n[c][k] = v ? __ldg(a.u[c] + node_n[k]) : T(0);
+        for (int c = 0; c < 3; ++c)
+          uc_n[c][k] = v ? sem_u_scaled(__ldg(a.u[c] + node_n[k]), usf, uscaled) : T(0);
     }
   };
   if (tid == 0) prefetch_batch(blockIdx.x);
@@ -124,10 +127,13 @@ __global__ void __launch_bounds__(EB * N * N, MINB)
       } else if constexpr (ASM) {
 #pragma unroll
         for (int k = 0; k < N; ++k) node[k] = valid ? __ldg(a.ibool + base + k * NN) : 0;
+        const bool uscaled = a.u_norm2 != nullptr;
+        const double usf = uscaled ? sem_u_factor(a.u_norm2) : 1.0;
 #pragma unroll
         for (int k = 0; k < N; ++k)
 #pragma unroll
-          for (int c = 0; c < 3; ++c) uc[c][k] = valid ? __ldg(a.u[c] + node[k]) : T(0);
+          for (int c = 0; c < 3; ++c)
+            uc[c][k] = valid ? sem_u_scaled(__ldg(a.u[c] + node[k]), usf, uscaled) : T(0);
       } else {
 #pragma unroll
         for (int k = 0; k < N; ++k) {

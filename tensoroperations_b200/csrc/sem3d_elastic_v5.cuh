@@ -351,6 +351,16 @@ __global__ void __launch_bounds__(EB * 25, MINB)
     // ---- B2: column Integrand9 (k-pairs in packed lanes) -> FX, FE ----
     float Fg[3][N];
     {
+      // the staged geometry of point k of this column: J[r][d], jac, l2m, mu
+      auto geom = [&](int k, float (&J)[3][3], float& jac, float& l2m, float& mu) {
+#pragma unroll
+        for (int r = 0; r < 3; ++r)
+#pragma unroll
+          for (int d = 0; d < 3; ++d) J[r][d] = stage[size_t(kXIX + 3 * r + d) * EP + spt + k * NN];
+        jac = stage[size_t(kJAC) * EP + spt + k * NN];
+        l2m = stage[size_t(kL2M) * EP + spt + k * NN];
+        mu = stage[size_t(kMU) * EP + spt + k * NN];
+      };
       auto point_pair = [&](int k0, int k1) {
         V2<float> dxi[3], det[3], dg[3], J[3][3];
 #pragma unroll
@@ -359,20 +369,16 @@ __global__ void __launch_bounds__(EB * 25, MINB)
           det[c] = mk2(RDE[c * CE + k0 * SKE + tid], RDE[c * CE + k1 * SKE + tid]);
           dg[c] = mk2(dgm[c][k0], dgm[c][k1]);
         }
+        float J0[3][3], J1[3][3], jac0, jac1, l2m0, l2m1, mu0, mu1;
+        geom(k0, J0, jac0, l2m0, mu0);
+        geom(k1, J1, jac1, l2m1, mu1);
 #pragma unroll
         for (int r = 0; r < 3; ++r)
 #pragma unroll
-          for (int d = 0; d < 3; ++d) {
-            const float* q = stage + size_t(kXIX + 3 * r + d) * EP + spt;
-            J[r][d] = mk2(q[k0 * NN], q[k1 * NN]);
-          }
-        const float* qj = stage + size_t(kJAC) * EP + spt;
-        const float* ql = stage + size_t(kL2M) * EP + spt;
-        const float* qm = stage + size_t(kMU) * EP + spt;
+          for (int d = 0; d < 3; ++d) J[r][d] = mk2(J0[r][d], J1[r][d]);
         V2<float> F[3][3];
-        integrand9_lanes<V2<float>, float>(dxi, det, dg, J, mk2(ql[k0 * NN], ql[k1 * NN]),
-                                           mk2(qm[k0 * NN], qm[k1 * NN]),
-                                           mk2(qj[k0 * NN], qj[k1 * NN]), F);
+        integrand9_lanes<V2<float>, float>(dxi, det, dg, J, mk2(l2m0, l2m1), mk2(mu0, mu1),
+                                           mk2(jac0, jac1), F);
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
           RX[c * CX + k0 * SKX + tid] = F[0][c].v.x;
@@ -394,14 +400,10 @@ __global__ void __launch_bounds__(EB * 25, MINB)
           det[c] = RDE[c * CE + k * SKE + tid];
           dg[c] = dgm[c][k];
         }
-#pragma unroll
-        for (int r = 0; r < 3; ++r)
-#pragma unroll
-          for (int d = 0; d < 3; ++d) J[r][d] = stage[size_t(kXIX + 3 * r + d) * EP + spt + k * NN];
+        float jac, l2m, mu;
+        geom(k, J, jac, l2m, mu);
         float F[3][3];
-        integrand9_lanes<float, float>(dxi, det, dg, J, stage[size_t(kL2M) * EP + spt + k * NN],
-                                       stage[size_t(kMU) * EP + spt + k * NN],
-                                       stage[size_t(kJAC) * EP + spt + k * NN], F);
+        integrand9_lanes<float, float>(dxi, det, dg, J, l2m, mu, jac, F);
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
           RX[c * CX + k * SKX + tid] = F[0][c];

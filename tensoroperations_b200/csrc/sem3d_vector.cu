@@ -45,13 +45,43 @@ __global__ void __launch_bounds__(kSumThreads)
   const long long total = 3 * n;
   const long long c0 = static_cast<long long>(blockIdx.x) * kSumChunk;
   const long long c1 = c0 + kSumChunk < total ? c0 + kSumChunk : total;
-  double acc = 0.0;
-  for (long long t = c0 + threadIdx.x; t < c1; t += kSumThreads) {
-    const int c = static_cast<int>(t / n);
-    const double v = static_cast<double>(f.x[c][first + (t - c * n)]);
-    acc = fma(v, v, acc);
+  // The chunk meets at most three components, each a contiguous run walked
+  // without a division per value.  In each run, thread tid takes the values
+  // t = s0' + 256 j (s0' its first index there, j = 0, 1, ...) into
+  // accumulator j % 4 -- four loads in flight -- and the four are added in a
+  // fixed order at the end: the grouping depends on n, first and the chunk
+  // only.
+  double acc[4] = {0.0, 0.0, 0.0, 0.0};
+  for (int c = static_cast<int>(c0 / n); c < 3 && static_cast<long long>(c) * n < c1; ++c) {
+    const long long s0 = c0 > c * n ? c0 : c * n;  // run [s0, s1) of component c
+    const long long s1 = c1 < (c + 1) * n ? c1 : (c + 1) * n;
+    long long t = s0 + ((static_cast<long long>(threadIdx.x) - (s0 - c0)) % kSumThreads +
+                        kSumThreads) % kSumThreads;
+    const T* x = f.x[c] + first - c * n;
+    for (; t + 3 * kSumThreads < s1; t += 4 * kSumThreads) {
+      const double v0 = static_cast<double>(x[t]);
+      const double v1 = static_cast<double>(x[t + kSumThreads]);
+      const double v2 = static_cast<double>(x[t + 2 * kSumThreads]);
+      const double v3 = static_cast<double>(x[t + 3 * kSumThreads]);
+      acc[0] = fma(v0, v0, acc[0]);
+      acc[1] = fma(v1, v1, acc[1]);
+      acc[2] = fma(v2, v2, acc[2]);
+      acc[3] = fma(v3, v3, acc[3]);
+    }
+    if (t < s1) {
+      const double v = static_cast<double>(x[t]);
+      acc[0] = fma(v, v, acc[0]);
+    }
+    if (t + kSumThreads < s1) {
+      const double v = static_cast<double>(x[t + kSumThreads]);
+      acc[1] = fma(v, v, acc[1]);
+    }
+    if (t + 2 * kSumThreads < s1) {
+      const double v = static_cast<double>(x[t + 2 * kSumThreads]);
+      acc[2] = fma(v, v, acc[2]);
+    }
   }
-  const double s = block_sum_fixed(acc, red);
+  const double s = block_sum_fixed((acc[0] + acc[1]) + (acc[2] + acc[3]), red);
   if (threadIdx.x == 0) partial[blockIdx.x] = s;
 }
 

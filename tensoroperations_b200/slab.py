@@ -241,7 +241,12 @@ class SlabOperator:
     power_step(): one step of u <- K u / ||K u|| (the steady-state loop of the
     large configuration): apply, sum of squares over the nodes this rank owns
     (shared planes counted once, by the lower rank), all-reduce of that one
-    double across ranks, and u rescaled on the device -- no host round trip."""
+    double across ranks -- no host round trip.  The division by the norm is
+    folded into the NEXT application (to_sem3d_fields.u_norm2: the operator
+    reads u * 1/sqrt(||f||^2) as it gathers), so a step makes no separate pass
+    over u and f; u and f swap roles every step.  power_u() writes the current
+    iterate, normalised, into the u tensors (the products of a step-by-step
+    rescale, rounded once the same way)."""
 
     def __init__(self, part: SlabPartition, plan, fields, f, device, group=None, u=None,
                  native=None, comm=None):
@@ -262,6 +267,9 @@ class SlabOperator:
         nown = part.nglob - part.owned_first
         self.sumsq_ws = torch.empty(max(1, abi.sumsq3_workspace_bytes(nown)), dtype=torch.uint8,
                                     device=device)
+        self._pw_parity = 0     # the latest unnormalised iterate: 0 in u (or none yet), 1 in f
+        self._pw_pending = False  # an iterate awaits the division by sqrt(sumsq)
+        self._pw_fields = None
         self.comm = None  # this library's NCCL communicator (native, world > 1)
         self._own_comm = False
         if self.native:
@@ -320,30 +328,34 @@ class SlabOperator:
             return (1 if self.boundary else 0) + (1 if self.interior[1] else 0) + k
         return len(self.boundary) + (1 if self.interior[1] else 0) + 2 * k
 
-    def apply(self, stream, events=None):
+    def apply(self, stream, events=None, fields=None, f=None):
         """One application on `stream`; `events` = (start, end) CUDA events are
-        recorded on it around this rank's operator (f's zeroing excluded)."""
+        recorded on it around this rank's operator (f's zeroing excluded).
+        `fields` / `f` replace the operator's own (the power iteration's
+        swapped buffers)."""
+        fields = self.fields if fields is None else fields
+        f_out = self.f if f is None else f
         if self.native:
             import torch
             with torch.cuda.stream(stream):
-                for x in self.f:
+                for x in f_out:
                     x.zero_()
             self.slab.f_is_zero = 1
             if events is not None:
                 events[0].record(stream)
-            abi.sem3d_elastic_mgpu(self.plan, self.fields, self.slab, self.comm,
+            abi.sem3d_elastic_mgpu(self.plan, fields, self.slab, self.comm,
                                    stream.cuda_stream, self.xstream.cuda_stream)
             if events is not None:
                 events[1].record(stream)
             return
         import torch
         s = stream.cuda_stream
-        for x in self.f:
+        for x in f_out:
             x.zero_()
         if events is not None:
             events[0].record(stream)
         for first, count in self.boundary:
-            self.plan.apply_elements(self.fields, first, count, s)
+            self.plan.apply_elements(fields, first, count, s)
         faces = self.part.interfaces()
         if faces:
             self.ev_bnd.record(stream)
@@ -351,32 +363,59 @@ class SlabOperator:
             cs = self.xstream.cuda_stream
             with torch.cuda.stream(self.xstream):
                 for (_, off), buf in zip(faces, self.send):
-                    abi.halo_pack(self.dtype, self.f, off, self.part.plane, buf, cs)
+                    abi.halo_pack(self.dtype, f_out, off, self.part.plane, buf, cs)
                 exchange_planes(self.part, self.send, self.recv, self.group)
                 for (_, off), buf in zip(faces, self.recv):
-                    abi.halo_accumulate(self.dtype, self.f, off, self.part.plane, buf, cs)
+                    abi.halo_accumulate(self.dtype, f_out, off, self.part.plane, buf, cs)
             self.ev_done.record(self.xstream)
         first, count = self.interior
         if count:
-            self.plan.apply_elements(self.fields, first, count, s)
+            self.plan.apply_elements(fields, first, count, s)
         if faces:
             stream.wait_event(self.ev_done)
         if events is not None:
             events[1].record(stream)
 
     def power_step(self, stream, events=None):
+        """f = K u, then ||f||^2 over the ranks into self.sumsq; the next step
+        reads f as its u divided by sqrt(||f||^2) (the buffers swap)."""
         import torch
         import torch.distributed as dist
         if self.u is None:
             raise ValueError("power_step needs the operator's u tensors (SlabOperator(..., u=u))")
-        self.apply(stream, events)
+        if getattr(self.plan, "interleaved", False):
+            raise ValueError("power_step: one array per component (node_layout 0)")
+        if self._pw_fields is None:
+            scaled = self.fields.copy()  # u -> f, u read divided by the norm
+            scaled.u_norm2 = self.sumsq.data_ptr()
+            swapped = scaled.copy()      # f -> u
+            for c in range(3):
+                swapped.u[c], swapped.f[c] = self.fields.f[c], self.fields.u[c]
+            self._pw_fields = (scaled, swapped)
+        if self._pw_parity == 0:
+            fields = self._pw_fields[0] if self._pw_pending else self.fields
+            out = self.f
+        else:
+            fields, out = self._pw_fields[1], self.u
+        self.apply(stream, events, fields, out)
         s = stream.cuda_stream
         first = self.part.owned_first
-        abi.sumsq3(self.dtype, self.f, first, self.part.nglob - first, self.sumsq, self.sumsq_ws, s)
+        abi.sumsq3(self.dtype, out, first, self.part.nglob - first, self.sumsq, self.sumsq_ws, s)
         if self.part.world > 1:
             if self.comm:
                 abi.nccl_allreduce_sum_f64(self.sumsq, 1, self.comm, s)
             else:
                 with torch.cuda.stream(stream):
                     dist.all_reduce(self.sumsq, group=self.group)
-        abi.scale3(self.dtype, self.u, self.f, self.part.nglob, self.sumsq, s)
+        self._pw_parity ^= 1
+        self._pw_pending = True
+
+    def power_u(self, stream):
+        """Write the current iterate K u / ||K u|| into the u tensors (one
+        to_scale3 on `stream`); later steps start from it."""
+        if not self._pw_pending:
+            return
+        src = self.f if self._pw_parity == 1 else self.u
+        abi.scale3(self.dtype, self.u, src, self.part.nglob, self.sumsq, stream.cuda_stream)
+        self._pw_parity = 0
+        self._pw_pending = False

@@ -46,6 +46,7 @@ def main(out_dir, nex, ney, nez, seed, mode="apply", ngll=5):
             else:
                 for _ in range(3):
                     op.power_step(stream)
+                op.power_u(stream)
         torch.cuda.synchronize()
         out = f if mode == "apply" else u
         np.save(os.path.join(out_dir, f"{'f' if mode == 'apply' else 'u'}{rank}.npy"),

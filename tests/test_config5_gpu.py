@@ -128,10 +128,40 @@ def test_power_iteration_single_gpu(ngll):
     with torch.cuda.stream(stream):
         for _ in range(4):
             op.power_step(stream)
+        op.power_u(stream)
     torch.cuda.synchronize()
     ref = _oracle_power(structured_problem(3, 2, 3, ngll=ngll, dtype=np.float64, assembled=True,
                                            seed=55), 4)
     assert osem.rel_l2([x.cpu().numpy() for x in u], ref) < 1e-12
+
+
+@pytest.mark.parametrize("ngll,dtype", [(8, np.float64), (5, np.float64), (5, np.float32)])
+def test_deferred_normalisation_is_bitwise_the_rescale(ngll, dtype):
+    """power_step folds 1/||f|| into the next application's gather: the
+    iterate after 3 steps equals apply + sum of squares + to_scale3 every step
+    (the same products, rounded once) up to the order of the scatter-adds,
+    which the GPU does not fix: relative L2 1e-14 (f64) / 1e-6 (f32)."""
+    torch = _torch()
+    part = SlabPartition(3, 2, 3, ngll, 1, 0)
+    prob = slab_problem(part, dtype, 57)
+    stream = torch.cuda.Stream()
+    u1, f1, arrays, ibool = to_device(prob, "cuda")
+    plan = prob.plan()
+    lazy = SlabOperator(part, plan, plan.fields(u1, f1, arrays, ibool), f1, "cuda", u=u1)
+    u2, f2, _, _ = to_device(prob, "cuda")
+    eager = SlabOperator(part, plan, plan.fields(u2, f2, arrays, ibool), f2, "cuda", u=u2)
+    s = stream.cuda_stream
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            lazy.power_step(stream)
+        lazy.power_u(stream)
+        for _ in range(3):
+            eager.apply(stream)
+            abi.sumsq3(plan.dtype, f2, 0, part.nglob, eager.sumsq, eager.sumsq_ws, s)
+            abi.scale3(plan.dtype, u2, f2, part.nglob, eager.sumsq, s)
+    torch.cuda.synchronize()
+    tol = 1e-14 if dtype == np.float64 else 1e-6
+    assert osem.rel_l2([x.cpu().numpy() for x in u1], [x.cpu().numpy() for x in u2]) < tol
 
 
 @pytest.mark.parametrize("dtype,ngll,world,rank", [(np.float64, 8, 3, 1), (np.float32, 5, 2, 0)])
