@@ -217,13 +217,13 @@ int launch_v5(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t
 
 // The line-owner kernel over up to two element ranges with ticketed batches
 // (f32 NGLL 5, assembled, either node layout; the z-slab operator's launches).
-template <bool IL, int OPT = kV5Packed | kV5Ranges, int EB = 8, int MINB = 3>
+template <bool IL, int OPT = kV5Packed | kV5Ranges>
 int launch_v5_ranges(const to_sem3d_plan* plan, const to_sem3d_fields* fl, const int64_t first[2],
                      const int64_t count[2], unsigned long long* ticket, cudaStream_t stream,
                      int dev, int sms) {
-  constexpr int NT = EB * 25;
+  constexpr int EB = 8, NT = EB * 25;
   const size_t smem = Sem3dV5Layout<EB, true>::kTotal;
-  auto kernel = sem3d_elastic_v5_kernel<EB, MINB, true, IL, OPT>;
+  auto kernel = sem3d_elastic_v5_kernel<EB, 3, true, IL, OPT>;
   static KernelSlot slot;
   int nb = 0;
   if (int st = configure(slot, kernel, dev, NT, smem, &nb)) return st;
@@ -310,16 +310,6 @@ int sem3d_f32_variant() {
     return e ? std::atoi(e) : 5;
   }();
   return v;
-}
-
-// Elements per batch of the ticketed launches: 8 (3 CTAs of 200 threads per SM)
-// or 12 (TO_SEM3D_EB=12: 2 CTAs of 300 threads).
-int sem3d_batch_elems() {
-  static const int eb = [] {
-    const char* e = std::getenv("TO_SEM3D_EB");
-    return e && std::atoi(e) == 12 ? 12 : 8;
-  }();
-  return eb;
 }
 
 // Warp-aggregated scatter-add in the ticketed launches (TO_SEM3D_WARP_AGG=1).
@@ -478,11 +468,6 @@ int sem3d_apply_ranges(const to_sem3d_plan* plan, const to_sem3d_fields* fl,
       constexpr int kAggOpt = kV5Packed | kV5Ranges | kV5WarpAgg;
       if (il) return launch_v5_ranges<true, kAggOpt>(plan, fl, first, count, ticket, stream, dev, sms);
       return launch_v5_ranges<false, kAggOpt>(plan, fl, first, count, ticket, stream, dev, sms);
-    }
-    if (sem3d_batch_elems() == 12) {
-      constexpr int kOpt = kV5Packed | kV5Ranges;
-      if (il) return launch_v5_ranges<true, kOpt, 12, 2>(plan, fl, first, count, ticket, stream, dev, sms);
-      return launch_v5_ranges<false, kOpt, 12, 2>(plan, fl, first, count, ticket, stream, dev, sms);
     }
     if (il) return launch_v5_ranges<true>(plan, fl, first, count, ticket, stream, dev, sms);
     return launch_v5_ranges<false>(plan, fl, first, count, ticket, stream, dev, sms);

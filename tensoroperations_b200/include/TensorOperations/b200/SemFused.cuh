@@ -424,11 +424,23 @@ __device__ __forceinline__ void sem_line(const V* in, V* out) {
 // Every table lookup below happens at compile time (static_for indices and
 // constexpr locals); a run-time index into the tables would put them in local
 // memory.
-// Resident CTAs per SM the kernel is compiled for (register budget), and the
-// points per group of functor calls in phase B2.
-#ifndef TO_SEM_FUSED_MIN_BLOCKS
-#define TO_SEM_FUSED_MIN_BLOCKS 2
+// Resident CTAs per SM the kernel is compiled for (its register budget): one
+// integrand (56 registers, a few bytes of spills) 5 -- 1.788 vs 1.816 ms for the
+// reference's LevelGraph program at E=786,432 --, three integrands (113
+// registers; 80 at 3 CTAs spill 164 bytes) 2.  TO_SEM_FUSED_MIN_BLOCKS
+// overrides both.
+#ifdef TO_SEM_FUSED_MIN_BLOCKS
+template <class Pat>
+constexpr int sem_fused_min_blocks() {
+  return TO_SEM_FUSED_MIN_BLOCKS;
+}
+#else
+template <class Pat>
+constexpr int sem_fused_min_blocks() {
+  return Pat::tables.nint == 1 ? 5 : 2;
+}
 #endif
+// Points per group of functor calls in phase B2.
 #ifndef TO_SEM_FUSED_B2_GROUP
 #define TO_SEM_FUSED_B2_GROUP 1
 #endif
@@ -445,7 +457,7 @@ __device__ __forceinline__ auto sem_call_integrand(const Fn& fn, const int (&P)[
 }
 
 template <class V, class Pat, class Src, class Views>
-__global__ void __launch_bounds__(SemFusedLayout::NT, TO_SEM_FUSED_MIN_BLOCKS)
+__global__ void __launch_bounds__(SemFusedLayout::NT, sem_fused_min_blocks<Pat>())
     sem_fused_kernel(const Src src, const Views views, long long nelem) {
   using LY = SemFusedLayout;
   constexpr int N = LY::N, NN = LY::NN, EB = LY::EB;
