@@ -530,6 +530,17 @@ __global__ void __launch_bounds__(SemFusedLayout::NT, sem_fused_min_blocks<Pat>(
       constexpr int k0 = decltype(gg)::value * KG;
       constexpr int nk = (N - k0 < KG) ? (N - k0) : KG;
       V F[nk][9];  // [point][divergence member]
+      // flux of divergence member md at point k -> its slot
+      auto store_flux = [&](auto mdc, auto kc, V value) {
+        constexpr int md = decltype(mdc)::value, k = decltype(kc)::value;
+        constexpr int ax = Pat::tables.d_axis[md], sl = Pat::tables.d_slot[md];
+        if constexpr (ax == 3)
+          X[sl * CX + k * SKX + tid] = value;
+        else if constexpr (ax == 2)
+          E[sl * CE + k * SKE + tid] = value;
+        else
+          Fg[sl][k] = value;
+      };
       static_for<nk>([&](auto kk) {
         constexpr int k = k0 + decltype(kk)::value;
         V g[9];  // [gradient member]
@@ -567,14 +578,7 @@ __global__ void __launch_bounds__(SemFusedLayout::NT, sem_fused_min_blocks<Pat>(
       static_for<nk>([&](auto kk) {
         constexpr int k = k0 + decltype(kk)::value;
         static_for<9>([&](auto mm) {
-          constexpr int md = decltype(mm)::value;
-          constexpr int ax = Pat::tables.d_axis[md], sl = Pat::tables.d_slot[md];
-          if constexpr (ax == 3)
-            X[sl * CX + k * SKX + tid] = F[decltype(kk)::value][md];
-          else if constexpr (ax == 2)
-            E[sl * CE + k * SKE + tid] = F[decltype(kk)::value][md];
-          else
-            Fg[sl][k] = F[decltype(kk)::value][md];
+          store_flux(mm, std::integral_constant<int, k>{}, F[decltype(kk)::value][decltype(mm)::value]);
         });
       });
     });

@@ -71,6 +71,30 @@ def test_apply_rejects_null_and_misaligned_pointers_before_any_launch():
     assert e.value.status == abi.TO_ERR_ALIGNMENT
 
 
+def test_u_norm2_is_checked_before_any_launch():
+    """The deferred normalisation (to_sem3d_fields.u_norm2) is for assembled
+    plans and wants an 8-byte aligned double."""
+    H, Hw, w = _ops()
+    bogus = 0x1000  # never dereferenced
+    fl = abi.Sem3dFields()
+    for c in range(3):
+        fl.u[c] = bogus
+        fl.f[c] = bogus
+    for n in abi.POINT_ARRAYS:
+        setattr(fl, n, bogus)
+    fl.u_norm2 = bogus
+    local = abi.Sem3dPlan(np.float64, 8, 4, *_ops(8))
+    with pytest.raises(abi.ToError) as e:
+        local.apply(fl)
+    assert e.value.status == abi.TO_ERR_UNSUPPORTED
+    fl.ibool = bogus
+    fl.u_norm2 = bogus + 4
+    asm = abi.Sem3dPlan(np.float64, 8, 4, *_ops(8), nglob=100, assembled=True)
+    with pytest.raises(abi.ToError) as e:
+        asm.apply(fl)
+    assert e.value.status == abi.TO_ERR_ALIGNMENT
+
+
 def test_algorithmic_bytes_and_flops_of_the_bench_config():
     H, Hw, w = _ops()
     E = 64 ** 3
