@@ -414,7 +414,8 @@ class Sem3dPlan:
 
     def __del__(self):
         h = getattr(self, "_h", None)
-        if h is not None and h.value:
+        # at interpreter exit the module's globals may already be cleared
+        if h is not None and h.value and lib is not None:
             lib.to_sem3d_plan_destroy(h)
             self._h = None
 
