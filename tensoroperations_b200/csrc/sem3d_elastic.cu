@@ -278,7 +278,15 @@ int launch_hc(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t
   constexpr int NT = EB * 128;
   const size_t smem = Sem3dHcLayout<T, EB>::kTotal;
   Sem3dArgs<T, 8> a = make_args<T, 8>(plan, fl);
-  a.prefetch = staged_arrays_aligned(fl, ASM) ? 1 : 0;
+  // L2 bulk prefetch of this CTA's next batches (TO_SEM3D_HC_PREFETCH batches
+  // ahead, 0..3): off by default -- 128^3 f64 power step 48.5 ms without it,
+  // 50.4 ms one batch ahead, 56.2 ms two (evict-first hints changed nothing)
+  static const int distance = [] {
+    const char* e = std::getenv("TO_SEM3D_HC_PREFETCH");
+    const int d = e ? std::atoi(e) : 0;
+    return d < 0 ? 0 : (d > 3 ? 3 : d);
+  }();
+  a.prefetch = staged_arrays_aligned(fl, ASM) ? distance : 0;
   auto go = [&](auto kernel, KernelSlot& slot) -> int {
     int nb = 0;
     if (int st = configure(slot, kernel, dev, NT, smem, &nb)) return st;

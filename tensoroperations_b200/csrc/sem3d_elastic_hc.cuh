@@ -77,12 +77,15 @@ __global__ void __launch_bounds__(EB * 128, MINB)
   const long long nbatch = (a.nelem + EB - 1) / EB;
   const long long G = gridDim.x;
 
+  // a.prefetch: how many of this CTA's batches ahead the L2 prefetch runs (0:
+  // none, the default -- see launch_hc)
+  const int pf_dist = a.prefetch;
   auto prefetch_batch = [&](long long bb) {
     if (bb >= nbatch) return;
     const long long e0 = bb * EB;
     const long long ne = (a.nelem - e0 < EB) ? (a.nelem - e0) : EB;
     const uint32_t bytes = static_cast<uint32_t>(ne * P * sizeof(T)) & ~15u;
-    if (!a.prefetch || bytes == 0) return;
+    if (!pf_dist || bytes == 0) return;
 #pragma unroll
     for (int q = 0; q < kNumPointArrays; ++q) l2_prefetch_bulk(a.m[q] + e0 * P, bytes);
     if (ASM)
@@ -100,10 +103,11 @@ __global__ void __launch_bounds__(EB * 128, MINB)
     if (tid == 0) s_ufac = sem_u_factor(a.u_norm2);
     __syncthreads();
   }
-  if (tid == 0) prefetch_batch(blockIdx.x);
+  if (tid == 0)
+    for (int d = 0; d < pf_dist; ++d) prefetch_batch(blockIdx.x + d * G);
 
   for (long long b = blockIdx.x; b < nbatch; b += G) {
-    if (tid == 0) prefetch_batch(b + G);
+    if (tid == 0) prefetch_batch(b + pf_dist * G);
     const long long e = b * EB + le;
     const bool valid = e < a.nelem;
     const long long base = e * P + col;  // point (k=0, j, i): + k*NN
