@@ -50,7 +50,11 @@ struct Sem3dHcLayout {
 // SCALE: u is read times 1 / sqrt(*a.u_norm2) (assembled); thread 0 computes
 // the factor once into shared memory, so the batches only add a broadcast
 // load and one multiply per gathered value.
-template <typename T, int EB, int MINB, bool ASM, bool PIPE = false, bool SCALE = false>
+// IBPIPE (assembled): the node ids of this thread's points in its NEXT batch are
+// loaded during phases C1 and C2, so phase A's u gathers issue at once instead
+// of after an ibool round trip.
+template <typename T, int EB, int MINB, bool ASM, bool PIPE = false, bool SCALE = false,
+          bool IBPIPE = false>
 __global__ void __launch_bounds__(EB * 128, MINB)
     sem3d_elastic_hc_kernel(const __grid_constant__ Sem3dArgs<T, 8> a) {
   using LY = Sem3dHcLayout<T, EB>;
@@ -105,6 +109,16 @@ __global__ void __launch_bounds__(EB * 128, MINB)
   }
   if (tid == 0)
     for (int d = 0; d < pf_dist; ++d) prefetch_batch(blockIdx.x + d * G);
+  int node_n[IBPIPE ? H : 1];
+  auto load_nodes = [&](long long bb) {
+    if constexpr (IBPIPE) {
+      const long long en = bb * EB + le;
+      const bool vn = bb < nbatch && en < a.nelem;
+#pragma unroll
+      for (int kk = 0; kk < H; ++kk) node_n[kk] = vn ? __ldg(a.ibool + en * P + col + (k0 + kk) * NN) : 0;
+    }
+  };
+  load_nodes(blockIdx.x);
 
   for (long long b = blockIdx.x; b < nbatch; b += G) {
     if (tid == 0) prefetch_batch(b + pf_dist * G);
@@ -119,7 +133,9 @@ __global__ void __launch_bounds__(EB * 128, MINB)
 #pragma unroll
       for (int kk = 0; kk < H; ++kk) {
         const long long pidx = base + (k0 + kk) * NN;
-        if constexpr (ASM) {
+        if constexpr (ASM && IBPIPE) {
+          node[kk] = node_n[kk];
+        } else if constexpr (ASM) {
           node[kk] = valid ? __ldg(a.ibool + pidx) : 0;
         } else {
           node[kk] = 0;
@@ -241,6 +257,7 @@ __global__ void __launch_bounds__(EB * 128, MINB)
       }
     }
     __syncthreads();
+    load_nodes(b + G);  // in flight during C1 and C2
 
     // ---- C1: the line's divergences (in place); the half-column's gamma-divergences from G ----
     if (h == 0) {
