@@ -272,7 +272,8 @@ int launch_lo(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t
 }
 
 // The half-column line-owner kernel (NGLL 8): two owners per column.
-template <typename T, int EB, int MINB, bool ASM, bool PIPE = false, bool IBPIPE = false>
+template <typename T, int EB, int MINB, bool ASM, bool PIPE = false, bool IBPIPE = false,
+          bool UPIPE = false>
 int launch_hc(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t stream,
               int dev, int sms) {
   constexpr int NT = EB * 128;
@@ -299,8 +300,8 @@ int launch_hc(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t
   };
   static KernelSlot slot, slot_scaled;
   if (ASM && a.u_norm2)
-    return go(sem3d_elastic_hc_kernel<T, EB, MINB, ASM, PIPE, true, IBPIPE>, slot_scaled);
-  return go(sem3d_elastic_hc_kernel<T, EB, MINB, ASM, PIPE, false, IBPIPE>, slot);
+    return go(sem3d_elastic_hc_kernel<T, EB, MINB, ASM, PIPE, true, IBPIPE, UPIPE>, slot_scaled);
+  return go(sem3d_elastic_hc_kernel<T, EB, MINB, ASM, PIPE, false, IBPIPE, UPIPE>, slot);
 }
 
 // Kernel variant for f32 NGLL 5 (TO_SEM3D_VARIANT; default 5):
@@ -372,10 +373,14 @@ int launch_sem3d(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStrea
     const int v = sem3d_f32_variant();
     if (v == 14)
       return launch_hc<T, 2, sizeof(T) == 8 ? 2 : 3, ASM, false>(plan, fl, stream, dev, sms);
-    // fp64 assembled: the next batch's node ids loaded during C1 / C2 (47.3 vs
-    // 49.3 ms per 128^3 power step; TO_SEM3D_VARIANT 13 loads them in phase A)
-    if (ASM && sizeof(T) == 8 && v != 2 && v != 10 && v != 12 && v != 13 && v != 14)
+    // fp64 assembled: the next batch's node ids loaded during C1 and its u
+    // gathered during C2, so phase A waits on no global load (per 128^3 power
+    // step: 49.3 ms with both in phase A -- TO_SEM3D_VARIANT 13 --, 47.3-47.9 ms
+    // with the node ids ahead -- 17 --, 46.0-46.1 ms with both)
+    if (ASM && sizeof(T) == 8 && v == 17)
       return launch_hc<T, 2, 2, ASM, true, true>(plan, fl, stream, dev, sms);
+    if (ASM && sizeof(T) == 8 && v != 2 && v != 10 && v != 12 && v != 13 && v != 14)
+      return launch_hc<T, 2, 2, ASM, true, true, true>(plan, fl, stream, dev, sms);
     if (v == 10 || v == 13 || (sizeof(T) == 8 && v != 2 && v != 12))
       return launch_hc<T, 2, sizeof(T) == 8 ? 2 : 3, ASM, true>(plan, fl, stream, dev, sms);
     if (v != 2)

@@ -54,7 +54,7 @@ struct Sem3dHcLayout {
 // loaded during phases C1 and C2, so phase A's u gathers issue at once instead
 // of after an ibool round trip.
 template <typename T, int EB, int MINB, bool ASM, bool PIPE = false, bool SCALE = false,
-          bool IBPIPE = false>
+          bool IBPIPE = false, bool UPIPE = false>
 __global__ void __launch_bounds__(EB * 128, MINB)
     sem3d_elastic_hc_kernel(const __grid_constant__ Sem3dArgs<T, 8> a) {
   using LY = Sem3dHcLayout<T, EB>;
@@ -119,6 +119,21 @@ __global__ void __launch_bounds__(EB * 128, MINB)
     }
   };
   load_nodes(blockIdx.x);
+  // UPIPE (with IBPIPE): the next batch's u values gathered at the start of C2
+  T uc_n[UPIPE ? 3 : 1][UPIPE ? H : 1];
+  auto gather_u = [&](long long bb) {
+    if constexpr (UPIPE) {
+      const long long en = bb * EB + le;
+      const bool vn = bb < nbatch && en < a.nelem;
+#pragma unroll
+      for (int kk = 0; kk < H; ++kk)
+#pragma unroll
+        for (int c = 0; c < 3; ++c)
+          uc_n[c][kk] = vn ? sem_u_scaled(__ldg(a.u[c] + node_n[kk]), SCALE ? s_ufac : 1.0, SCALE)
+                           : T(0);
+    }
+  };
+  gather_u(blockIdx.x);
 
   for (long long b = blockIdx.x; b < nbatch; b += G) {
     if (tid == 0) prefetch_batch(b + pf_dist * G);
@@ -145,7 +160,9 @@ __global__ void __launch_bounds__(EB * 128, MINB)
       for (int kk = 0; kk < H; ++kk)
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
-          if constexpr (ASM)
+          if constexpr (ASM && UPIPE)
+            uc[c][kk] = uc_n[c][kk];
+          else if constexpr (ASM)
             uc[c][kk] = valid ? sem_u_scaled(__ldg(a.u[c] + node[kk]), SCALE ? s_ufac : 1.0, SCALE)
                               : T(0);
           else
@@ -304,6 +321,7 @@ __global__ void __launch_bounds__(EB * 128, MINB)
       }
     }
     __syncthreads();
+    gather_u(b + G);  // in flight during C2
 
     // ---- C2: WeightedSum at the half-column's points -> scatter-add / store ----
 #pragma unroll
