@@ -273,7 +273,7 @@ int launch_lo(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t
 
 // The half-column line-owner kernel (NGLL 8): two owners per column.
 template <typename T, int EB, int MINB, bool ASM, bool PIPE = false, bool IBPIPE = false,
-          bool UPIPE = false>
+          bool UPIPE = false, bool GEARLY = false>
 int launch_hc(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t stream,
               int dev, int sms) {
   constexpr int NT = EB * 128;
@@ -300,8 +300,9 @@ int launch_hc(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStream_t
   };
   static KernelSlot slot, slot_scaled;
   if (ASM && a.u_norm2)
-    return go(sem3d_elastic_hc_kernel<T, EB, MINB, ASM, PIPE, true, IBPIPE, UPIPE>, slot_scaled);
-  return go(sem3d_elastic_hc_kernel<T, EB, MINB, ASM, PIPE, false, IBPIPE, UPIPE>, slot);
+    return go(sem3d_elastic_hc_kernel<T, EB, MINB, ASM, PIPE, true, IBPIPE, UPIPE, GEARLY>,
+              slot_scaled);
+  return go(sem3d_elastic_hc_kernel<T, EB, MINB, ASM, PIPE, false, IBPIPE, UPIPE, GEARLY>, slot);
 }
 
 // Kernel variant for f32 NGLL 5 (TO_SEM3D_VARIANT; default 5):
@@ -379,8 +380,12 @@ int launch_sem3d(const to_sem3d_plan* plan, const to_sem3d_fields* fl, cudaStrea
     // with the node ids ahead -- 17 --, 46.0-46.1 ms with both)
     if (ASM && sizeof(T) == 8 && v == 17)
       return launch_hc<T, 2, 2, ASM, true, true>(plan, fl, stream, dev, sms);
-    if (ASM && sizeof(T) == 8 && v != 2 && v != 10 && v != 12 && v != 13 && v != 14)
+    // ... and the first point's geometry requested before B1 (43.5-43.6 vs
+    // 43.9-44.0 ms on one box; TO_SEM3D_VARIANT 18 requests it at B2)
+    if (ASM && sizeof(T) == 8 && v == 18)
       return launch_hc<T, 2, 2, ASM, true, true, true>(plan, fl, stream, dev, sms);
+    if (ASM && sizeof(T) == 8 && v != 2 && v != 10 && v != 12 && v != 13 && v != 14)
+      return launch_hc<T, 2, 2, ASM, true, true, true, true>(plan, fl, stream, dev, sms);
     if (v == 10 || v == 13 || (sizeof(T) == 8 && v != 2 && v != 12))
       return launch_hc<T, 2, sizeof(T) == 8 ? 2 : 3, ASM, true>(plan, fl, stream, dev, sms);
     if (v != 2)

@@ -54,7 +54,7 @@ struct Sem3dHcLayout {
 // loaded during phases C1 and C2, so phase A's u gathers issue at once instead
 // of after an ibool round trip.
 template <typename T, int EB, int MINB, bool ASM, bool PIPE = false, bool SCALE = false,
-          bool IBPIPE = false, bool UPIPE = false>
+          bool IBPIPE = false, bool UPIPE = false, bool GEARLY = false>
 __global__ void __launch_bounds__(EB * 128, MINB)
     sem3d_elastic_hc_kernel(const __grid_constant__ Sem3dArgs<T, 8> a) {
   using LY = Sem3dHcLayout<T, EB>;
@@ -180,6 +180,22 @@ __global__ void __launch_bounds__(EB * 128, MINB)
     }
     __syncthreads();
 
+    T Jn[3][3], jacn = T(0), l2mn = T(0), mun = T(0);  // the next point's (PIPE)
+    auto load_geom = [&](int kk, T (&Jd)[3][3], T& jd, T& ld, T& md) {
+      const long long pidx = base + (k0 + kk) * NN;
+#pragma unroll
+      for (int rr = 0; rr < 3; ++rr)
+#pragma unroll
+        for (int d = 0; d < 3; ++d) Jd[rr][d] = valid ? __ldcs(a.m[kXIX + 3 * rr + d] + pidx) : T(0);
+      if (valid) {
+        jd = __ldcs(a.m[kJAC] + pidx);
+        ld = __ldcs(a.m[kL2M] + pidx);
+        md = __ldcs(a.m[kMU] + pidx);
+      }
+    };
+    // GEARLY: the first point's geometry requested now, in flight during B1
+    if constexpr (PIPE && GEARLY) load_geom(0, Jn, jacn, l2mn, mun);
+
     // ---- B1: the line's gradients (in place); the half-column's gamma-gradients from G ----
     T dgm[3][H];
     if (h == 0) {
@@ -227,20 +243,7 @@ __global__ void __launch_bounds__(EB * 128, MINB)
     __syncthreads();
 
     // ---- B2: Integrand9 at the half-column's points; geometry from global ----
-    T Jn[3][3], jacn = T(0), l2mn = T(0), mun = T(0);  // the next point's (PIPE)
-    auto load_geom = [&](int kk, T (&Jd)[3][3], T& jd, T& ld, T& md) {
-      const long long pidx = base + (k0 + kk) * NN;
-#pragma unroll
-      for (int rr = 0; rr < 3; ++rr)
-#pragma unroll
-        for (int d = 0; d < 3; ++d) Jd[rr][d] = valid ? __ldcs(a.m[kXIX + 3 * rr + d] + pidx) : T(0);
-      if (valid) {
-        jd = __ldcs(a.m[kJAC] + pidx);
-        ld = __ldcs(a.m[kL2M] + pidx);
-        md = __ldcs(a.m[kMU] + pidx);
-      }
-    };
-    if constexpr (PIPE) load_geom(0, Jn, jacn, l2mn, mun);
+    if constexpr (PIPE && !GEARLY) load_geom(0, Jn, jacn, l2mn, mun);
 #pragma unroll
     for (int kk = 0; kk < H; ++kk) {
       const int k = k0 + kk;
