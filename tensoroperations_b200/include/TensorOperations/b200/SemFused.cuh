@@ -440,6 +440,21 @@ constexpr int sem_fused_min_blocks() {
   return Pat::tables.nint == 1 ? 5 : 2;
 }
 #endif
+// Whether the kernel reads the next batch's fields ahead: on for several
+// integrands (128 registers, no spills; the reference's DagGraph program 3.08 vs
+// 3.11 ms), off for one (at its 56-register budget it would spill 40 bytes).
+// TO_SEM_FUSED_U_PIPE = 0 / 1 forces it off / on for every spelling.
+#ifdef TO_SEM_FUSED_U_PIPE
+template <class Pat>
+constexpr bool sem_fused_u_pipe() {
+  return TO_SEM_FUSED_U_PIPE != 0;
+}
+#else
+template <class Pat>
+constexpr bool sem_fused_u_pipe() {
+  return Pat::tables.nint > 1;
+}
+#endif
 // Points per group of functor calls in phase B2.
 #ifndef TO_SEM_FUSED_B2_GROUP
 #define TO_SEM_FUSED_B2_GROUP 1
@@ -474,6 +489,24 @@ __global__ void __launch_bounds__(SemFusedLayout::NT, sem_fused_min_blocks<Pat>(
   const int lx = rb * SKX + le * NN + ra * N;  // x3-line (k = rb, j = ra): + i
   const int ly = ra * SKE + le * NN + rb;      // x2-line (k = ra, i = rb): + N j
 
+  // kUPipe: the next batch's column of the three fields is read during C1 and
+  // C2 of this one, so phase A waits on no global load
+  constexpr bool kUPipe = sem_fused_u_pipe<Pat>();
+  V un[kUPipe ? 3 : 1][kUPipe ? N : 1];
+  auto load_u = [&](long long bb) {
+    if constexpr (kUPipe) {
+      const long long en = bb * EB + le;
+      const bool vn = en < nelem;
+      const int eni = vn ? static_cast<int>(en) : 0;
+      static_for<3>([&](auto cc) {
+        constexpr int c = decltype(cc)::value;
+        const auto& u = src.fields.template get<c>();
+#pragma unroll
+        for (int k = 0; k < N; ++k) un[c][k] = vn ? static_cast<V>(u(eni, k, ra, rb)) : V(0);
+      });
+    }
+  };
+  load_u(blockIdx.x);
   for (long long b = blockIdx.x; b * EB < nelem; b += gridDim.x) {
     const long long e = b * EB + le;
     const bool valid = e < nelem;
@@ -486,7 +519,12 @@ __global__ void __launch_bounds__(SemFusedLayout::NT, sem_fused_min_blocks<Pat>(
       const auto& u = src.fields.template get<c>();
       V uc[N];
 #pragma unroll
-      for (int k = 0; k < N; ++k) uc[k] = valid ? static_cast<V>(u(ei, k, ra, rb)) : V(0);
+      for (int k = 0; k < N; ++k) {
+        if constexpr (kUPipe)
+          uc[k] = un[c][k];
+        else
+          uc[k] = valid ? static_cast<V>(u(ei, k, ra, rb)) : V(0);
+      }
 #pragma unroll
       for (int k = 0; k < N; ++k) {
         X[c * CX + k * SKX + tid] = uc[k];
@@ -583,6 +621,8 @@ __global__ void __launch_bounds__(SemFusedLayout::NT, sem_fused_min_blocks<Pat>(
       });
     });
     __syncthreads();
+
+    load_u(b + gridDim.x);  // in flight during C1 and C2
 
     // ---- C1: divergences along x3 and x2, in place ----
     static_for<3>([&](auto ss) {
