@@ -738,10 +738,14 @@ inline bool sem_fused_enabled() {
   return enabled;
 }
 
-// A dense row-major 5 x 5 view.
-template <class H>
+// A dense row-major 5 x 5 view of V (its data is copied into the constant bank
+// as V, so another element type keeps the generic evaluator, which converts).
+template <class V, class H>
 bool sem_dense_operator(const H& h) {
-  return h.extent(0) == 5 && h.extent(1) == 5 && h.stride(0) == 5 && h.stride(1) == 1;
+  if constexpr (!std::is_same_v<typename value_of<H>::type, V>)
+    return false;
+  else
+    return h.extent(0) == 5 && h.extent(1) == 5 && h.stride(0) == 5 && h.stride(1) == 1;
 }
 
 // Root view R of extents (nelem, 5, 5, 5) in physical order, permuted by the
@@ -794,7 +798,7 @@ bool sem_fused_launch(const Levels& levels, const Views& views, long long nelem,
       (
           [&] {
             const auto& h = levels.template get<0>().template get<S>().operand_.handle.tensor;
-            shapes = shapes && sem_dense_operator(h);
+            shapes = shapes && sem_dense_operator<V>(h);
             ops.p[S] = reinterpret_cast<const V*>(h.data());
           }(),
           ...);

@@ -348,7 +348,7 @@ int sem_fused_dag_launch(const NodesT& nodes, cudaError_t* err, const ViewTs&...
           [&] {
             const auto& g = nodes.template get<T.g_node[M]>().node_a.handle.tensor;
             const auto& d = nodes.template get<T.d_node[M]>().node_a.handle.tensor;
-            ok = ok && sem_dense_operator(g) && sem_dense_operator(d);
+            ok = ok && sem_dense_operator<V>(g) && sem_dense_operator<V>(d);
             ops.p[M] = reinterpret_cast<const V*>(g.data());
             ops.p[9 + M] = reinterpret_cast<const V*>(d.data());
           }(),
