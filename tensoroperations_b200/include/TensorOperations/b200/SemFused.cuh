@@ -424,6 +424,9 @@ __device__ __forceinline__ void sem_line(const V* in, V* out) {
 // Every table lookup below happens at compile time (static_for indices and
 // constexpr locals); a run-time index into the tables would put them in local
 // memory.
+#ifndef TO_SEM_FUSED_ZBUF
+#define TO_SEM_FUSED_ZBUF 1
+#endif
 // Resident CTAs per SM the kernel is compiled for (its register budget): one
 // integrand (56 registers, a few bytes of spills) 5 -- 1.788 vs 1.816 ms for the
 // reference's LevelGraph program at E=786,432 --, three integrands (113
@@ -437,12 +440,23 @@ constexpr int sem_fused_min_blocks() {
 #else
 template <class Pat>
 constexpr int sem_fused_min_blocks() {
-  return Pat::tables.nint == 1 ? 5 : 2;
+  return Pat::tables.nint == 1 ? 5 : (TO_SEM_FUSED_ZBUF ? 3 : 2);
 }
 #endif
+// Several integrands: the column's x1 gradients and fluxes live in a third
+// shared buffer Z ([3][N][NT], the column owner's own words) instead of 30
+// registers, so the kernel fits 3 CTAs per SM at 80 registers without spills
+// (the reference's DagGraph program 2.979 vs 3.079 ms with them in registers
+// and the fields read ahead).  TO_SEM_FUSED_ZBUF=0 keeps them in registers.
+template <class Pat>
+constexpr bool sem_fused_zbuf() {
+  return TO_SEM_FUSED_ZBUF != 0 && Pat::tables.nint > 1;
+}
 // Whether the kernel reads the next batch's fields ahead: on for several
-// integrands (128 registers, no spills; the reference's DagGraph program 3.08 vs
-// 3.11 ms), off for one (at its 56-register budget it would spill 40 bytes).
+// integrands with x1 data in registers (128 registers, no spills; the
+// reference's DagGraph program 3.08 vs 3.11 ms), off with the Z buffer (it
+// would spill at 80 registers) and for one integrand (it would spill 40 bytes
+// at 56).
 // TO_SEM_FUSED_U_PIPE = 0 / 1 forces it off / on for every spelling.
 #ifdef TO_SEM_FUSED_U_PIPE
 template <class Pat>
@@ -452,7 +466,7 @@ constexpr bool sem_fused_u_pipe() {
 #else
 template <class Pat>
 constexpr bool sem_fused_u_pipe() {
-  return Pat::tables.nint > 1;
+  return Pat::tables.nint > 1 && !sem_fused_zbuf<Pat>();
 }
 #endif
 // Points per group of functor calls in phase B2.
@@ -475,11 +489,13 @@ template <class V, class Pat, class Src, class Views>
 __global__ void __launch_bounds__(SemFusedLayout::NT, sem_fused_min_blocks<Pat>())
     sem_fused_kernel(const Src src, const Views views, long long nelem) {
   using LY = SemFusedLayout;
-  constexpr int N = LY::N, NN = LY::NN, EB = LY::EB;
+  constexpr int N = LY::N, NN = LY::NN, EB = LY::EB, NT = LY::NT;
   constexpr int SKX = LY::SKX, SKE = LY::SKE, CX = LY::CX, CE = LY::CE;
   extern __shared__ __align__(16) unsigned char sem_smem[];
   V* X = reinterpret_cast<V*>(sem_smem);  // [3][N][SKX]: rows along x3 (i)
   V* E = X + 3 * CX;                      // [3][N][SKE]: rows along x2 (j)
+  constexpr bool kZ = sem_fused_zbuf<Pat>();
+  V* Z = E + 3 * CE;                      // kZ: [3][N][NT], x1 data of the columns
 
   const int tid = threadIdx.x;
   const int le = tid / NN;
@@ -513,7 +529,7 @@ __global__ void __launch_bounds__(SemFusedLayout::NT, sem_fused_min_blocks<Pat>(
     const int ei = valid ? static_cast<int>(e) : 0;
 
     // ---- A: the column's fields -> X, E; gradients along x1 in registers ----
-    V dg[3][N];
+    V dg[kZ ? 1 : 3][kZ ? 1 : N];
     static_for<3>([&](auto cc) {
       constexpr int c = decltype(cc)::value;
       const auto& u = src.fields.template get<c>();
@@ -531,7 +547,14 @@ __global__ void __launch_bounds__(SemFusedLayout::NT, sem_fused_min_blocks<Pat>(
         E[c * CE + k * SKE + tid] = uc[k];
       }
       constexpr int m = Pat::tables.g_of[c][1];
-      sem_line<V, Pat::tables.g_op[m], Pat::tables.g_tr[m]>(uc, dg[c]);
+      if constexpr (kZ) {
+        V gl[N];
+        sem_line<V, Pat::tables.g_op[m], Pat::tables.g_tr[m]>(uc, gl);
+#pragma unroll
+        for (int k = 0; k < N; ++k) Z[(c * N + k) * NT + tid] = gl[k];
+      } else {
+        sem_line<V, Pat::tables.g_op[m], Pat::tables.g_tr[m]>(uc, dg[c]);
+      }
     });
     __syncthreads();
 
@@ -562,7 +585,7 @@ __global__ void __launch_bounds__(SemFusedLayout::NT, sem_fused_min_blocks<Pat>(
     // group is made before any flux is stored, so the functors' own global
     // loads (through generic pointers, which the compiler may not move across
     // a shared-memory store) of the whole group are in flight together.
-    V Fg[3][N];
+    V Fg[kZ ? 1 : 3][kZ ? 1 : N];
     constexpr int KG = TO_SEM_FUSED_B2_GROUP;
     static_for<(N + KG - 1) / KG>([&](auto gg) {
       constexpr int k0 = decltype(gg)::value * KG;
@@ -576,6 +599,8 @@ __global__ void __launch_bounds__(SemFusedLayout::NT, sem_fused_min_blocks<Pat>(
           X[sl * CX + k * SKX + tid] = value;
         else if constexpr (ax == 2)
           E[sl * CE + k * SKE + tid] = value;
+        else if constexpr (kZ)
+          Z[(sl * N + k) * NT + tid] = value;
         else
           Fg[sl][k] = value;
       };
@@ -590,7 +615,7 @@ __global__ void __launch_bounds__(SemFusedLayout::NT, sem_fused_min_blocks<Pat>(
           else if constexpr (ax == 2)
             g[m] = E[comp * CE + k * SKE + tid];
           else
-            g[m] = dg[comp][k];
+            g[m] = kZ ? Z[(comp * N + k) * NT + tid] : dg[kZ ? 0 : comp][kZ ? 0 : k];
         });
         const int P[4] = {ei, k, ra, rb};
         static_for<Pat::tables.nint>([&](auto ci) {
@@ -649,7 +674,14 @@ __global__ void __launch_bounds__(SemFusedLayout::NT, sem_fused_min_blocks<Pat>(
     static_for<3>([&](auto ss) {
       constexpr int sl = decltype(ss)::value;
       constexpr int m = Pat::tables.d_at[1][sl];
-      sem_line<V, Pat::tables.d_op[m], Pat::tables.d_tr[m]>(Fg[sl], tgc[sl]);
+      if constexpr (kZ) {
+        V fz[N];
+#pragma unroll
+        for (int q = 0; q < N; ++q) fz[q] = Z[(sl * N + q) * NT + tid];
+        sem_line<V, Pat::tables.d_op[m], Pat::tables.d_tr[m]>(fz, tgc[sl]);
+      } else {
+        sem_line<V, Pat::tables.d_op[m], Pat::tables.d_tr[m]>(Fg[sl], tgc[sl]);
+      }
     });
 #pragma unroll
     for (int k = 0; k < N; ++k) {
@@ -695,7 +727,8 @@ template <class V, class Pat, class Src, class Views>
 cudaError_t sem_fused_run(const Src& src, const Views& views, long long nelem,
                           const SemOpPtrs<V>& ops, int nops) {
   using LY = SemFusedLayout;
-  constexpr std::size_t smem = LY::bytes<V>();
+  constexpr std::size_t smem =
+      LY::bytes<V>() + (sem_fused_zbuf<Pat>() ? sizeof(V) * 3 * LY::N * LY::NT : 0);
   auto kernel = sem_fused_kernel<V, Pat, Src, Views>;
   int dev = 0, sms = 0, nb = 0;
   cudaError_t err = cudaGetDevice(&dev);
